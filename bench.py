@@ -1,0 +1,476 @@
+"""Benchmark: SpMM effective GFLOP/s (2*nnz*K/t) and % of the HBM roofline.
+
+Default workload (N=1 line): BASELINE config 2 -- 3-D FEM hex mesh, 64^3 nodes x
+3 DOF (786,432 rows, 61,731,000 nonzeros), BOO with identity grouping at
+target 32x32, X [786432, 128] fp32 ~ N(0,1); synthetic, seeded.  One step = one
+Y = A*X over the whole matrix with A, X and Y resident in HBM (1.18 GB, far
+larger than the 126 MB L2, so no flush is needed between steps).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
+                  [--config c2_fem3d] [--format boo|pbr]
+
+Multi-GPU (torchrun, one process per GPU): the feature columns are split --
+every rank holds the replicated A and its own 128-column slab of X / Y, so the
+timed region has no collective (weak scaling: total K = N * 128).  The time is
+the max over ranks of the device-measured duration.
+
+``--impl reference`` times the reference's own CPU implementation
+(boo_batched_matmul_cpu of the reference core built into oracle/_ref, else the
+C restatement in oracle/) on this host's cores, rows split across worker
+processes, on the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = 'SpMM effective GFLOP/s (2*nnz*K/t)'
+PROFILES = os.path.join(ROOT, 'profiles')
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=200)
+    ap.add_argument('--warmup', type=int, default=5)
+    ap.add_argument('--impl', choices=('native', 'reference'), default='native')
+    ap.add_argument('--config', default='c2_fem3d')
+    ap.add_argument('--format', choices=('boo', 'pbr'), default=None)
+    ap.add_argument('--e2e-steps', type=int, default=5)
+    ap.add_argument('--no-cpu-baseline', action='store_true')
+    return ap.parse_args()
+
+
+def make_matrix(cfg_name):
+    from spmm_b200 import workloads as W
+    cfg = W.CONFIGS[cfg_name]
+    return cfg['gen'](**cfg['kw']), cfg
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+              'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+              'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, gpu_id: str):
+        self.proc = None
+        self.gpu_id = gpu_id
+        self.path = os.path.join(ROOT, 'gpurun_out', f'clocks_{os.getpid()}.csv')
+
+    def start(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.out = open(self.path, 'w')
+            self.proc = subprocess.Popen(
+                ['nvidia-smi', f'--query-gpu={self.FIELDS}', '--format=csv,noheader,nounits',
+                 '-lms', '100', '-i', self.gpu_id], stdout=self.out, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except (OSError, ValueError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.out.close()
+        sm, smax, reasons = [], [], set()
+        names = ('hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap')
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(',')]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith('active'):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {'sm_mhz': statistics.median(sm), 'sm_max_mhz': max(smax),
+                'reasons': sorted(reasons), 'samples': len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's CPU SpMM on a bounded row sample
+# ---------------------------------------------------------------------------
+
+def _reference_core():
+    try:
+        from oracle.build_ref import load_reference
+        return load_reference()
+    except Exception:
+        return None
+
+
+def _sample(mat, rows):
+    sub = mat[:rows]
+    return sub
+
+
+def _build_ref_boo(core, sub, cols, target):
+    rl = (np.arange(sub.shape[0], dtype=np.int32) // target).astype(np.int32)
+    cl = (np.arange(cols, dtype=np.int32) // target).astype(np.int32)
+    if core is not None:
+        return core.csr_to_boo(sub.indptr, sub.indices, sub.data, sub.shape[0], cols, rl, cl, 2, 4, 0), 'reference'
+    from oracle import oracle as O
+    return O.boo_build(sub.indptr, sub.indices, sub.data, sub.shape[0], cols, rl, cl, 2, 4, 0), 'port'
+
+
+def _ref_matmul(obj, kind, x_np, fmt='boo'):
+    if kind == 'reference':
+        import torch
+        core = _reference_core()
+        f = core.boo_batched_matmul_cpu if fmt == 'boo' else core.pbr_batched_matmul_cpu
+        return f(obj, torch.from_numpy(x_np))
+    from oracle import oracle as O
+    return (O.boo_matmul if fmt == 'boo' else O.pbr_matmul)(obj, x_np)
+
+
+def _build_ref_pbr(core, sub, cols):
+    if core is not None:
+        return core.csr_to_pbr(sub.indptr, sub.indices, sub.data, sub.shape[0], cols, 8, 8, 4), 'reference'
+    from oracle import oracle as O
+    return O.pbr_build(sub.indptr, sub.indices, sub.data, sub.shape[0], cols, 8, 8, 4), 'port'
+
+
+def cpu_baseline(mat, cfg, x_np, fmt='boo', budget_s=12.0):
+    """Single-threaded reference CPU SpMM on the first rows of the matrix."""
+    core = _reference_core()
+    K = x_np.shape[1]
+    frac = 16
+    rows = max(1, mat.shape[0] // frac)
+    sub = _sample(mat, rows)
+    if fmt == 'boo':
+        obj, kind = _build_ref_boo(core, sub, mat.shape[1], cfg['target'])
+    else:
+        obj, kind = _build_ref_pbr(core, sub, mat.shape[1])
+    times = []
+    t_end = time.perf_counter() + budget_s
+    _ref_matmul(obj, kind, x_np, fmt)           # warm-up
+    while len(times) < 3 or (time.perf_counter() < t_end and len(times) < 10):
+        t0 = time.perf_counter()
+        _ref_matmul(obj, kind, x_np, fmt)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {'value': round(2.0 * sub.nnz * K / t / 1e9, 4), 'unit': 'GFLOP/s', 'cores': 1,
+            'kind': kind,
+            'sample': f'rows [0, {rows}) of the workload ({sub.nnz} nnz), K={K}, '
+                      f'median of {len(times)} calls, 1 thread'}
+
+
+# ---------------------------------------------------------------------------
+# reference arm: the reference's CPU SpMM on all host cores
+# ---------------------------------------------------------------------------
+
+_W = {}
+
+
+def _worker_init(shm_name, shape, dtype, indptr, indices, data, cols, target):
+    from multiprocessing import shared_memory
+    shm = shared_memory.SharedMemory(name=shm_name)
+    _W['shm'] = shm
+    _W['x'] = np.ndarray(shape, dtype=dtype, buffer=shm.buf)
+    import scipy.sparse as sp
+    sub = sp.csr_matrix((data, indices, indptr), shape=(len(indptr) - 1, cols))
+    core = _reference_core()
+    _W['obj'], _W['kind'] = _build_ref_boo(core, sub, cols, target)
+    if _W['kind'] == 'reference':
+        import torch
+        torch.set_num_threads(1)
+        _W['xt'] = torch.from_numpy(_W['x'])
+
+
+def _worker_step(_):
+    t0 = time.perf_counter()
+    if _W['kind'] == 'reference':
+        _reference_core().boo_batched_matmul_cpu(_W['obj'], _W['xt'])
+    else:
+        from oracle import oracle as O
+        O.boo_matmul(_W['obj'], _W['x'])
+    return time.perf_counter() - t0
+
+
+def reference_arm(args):
+    import multiprocessing as mp
+    from multiprocessing import shared_memory
+    rank = int(os.environ.get('RANK', '0'))
+    if rank != 0:
+        return 0
+    mat, cfg = make_matrix(args.config)
+    K = cfg['K']
+    from spmm_b200 import workloads as W
+    x = W.dense_x(mat.shape[1], K, seed=0).numpy()
+    try:
+        cores = len(os.sched_getaffinity(0))
+    except AttributeError:
+        cores = os.cpu_count() or 1
+    P = max(1, min(cores, 64))
+    # bounded sample: enough rows that one step is ~0.5 s of work on P cores
+    est_rate = 2.0e9                    # flop/s per core of the serial reference loop
+    rows = min(mat.shape[0], int(mat.shape[0] * min(1.0, 0.5 * P * est_rate /
+                                                    (2.0 * mat.nnz * K))))
+    rows = max(rows - rows % cfg['target'], cfg['target'])
+    sub = mat[:rows]
+    shm = shared_memory.SharedMemory(create=True, size=x.nbytes)
+    try:
+        xs = np.ndarray(x.shape, dtype=x.dtype, buffer=shm.buf)
+        xs[:] = x
+        bounds = np.linspace(0, rows // cfg['target'], P + 1).astype(int) * cfg['target']
+        ctx = mp.get_context('spawn')
+        pools = []
+        for i in range(P):
+            part = sub[bounds[i]:bounds[i + 1]]
+            if part.shape[0] == 0:
+                continue
+            pools.append(ctx.Pool(1, initializer=_worker_init,
+                                  initargs=(shm.name, x.shape, x.dtype, part.indptr, part.indices,
+                                            part.data, mat.shape[1], cfg['target'])))
+        kind = 'reference' if _reference_core() is not None else 'port'
+
+        def step():
+            t0 = time.perf_counter()
+            rs = [p.apply_async(_worker_step, (0,)) for p in pools]
+            [r.get() for r in rs]
+            return time.perf_counter() - t0
+
+        for _ in range(args.warmup):
+            step()
+        ts = [step() for _ in range(args.steps)]
+        for p in pools:
+            p.close()
+            p.join()
+    finally:
+        shm.close()
+        shm.unlink()
+    t = sum(ts) / len(ts)
+    value = 2.0 * sub.nnz * K / t / 1e9
+    sample = (f'rows [0, {rows}) of {args.config} ({sub.nnz} nnz), K={K}, rows split over '
+              f'{len(pools)} single-threaded processes')
+    line = {'impl': 'reference', 'metric': METRIC, 'value': round(value, 4), 'unit': 'GFLOP/s',
+            'n_gpus': args.gpus, 'steps': args.steps, 'warmup': args.warmup,
+            'ms_per_step': round(1e3 * t, 3), 'higher_is_better': True, 'scaling': 'weak',
+            'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic (seeded generator)',
+            'config': {'workload': args.config, 'format': 'boo', 'rows': int(mat.shape[0]),
+                       'nnz': int(mat.nnz), 'K': K},
+            'cpu_baseline': {'value': round(value, 4), 'unit': 'GFLOP/s', 'cores': len(pools),
+                             'kind': kind, 'sample': sample},
+            'e2e': {'value': round(value, 4), 'unit': 'GFLOP/s', 'h2d_bytes_per_step': 0,
+                    'd2h_bytes_per_step': 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# native arm
+# ---------------------------------------------------------------------------
+
+def format_bytes_boo(boo, K, batch=1):
+    """Compulsory bytes of one BOO product: every staged array the kernel
+    reads once, X once, Y once."""
+    s = boo._sizes
+    sb = 4 if boo._scalar_dtype == np.float32 else 8
+    a = (4 * (s['n_rg'] + 1) + 4 * s['rows']            # row groups
+         + 4 * (s['n_cg'] + 1) + 4 * s['cols']          # col groups
+         + s['nb'] * (4 + 4 + 4 + 1) + 4                # block arrays
+         + s['nnz_c'] * (2 + sb)                        # nz_idx + nz_val
+         + 4 * (s['rows'] + 1) + s['rem_nnz'] * (4 + sb)
+         + s['tail_nnz'] * (4 + 4 + sb))
+    return a, batch * s['cols'] * K * sb, batch * s['rows'] * K * sb
+
+
+def format_bytes_pbr(pbr, K, batch=1):
+    s = pbr._sizes
+    sb = 4 if pbr._scalar_dtype == np.float32 else 8
+    ib = 4 if pbr._index_dtype == np.int32 else 8
+    a = (s['nb'] * (8 + 2 * ib + ib) + ib + s['nnz_c'] * sb
+         + ib * (s['rows'] + 1) + s['rem_nnz'] * (ib + sb))
+    return a, batch * s['cols'] * K * sb, batch * s['rows'] * K * sb
+
+
+def load_peaks():
+    path = os.path.join(ROOT, 'MEASURED_PEAKS.json')
+    if os.path.exists(path):
+        d = json.load(open(path))
+        return float(d['hbm_gbs']), 'measured'
+    return 6650.0, 'fallback'
+
+
+def load_traffic(kernel_tag):
+    """DRAM bytes per launch from the committed ncu summary of this workload."""
+    path = os.path.join(PROFILES, 'traffic.json')
+    if not os.path.exists(path):
+        return None
+    try:
+        d = json.load(open(path))
+        return d.get(kernel_tag)
+    except (OSError, ValueError):
+        return None
+
+
+def native_arm(args):
+    import torch
+    import torch.distributed as dist
+
+    import spmm_b200 as S
+    from spmm_b200 import _lib
+    from spmm_b200 import workloads as W
+
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    torch.cuda.set_device(local)
+    dev = torch.device('cuda', local)
+    if world > 1:
+        import datetime
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    mat, cfg = make_matrix(args.config)
+    fmt = args.format or cfg['fmt']
+    K = cfg['K']
+    t0 = time.perf_counter()
+    if fmt == 'boo':
+        A = S.csr_to_boo(mat, cluster='identity', target_nr=cfg['target'], target_nc=cfg['target'])
+    else:
+        A = S.csr_to_pbr(mat, 8, 8, 4)
+    torch.cuda.synchronize(dev)
+    build_s = time.perf_counter() - t0
+    A.to(dev)
+    meta = A._gpu_meta
+    st = A._dev_struct(meta)
+    L = _lib.lib()
+    fn = L.spmm_boo_matmul if fmt == 'boo' else L.spmm_pbr_matmul
+    x = W.dense_x(mat.shape[1], K, seed=rank).to(dev)
+    y = torch.empty((mat.shape[0], K), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sh = stream.cuda_stream
+
+    def launch():
+        rc = fn(C.byref(st), x.data_ptr(), y.data_ptr(), 1, K, None, sh)
+        if rc:
+            raise _lib.SpmmError(rc, 'bench')
+
+    for _ in range(max(args.warmup, 3)):
+        launch()
+    torch.cuda.synchronize(dev)
+
+    clocks = None
+    sampler = None
+    if rank == 0:
+        try:
+            uuid = str(torch.cuda.get_device_properties(dev).uuid)
+            gid = uuid if uuid.startswith('GPU-') else f'GPU-{uuid}'
+        except Exception:
+            gid = str(local)
+        sampler = ClockSampler(gid)
+        sampler.start()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        launch()
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    if sampler is not None:
+        clocks = sampler.stop()
+
+    ms_step = ms / args.steps
+    flops_rank = 2.0 * mat.nnz * K
+    value = world * flops_rank / (ms_step * 1e-3) / 1e9
+
+    abytes, xbytes, ybytes = (format_bytes_boo if fmt == 'boo' else format_bytes_pbr)(A, K)
+    alg = abytes + xbytes + ybytes
+    peak, peak_kind = load_peaks()
+    achieved = alg / (ms_step * 1e-3) / 1e9
+    tag = f'{args.config}:{fmt}'
+    traffic = load_traffic(tag)
+
+    # e2e: the public API with host operands (pinned H2D of X, D2H of Y per step)
+    x_host = x.cpu().pin_memory()
+    for _ in range(2):
+        (S.boo_matmul if fmt == 'boo' else S.pbr_matmul)(A, x_host)
+    torch.cuda.synchronize(dev)
+    e0 = time.perf_counter()
+    for _ in range(args.e2e_steps):
+        yh = (S.boo_matmul if fmt == 'boo' else S.pbr_matmul)(A, x_host)
+    torch.cuda.synchronize(dev)
+    e_s = (time.perf_counter() - e0) / args.e2e_steps
+    if world > 1:
+        t = torch.tensor([e_s], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e_s = float(t.item())
+    e2e = {'value': round(world * flops_rank / e_s / 1e9, 3), 'unit': 'GFLOP/s',
+           'h2d_bytes_per_step': int(x_host.numel() * 4), 'd2h_bytes_per_step': int(yh.numel() * 4),
+           'ms_per_step': round(e_s * 1e3, 3)}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(mat, cfg, x.cpu().numpy(), fmt)
+
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {
+        'metric': METRIC, 'value': round(value, 3), 'unit': 'GFLOP/s', 'n_gpus': world,
+        'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(ms_step, 5),
+        'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32',
+        'data': 'synthetic (seeded generator of the config)',
+        'config': {'workload': args.config, 'format': fmt,
+                   'grouping': 'identity' if fmt == 'boo' else '8x8 bitset blocks',
+                   'target': cfg['target'] if fmt == 'boo' else None, 'rows': int(mat.shape[0]),
+                   'nnz': int(mat.nnz), 'K_per_gpu': K, 'parallelism': f'feature-split x{world}',
+                   'l2': 'inputs larger than L2 (A+X+Y = %.2f GB), no flush' % (alg / 1e9),
+                   'build_s': round(build_s, 3)},
+        'roofline': {'bound': 'hbm', 'achieved': round(achieved, 1), 'peak': peak,
+                     'unit': 'GB/s', 'frac': round(achieved / peak, 4), 'traffic': traffic,
+                     'peak_kind': peak_kind, 'alg_bytes_per_launch': int(alg),
+                     'kernel': 'boo_spmm_kernel' if fmt == 'boo' else 'pbr_spmm_kernel'},
+        'e2e': e2e, 'gpu_launches': args.steps,
+        'clocks': clocks, 'cpu_baseline': cpu,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == 'reference':
+        return reference_arm(args)
+    return native_arm(args)
+
+
+if __name__ == '__main__':
+    sys.exit(main())

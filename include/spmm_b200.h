@@ -1,0 +1,189 @@
+/*
+ * spmm_b200.h -- C ABI of the B200 (sm_100a) BOO / PBR SpMM engine.
+ *
+ * Drop-in boundary for the hot path of Dayan135/SPMM (torch_fast_spdmm):
+ * GPU format construction (csr_to_boo, csr_to_pbr) and Y = A*X with A in the
+ * BOO or PBR format.  Every entry point takes plain device pointers and sizes
+ * and a CUDA stream; no torch types cross this boundary.
+ *
+ * Conventions
+ *   - Ownership: the caller owns every buffer (inputs, outputs, workspace).
+ *     The library allocates no device memory and keeps no state between calls.
+ *   - Errors: every entry point returns an int status (SPMM_OK == 0).  No C++
+ *     exception crosses the ABI.  spmm_status_string() gives the text.
+ *   - Streams: work is enqueued on `stream` (cudaStream_t; NULL = legacy
+ *     default stream) in order with the caller's other work on that stream.
+ *     Only the *_analyze builder phases block the host (they must return sizes).
+ *   - Threading: no globals; concurrent calls on different streams with
+ *     different buffers are safe.
+ *   - Devices: work runs on the CUDA device current on the calling thread; all
+ *     pointers must belong to that device.
+ *   - Dense operands: X is [batch][cols][K] and Y is [batch][rows][K], both
+ *     C-contiguous in the format's scalar type.  Y is fully overwritten.
+ */
+#ifndef SPMM_B200_H
+#define SPMM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *spmm_stream_t; /* == cudaStream_t */
+
+enum spmm_status {
+    SPMM_OK = 0,
+    SPMM_EINVAL = 1,          /* bad argument (policy, order, sizes, null pointer) */
+    SPMM_ELABEL = 2,          /* cluster label out of range */
+    SPMM_EOVERFLOW_U16 = 3,   /* a kept BOO block's local index space exceeds uint16 */
+    SPMM_EDUPLICATE = 4,      /* PBR input has duplicate (row, col) entries */
+    SPMM_ECUDA = 5,           /* a CUDA runtime call or kernel launch failed */
+    SPMM_EWORKSPACE = 6,      /* workspace smaller than *_workspace_size() asked for */
+    SPMM_EUNSUPPORTED = 7,    /* size or type outside what this build handles */
+    SPMM_EALIGN = 8           /* a pointer lacks the alignment its dtype requires */
+};
+
+enum spmm_index_type { SPMM_INDEX_I32 = 0, SPMM_INDEX_I64 = 1 };
+enum spmm_scalar_type { SPMM_F32 = 0, SPMM_F64 = 1 };
+enum spmm_boo_policy { SPMM_BOO_KEEP = 0, SPMM_BOO_MERGE = 1, SPMM_BOO_REMAINDER = 2,
+                       SPMM_BOO_TAIL_BATCH = 3 };
+enum spmm_boo_order { SPMM_BOO_ROWMAJOR = 0, SPMM_BOO_COLMAJOR = 1 };
+
+/* A CSR matrix in device memory. */
+typedef struct {
+    int64_t rows, cols, nnz;
+    const void *indptr;   /* rows+1 entries of index_type */
+    const void *indices;  /* nnz entries of index_type */
+    const void *values;   /* nnz entries of scalar_type */
+    int32_t index_type;   /* enum spmm_index_type */
+    int32_t scalar_type;  /* enum spmm_scalar_type */
+} spmm_csr_dev;
+
+/*
+ * BOO (Blocked COO) in device memory.  Field meanings follow the reference's
+ * boo_matrix_t (torch_fast_spdmm/boo_matrix/boo_matrix.hpp:56-138); index
+ * arrays are int32 and nz_idx is uint16, as the reference stages them onto the
+ * GPU (torch_fast_spdmm/torch_fast_spdmm/boo.py:54-96).
+ */
+typedef struct {
+    int64_t rows, cols, total_nnz;
+    int64_t n_rg, n_cg;            /* row / column groups */
+    int64_t nb, nnz_c;             /* blocks, nonzeros stored in blocks */
+    int64_t rem_nnz, tail_nnz;     /* CSR remainder, flat COO tail */
+    int64_t max_nr, max_nc, max_nnz_blk;
+    int32_t nz_order;              /* enum spmm_boo_order */
+    int32_t scalar_type;           /* enum spmm_scalar_type */
+    int32_t *row_grp_ptr;          /* n_rg+1 */
+    int32_t *row_ids;              /* rows */
+    int32_t *col_grp_ptr;          /* n_cg+1 */
+    int32_t *col_ids;              /* cols */
+    int32_t *blk_row_grp;          /* nb, ascending (blocks sorted by (rg, cg)) */
+    int32_t *blk_col_grp;          /* nb */
+    int32_t *blk_nz_ptr;           /* nb+1 */
+    uint8_t *blk_shift;            /* nb */
+    uint16_t *nz_idx;              /* nnz_c: (local_row << shift) | local_col */
+    void *nz_val;                  /* nnz_c */
+    int32_t *rem_indptr;           /* rows+1 */
+    int32_t *rem_col_ind;          /* rem_nnz */
+    void *rem_vals;                /* rem_nnz */
+    int32_t *tail_row;             /* tail_nnz, non-decreasing (CSR traversal order) */
+    int32_t *tail_col;             /* tail_nnz */
+    void *tail_val;                /* tail_nnz */
+} spmm_boo_dev;
+
+/*
+ * PBR (packed 64-bit-bitset blocks) in device memory.  Field meanings follow
+ * the reference's pbr_matrix_t (torch_fast_spdmm/pbr_matrix/pbr_matrix.hpp:
+ * 98-167) as staged by PBRMatrix.to() (torch_fast_spdmm/torch_fast_spdmm/
+ * __init__.py:17-40): codes as 64-bit words, coordinates, offsets and the
+ * remainder in the host index type.  Blocks are grouped by stripe
+ * (row / block_rows) in ascending stripe order; the builder here emits them in
+ * (stripe, block column) order.
+ */
+typedef struct {
+    int64_t rows, cols, block_rows, block_cols, total_nnz;
+    int64_t nb, nnz_c, rem_nnz;
+    int32_t index_type;            /* enum spmm_index_type (coords, offsets, remainder) */
+    int32_t scalar_type;
+    uint64_t *codes;               /* nb: bit (r*block_cols + c) set for a nonzero */
+    void *coords;                  /* 2*nb: top-left (row, col) of each block */
+    void *offsets;                 /* nb+1: start of each block's values in data */
+    void *data;                    /* nnz_c: values, consumed in bit order */
+    void *rem_indptr;              /* rows+1 */
+    void *rem_col_ind;             /* rem_nnz */
+    void *rem_vals;                /* rem_nnz */
+} spmm_pbr_dev;
+
+/* Optional per-call tuning; NULL selects the defaults.  No process-wide state:
+ * the reference's global setters (torch_fast_spdmm/kernels/boo_kernel.cu:
+ * 58-99) have no counterpart here. */
+typedef struct {
+    int32_t version;        /* must be 1 */
+    int32_t slab_features;  /* features per CTA slab (0 = auto) */
+    int32_t reserved[6];
+} spmm_launch_cfg;
+
+/* ---- status ---------------------------------------------------------- */
+const char *spmm_status_string(int status);
+int spmm_abi_version(void);
+
+/* ---- BOO build (replaces csr_to_boo, torch_fast_spdmm/boo_matrix/
+ * boo_matrix.cpp:53-274, bound at bindings/bindings.cpp:210-213) ---------
+ *
+ * Two phases over one caller-owned workspace:
+ *   1. spmm_boo_build_analyze() runs the whole build up to the output sizes and
+ *      fills the size fields of *sizes (rows, cols, total_nnz, n_rg, n_cg, nb,
+ *      nnz_c, rem_nnz, tail_nnz, max_nr, max_nc, max_nnz_blk, nz_order,
+ *      scalar_type).  It blocks the host until the sizes are known.
+ *   2. The caller allocates the arrays of a spmm_boo_dev with those sizes and
+ *      calls spmm_boo_build_emit() with the same arguments and workspace,
+ *      untouched in between.  Emit is asynchronous on `stream`.
+ * Labels are int32 device arrays of length rows / cols with values in
+ * [0, rows) / [0, cols); the number of groups is max(label) + 1.
+ */
+size_t spmm_boo_build_workspace_size(int64_t rows, int64_t cols, int64_t nnz);
+int spmm_boo_build_analyze(const spmm_csr_dev *A, const int32_t *row_labels,
+                           const int32_t *col_labels, int policy, int64_t threshold,
+                           int nz_order, void *workspace, size_t workspace_bytes,
+                           spmm_boo_dev *sizes, spmm_stream_t stream);
+int spmm_boo_build_emit(const spmm_csr_dev *A, const int32_t *row_labels,
+                        const int32_t *col_labels, int policy, int64_t threshold, int nz_order,
+                        void *workspace, size_t workspace_bytes, spmm_boo_dev *out,
+                        spmm_stream_t stream);
+
+/* ---- PBR build (replaces csr_to_pbr, torch_fast_spdmm/pbr_matrix/
+ * pbr_matrix.cpp:333-448, bound at bindings/bindings.cpp:180-183) ---------
+ * Same two-phase protocol.  block_rows * block_cols <= 64.  Keeps a block iff
+ * popcount(code) >= min_nnz_per_block (the reference's uint8_t parameter,
+ * pbr_matrix.cpp:398).  out->index_type selects the emitted index type. */
+size_t spmm_pbr_build_workspace_size(int64_t rows, int64_t cols, int64_t nnz);
+int spmm_pbr_build_analyze(const spmm_csr_dev *A, int64_t block_rows, int64_t block_cols,
+                           int min_nnz_per_block, void *workspace, size_t workspace_bytes,
+                           spmm_pbr_dev *sizes, spmm_stream_t stream);
+int spmm_pbr_build_emit(const spmm_csr_dev *A, int64_t block_rows, int64_t block_cols,
+                        int min_nnz_per_block, void *workspace, size_t workspace_bytes,
+                        spmm_pbr_dev *out, spmm_stream_t stream);
+
+/* ---- SpMM ------------------------------------------------------------ */
+
+/* Y = A*X for a BOO matrix (replaces boo_spmm_cuda_impl / boo_run_into,
+ * torch_fast_spdmm/bindings/bindings_boo.cu:34-313, bound as
+ * boo_spmm_cuda_{f32,f64} at bindings_boo.cu:408-476).  One launch: blocks,
+ * CSR remainder and COO tail of each row group are summed by the CTA that owns
+ * the group and every Y element is written once (no memset, no atomics). */
+int spmm_boo_matmul(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch, int64_t K,
+                    const spmm_launch_cfg *cfg, spmm_stream_t stream);
+
+/* Y = A*X for a PBR matrix (replaces pbr_spmm_cuda_dispatch / pbr_run_into,
+ * torch_fast_spdmm/bindings/bindings_kernels.cu:18-123, bound as
+ * pbr_spmm_cuda_{i32,i64}_{f32,f64} at bindings_kernels.cu:433-459).  Any
+ * block shape with block_rows * block_cols <= 64 and any K. */
+int spmm_pbr_matmul(const spmm_pbr_dev *A, const void *X, void *Y, int64_t batch, int64_t K,
+                    const spmm_launch_cfg *cfg, spmm_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SPMM_B200_H */

@@ -1,0 +1,21 @@
+// abi.cu -- status text and ABI version of the spmm_b200 C interface.
+#include "../../include/spmm_b200.h"
+
+extern "C" const char *spmm_status_string(int status) {
+    switch (status) {
+        case SPMM_OK: return "ok";
+        case SPMM_EINVAL: return "invalid argument";
+        case SPMM_ELABEL: return "cluster label out of range";
+        case SPMM_EOVERFLOW_U16:
+            return "csr_to_boo: block local index space exceeds uint16 -- reduce max_nr/max_nc in "
+                   "the clustering";
+        case SPMM_EDUPLICATE: return "csr_to_pbr: duplicate (row, col) entries in the input CSR";
+        case SPMM_ECUDA: return "CUDA error";
+        case SPMM_EWORKSPACE: return "workspace too small";
+        case SPMM_EUNSUPPORTED: return "size or type not supported";
+        case SPMM_EALIGN: return "misaligned pointer";
+        default: return "unknown status";
+    }
+}
+
+extern "C" int spmm_abi_version(void) { return 1; }

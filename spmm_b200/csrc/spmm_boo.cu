@@ -1,0 +1,389 @@
+// spmm_boo.cu -- Y = A*X for A in BOO format on sm_100a.
+//
+// Replaces the reference's block kernel + CSR-remainder kernel + tail kernel
+// trio and their 3-stream fork/join over a memset Y (torch_fast_spdmm/
+// bindings/bindings_boo.cu:34-118, kernels/boo_kernel.cu:410-595 and 905-937,
+// kernels/pbr_kernel.cu:976-1049) with ONE launch in which a CTA owns a
+// (row group, feature slab, batch) work item:
+//   * blocks of the row group are contiguous (sorted by (rg, cg),
+//     boo_matrix.cpp:123-125); the CTA stages their nonzeros in shared memory
+//     as (global column, value) pairs in batches, with a per-row start table;
+//   * each group of LPR lanes owns rows of the group and accumulates, in
+//     registers, the row's block entries, then its CSR-remainder row, then its
+//     tail entries (tail rows are non-decreasing: binary search);
+//   * every Y element is stored exactly once -- no memset, no atomics.
+// Per output row the nonzeros are summed in the reference CPU path's order
+// (blocks in order, entries in order, remainder, tail; boo_matrix.cpp:
+// 336-396), with fused multiply-adds.
+#include "spmm_common.cuh"
+
+namespace spmm {
+namespace {
+
+constexpr int kBooThreads = 256;
+constexpr int kRowsChunk = 32;      // rows of a row group handled per pass
+constexpr int kStageCap = 2048;     // staged nonzeros per batch
+constexpr int kMaxSeg = 32;         // block segments per batch (one per warp-0 lane)
+
+template <typename S>
+struct BooParams {
+    int64_t rows, cols, K, batch, nb, tail_nnz;
+    const int32_t *row_grp_ptr, *row_ids, *col_grp_ptr, *col_ids;
+    const int32_t *blk_row_grp, *blk_col_grp, *blk_nz_ptr;
+    const uint8_t *blk_shift;
+    const uint16_t *nz_idx;
+    const S *nz_val;
+    const int32_t *rem_indptr, *rem_col;
+    const S *rem_val;
+    const int32_t *tail_row, *tail_col;
+    const S *tail_val;
+    const S *X;
+    S *Y;
+    int rowmajor;
+};
+
+// first index in a[0..n) with a[i] >= key (a ascending)
+__device__ __forceinline__ int64_t lower_bound_i32(const int32_t *a, int64_t n, int64_t key) {
+    int64_t lo = 0, hi = n;
+    while (lo < hi) {
+        int64_t mid = (lo + hi) >> 1;
+        if ((int64_t)a[mid] < key) lo = mid + 1; else hi = mid;
+    }
+    return lo;
+}
+
+// last segment s in [0, nseg) with start[s] <= e
+__device__ __forceinline__ int find_seg(const int32_t *start, int nseg, int e) {
+    int lo = 0, hi = nseg - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (start[mid] <= e) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+}
+
+template <typename S>
+struct BooSmem {
+    int32_t col[kStageCap];
+    S val[kStageCap];
+    uint16_t lrow[kStageCap];
+    uint16_t rt[kMaxSeg][kRowsChunk + 1];   // row start table per segment
+    int32_t seg_start[kMaxSeg + 1];         // staging offset of each segment
+    int32_t seg_k0[kMaxSeg];
+    int32_t seg_cbase[kMaxSeg];
+    uint8_t seg_shift[kMaxSeg];
+    int32_t nseg, total;
+    int64_t blk_lo, blk_hi, next_blk, next_k;
+};
+
+// acc += a * X[c, lane's features]; `vm` masks slots past K.
+template <typename S, int VEC, int VPT, int LPR, int U>
+__device__ __forceinline__ void accumulate(Frag<S, VEC> (&acc)[VPT], const int32_t *cols,
+                                           const S *vals, int64_t e0, int64_t e1, const S *xl,
+                                           int64_t K, const bool (&vm)[VPT]) {
+    constexpr int STR = LPR * VEC;
+    int64_t e = e0;
+    for (; e + U <= e1; e += U) {
+        S a[U];
+        Frag<S, VEC> x[U][VPT];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            a[u] = vals[e + u];
+            const S *xr = xl + (int64_t)cols[e + u] * K;
+#pragma unroll
+            for (int v = 0; v < VPT; ++v)
+                if (vm[v]) x[u][v] = ldg_frag<S, VEC>(xr + v * STR);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+#pragma unroll
+            for (int v = 0; v < VPT; ++v)
+                if (vm[v])
+#pragma unroll
+                    for (int q = 0; q < VEC; ++q) acc[v].v[q] = fma(a[u], x[u][v].v[q], acc[v].v[q]);
+    }
+    for (; e < e1; ++e) {
+        const S a = vals[e];
+        const S *xr = xl + (int64_t)cols[e] * K;
+#pragma unroll
+        for (int v = 0; v < VPT; ++v)
+            if (vm[v]) {
+                Frag<S, VEC> x = ldg_frag<S, VEC>(xr + v * STR);
+#pragma unroll
+                for (int q = 0; q < VEC; ++q) acc[v].v[q] = fma(a, x.v[q], acc[v].v[q]);
+            }
+    }
+}
+
+template <typename S, int VEC, int VPT, int LPR>
+__global__ void __launch_bounds__(kBooThreads)
+boo_spmm_kernel(const BooParams<S> p) {
+    constexpr int NG = kBooThreads / LPR;        // lane groups per CTA
+    constexpr int RPG = kRowsChunk / NG;          // rows per lane group per chunk
+    constexpr int SLAB = LPR * VPT * VEC;
+    constexpr int U = VPT == 1 ? 4 : 2;
+    static_assert(RPG >= 1 && RPG * NG == kRowsChunk, "row mapping");
+    __shared__ BooSmem<S> sm;
+
+    const int tid = threadIdx.x;
+    const int g = tid / LPR, l = tid % LPR;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int64_t rg = blockIdx.x;
+    const int64_t f0 = (int64_t)blockIdx.y * SLAB + (int64_t)l * VEC;
+    bool vm[VPT];
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) vm[v] = f0 + (int64_t)v * LPR * VEC < p.K;
+
+    const int32_t rbase = p.row_grp_ptr[rg];
+    const int32_t n_r = p.row_grp_ptr[rg + 1] - rbase;
+    if (tid == 0) {
+        sm.blk_lo = lower_bound_i32(p.blk_row_grp, p.nb, rg);
+        sm.blk_hi = lower_bound_i32(p.blk_row_grp, p.nb, rg + 1);
+    }
+    __syncthreads();
+    const int64_t blk_lo = sm.blk_lo, blk_hi = sm.blk_hi;
+
+    for (int64_t bt = blockIdx.z; bt < p.batch; bt += gridDim.z) {
+        const S *xl = p.X + bt * p.cols * p.K + f0;
+        S *yb = p.Y + bt * p.rows * p.K;
+        for (int32_t r0 = 0; r0 < n_r; r0 += kRowsChunk) {
+            const int R = n_r - r0 < kRowsChunk ? n_r - r0 : kRowsChunk;
+            Frag<S, VEC> acc[RPG][VPT];
+#pragma unroll
+            for (int i = 0; i < RPG; ++i)
+#pragma unroll
+                for (int v = 0; v < VPT; ++v)
+#pragma unroll
+                    for (int q = 0; q < VEC; ++q) acc[i][v].v[q] = S(0);
+
+            int64_t cur_blk = blk_lo;
+            int64_t cur_k = blk_lo < blk_hi ? p.blk_nz_ptr[blk_lo] : 0;
+            while (cur_blk < blk_hi) {
+                // ---- plan a batch of block segments (warp 0) ----
+                if (warp == 0) {
+                    const int64_t b = cur_blk + lane;
+                    const bool valid = b < blk_hi;
+                    int64_t k0 = 0, k1 = 0;
+                    if (valid) {
+                        k0 = lane == 0 ? cur_k : (int64_t)p.blk_nz_ptr[b];
+                        k1 = p.blk_nz_ptr[b + 1];
+                    }
+                    int64_t len = k1 - k0;
+                    int64_t pre = len;  // inclusive prefix
+#pragma unroll
+                    for (int o = 1; o < 32; o <<= 1) {
+                        int64_t n = __shfl_up_sync(kFullMask, pre, o);
+                        if (lane >= o) pre += n;
+                    }
+                    const unsigned fits = __ballot_sync(kFullMask, valid && pre <= kStageCap);
+                    const int nfit = __popc(fits);
+                    if (nfit == 0) {
+                        // first block alone overflows the stage: take a piece of it
+                        if (lane == 0) {
+                            sm.seg_start[0] = 0;
+                            sm.seg_start[1] = kStageCap;
+                            sm.seg_k0[0] = (int32_t)k0;
+                            sm.seg_shift[0] = p.blk_shift[b];
+                            sm.seg_cbase[0] = p.col_grp_ptr[p.blk_col_grp[b]];
+                            sm.nseg = 1;
+                            sm.total = kStageCap;
+                            const int64_t nk = k0 + kStageCap;
+                            sm.next_blk = nk >= k1 ? b + 1 : b;
+                            sm.next_k = nk;
+                        }
+                    } else {
+                        if (lane < nfit) {
+                            sm.seg_start[lane] = (int32_t)(pre - len);
+                            sm.seg_k0[lane] = (int32_t)k0;
+                            sm.seg_shift[lane] = p.blk_shift[b];
+                            sm.seg_cbase[lane] = p.col_grp_ptr[p.blk_col_grp[b]];
+                        }
+                        if (lane == nfit - 1) {
+                            sm.seg_start[nfit] = (int32_t)pre;
+                            sm.nseg = nfit;
+                            sm.total = (int32_t)pre;
+                            sm.next_blk = cur_blk + nfit;
+                            sm.next_k = k1;  // == blk_nz_ptr[cur_blk + nfit]
+                        }
+                    }
+                }
+                __syncthreads();
+                const int nseg = sm.nseg, total = sm.total;
+                // ---- stage (global column, value, local row) ----
+                for (int e = tid; e < total; e += kBooThreads) {
+                    const int s = find_seg(sm.seg_start, nseg, e);
+                    const int64_t k = (int64_t)sm.seg_k0[s] + (e - sm.seg_start[s]);
+                    const uint32_t idx = p.nz_idx[k];
+                    const uint32_t shift = sm.seg_shift[s];
+                    sm.col[e] = p.col_ids[sm.seg_cbase[s] + (int32_t)(idx & ((1u << shift) - 1u))];
+                    sm.val[e] = p.nz_val[k];
+                    sm.lrow[e] = (uint16_t)(idx >> shift);
+                }
+                __syncthreads();
+                if (p.rowmajor) {
+                    // rt[s][q] = first staged entry of segment s with local row >= r0+q
+                    for (int e = tid; e < total; e += kBooThreads) {
+                        const int s = find_seg(sm.seg_start, nseg, e);
+                        const int lr = sm.lrow[e];
+                        const int prev = e == sm.seg_start[s] ? -1 : (int)sm.lrow[e - 1];
+                        int qa = prev - r0 + 1, qb = lr - r0;
+                        if (qa < 0) qa = 0;
+                        if (qb > R) qb = R;
+                        for (int q = qa; q <= qb; ++q) sm.rt[s][q] = (uint16_t)e;
+                        if (e + 1 == sm.seg_start[s + 1]) {
+                            int qc = lr - r0 + 1;
+                            if (qc < 0) qc = 0;
+                            for (int q = qc; q <= R; ++q) sm.rt[s][q] = (uint16_t)(e + 1);
+                        }
+                    }
+                    __syncthreads();
+                }
+                // ---- accumulate ----
+#pragma unroll
+                for (int i = 0; i < RPG; ++i) {
+                    const int q = g + i * NG;
+                    if (q < R) {
+                        for (int s = 0; s < nseg; ++s) {
+                            if (p.rowmajor) {
+                                accumulate<S, VEC, VPT, LPR, U>(acc[i], sm.col, sm.val, sm.rt[s][q],
+                                                                sm.rt[s][q + 1], xl, p.K, vm);
+                            } else {
+                                const int lr = r0 + q;
+                                for (int e = sm.seg_start[s]; e < sm.seg_start[s + 1]; ++e)
+                                    if (sm.lrow[e] == lr)
+                                        accumulate<S, VEC, VPT, LPR, 1>(acc[i], sm.col, sm.val, e, e + 1,
+                                                                        xl, p.K, vm);
+                            }
+                        }
+                    }
+                }
+                cur_blk = sm.next_blk;
+                cur_k = sm.next_k;
+                __syncthreads();
+            }
+            // ---- remainder row, tail entries, store ----
+#pragma unroll
+            for (int i = 0; i < RPG; ++i) {
+                const int q = g + i * NG;
+                if (q < R) {
+                    const int32_t row = p.row_ids[rbase + r0 + q];
+                    accumulate<S, VEC, VPT, LPR, U>(acc[i], p.rem_col, p.rem_val, p.rem_indptr[row],
+                                                    p.rem_indptr[row + 1], xl, p.K, vm);
+                    if (p.tail_nnz) {
+                        const int64_t t0 = lower_bound_i32(p.tail_row, p.tail_nnz, row);
+                        const int64_t t1 = lower_bound_i32(p.tail_row, p.tail_nnz, (int64_t)row + 1);
+                        accumulate<S, VEC, VPT, LPR, 1>(acc[i], p.tail_col, p.tail_val, t0, t1, xl,
+                                                        p.K, vm);
+                    }
+                    S *yr = yb + (int64_t)row * p.K + f0;
+#pragma unroll
+                    for (int v = 0; v < VPT; ++v)
+                        if (vm[v]) st_frag<S, VEC>(yr + v * LPR * VEC, acc[i][v]);
+                }
+            }
+        }
+    }
+}
+
+template <typename S, int VEC, int VPT, int LPR>
+int launch_boo_n(const BooParams<S> &p, int64_t n_rg, cudaStream_t s) {
+    constexpr int SLAB = LPR * VPT * VEC;
+    const int64_t slabs = ceil_div(p.K, SLAB);
+    if (slabs > 65535 || n_rg > 0x7fffffffLL) return SPMM_EUNSUPPORTED;
+    dim3 grid((unsigned)n_rg, (unsigned)slabs, (unsigned)(p.batch < 65535 ? p.batch : 65535));
+    boo_spmm_kernel<S, VEC, VPT, LPR><<<grid, kBooThreads, 0, s>>>(p);
+    SPMM_LAUNCH_CHECK();
+    return SPMM_OK;
+}
+
+template <typename S>
+int boo_dispatch(const BooParams<S> &p, int64_t n_rg, bool aligned, cudaStream_t s);
+
+template <>
+int boo_dispatch<float>(const BooParams<float> &p, int64_t n_rg, bool aligned, cudaStream_t s) {
+    const int64_t K = p.K;
+    if (aligned && K % 4 == 0) {
+        if (K <= 32) return launch_boo_n<float, 4, 1, 8>(p, n_rg, s);
+        if (K <= 64) return launch_boo_n<float, 4, 1, 16>(p, n_rg, s);
+        if (K <= 128) return launch_boo_n<float, 4, 1, 32>(p, n_rg, s);
+        if (K <= 256) return launch_boo_n<float, 4, 2, 32>(p, n_rg, s);
+        return launch_boo_n<float, 4, 4, 32>(p, n_rg, s);
+    }
+    if (K <= 32) return launch_boo_n<float, 1, 1, 32>(p, n_rg, s);
+    if (K <= 64) return launch_boo_n<float, 1, 2, 32>(p, n_rg, s);
+    return launch_boo_n<float, 1, 4, 32>(p, n_rg, s);
+}
+
+template <>
+int boo_dispatch<double>(const BooParams<double> &p, int64_t n_rg, bool aligned, cudaStream_t s) {
+    const int64_t K = p.K;
+    if (aligned && K % 2 == 0) {
+        if (K <= 16) return launch_boo_n<double, 2, 1, 8>(p, n_rg, s);
+        if (K <= 32) return launch_boo_n<double, 2, 1, 16>(p, n_rg, s);
+        if (K <= 64) return launch_boo_n<double, 2, 1, 32>(p, n_rg, s);
+        if (K <= 128) return launch_boo_n<double, 2, 2, 32>(p, n_rg, s);
+        return launch_boo_n<double, 2, 4, 32>(p, n_rg, s);
+    }
+    if (K <= 32) return launch_boo_n<double, 1, 1, 32>(p, n_rg, s);
+    if (K <= 64) return launch_boo_n<double, 1, 2, 32>(p, n_rg, s);
+    return launch_boo_n<double, 1, 4, 32>(p, n_rg, s);
+}
+
+template <typename S>
+int boo_matmul_impl(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch, int64_t K,
+                    cudaStream_t s) {
+    BooParams<S> p;
+    p.rows = A->rows;
+    p.cols = A->cols;
+    p.K = K;
+    p.batch = batch;
+    p.nb = A->nb;
+    p.tail_nnz = A->tail_nnz;
+    p.row_grp_ptr = A->row_grp_ptr;
+    p.row_ids = A->row_ids;
+    p.col_grp_ptr = A->col_grp_ptr;
+    p.col_ids = A->col_ids;
+    p.blk_row_grp = A->blk_row_grp;
+    p.blk_col_grp = A->blk_col_grp;
+    p.blk_nz_ptr = A->blk_nz_ptr;
+    p.blk_shift = A->blk_shift;
+    p.nz_idx = A->nz_idx;
+    p.nz_val = (const S *)A->nz_val;
+    p.rem_indptr = A->rem_indptr;
+    p.rem_col = A->rem_col_ind;
+    p.rem_val = (const S *)A->rem_vals;
+    p.tail_row = A->tail_row;
+    p.tail_col = A->tail_col;
+    p.tail_val = (const S *)A->tail_val;
+    p.X = (const S *)X;
+    p.Y = (S *)Y;
+    p.rowmajor = A->nz_order == SPMM_BOO_ROWMAJOR;
+    const uintptr_t mis = ((uintptr_t)X | (uintptr_t)Y) & 15;
+    return boo_dispatch<S>(p, A->n_rg, mis == 0, s);
+}
+
+}  // namespace
+}  // namespace spmm
+
+using namespace spmm;
+
+extern "C" int spmm_boo_matmul(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch, int64_t K,
+                               const spmm_launch_cfg *cfg, spmm_stream_t stream) {
+    if (!A || batch < 0 || K < 0) return SPMM_EINVAL;
+    if (cfg && cfg->version != 1) return SPMM_EINVAL;
+    if (A->scalar_type != SPMM_F32 && A->scalar_type != SPMM_F64) return SPMM_EINVAL;
+    if (A->nz_order != SPMM_BOO_ROWMAJOR && A->nz_order != SPMM_BOO_COLMAJOR) return SPMM_EINVAL;
+    if (A->rows < 0 || A->cols < 0 || A->n_rg < 0 || A->nb < 0 || A->tail_nnz < 0) return SPMM_EINVAL;
+    if (A->rows > 0x7fffffffLL || A->cols > 0x7fffffffLL) return SPMM_EUNSUPPORTED;
+    if (A->max_nr > 65536 || A->max_nc > 65536) return SPMM_EUNSUPPORTED;
+    if (batch == 0 || K == 0 || A->rows == 0) return SPMM_OK;
+    if (!Y || (A->cols && !X)) return SPMM_EINVAL;
+    if (!A->row_grp_ptr || !A->row_ids || !A->rem_indptr) return SPMM_EINVAL;
+    if (A->nb && (!A->blk_row_grp || !A->blk_col_grp || !A->blk_nz_ptr || !A->blk_shift ||
+                  !A->nz_idx || !A->nz_val || !A->col_grp_ptr || !A->col_ids))
+        return SPMM_EINVAL;
+    if (A->n_rg == 0) return SPMM_EINVAL;  // rows > 0 need at least one group
+    cudaStream_t s = (cudaStream_t)stream;
+    if (A->scalar_type == SPMM_F32) return boo_matmul_impl<float>(A, X, Y, batch, K, s);
+    return boo_matmul_impl<double>(A, X, Y, batch, K, s);
+}

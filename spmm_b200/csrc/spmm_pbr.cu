@@ -1,0 +1,220 @@
+// spmm_pbr.cu -- Y = A*X for A in PBR format on sm_100a.
+//
+// Replaces the reference's per-block kernel pbr_spmm_vec_kernel /
+// pbr_spmm_zero_idle_kernel plus the concurrent CSR-remainder kernel over a
+// memset Y (torch_fast_spdmm/kernels/pbr_kernel.cu:12-326 and 976-1135,
+// bindings/bindings_kernels.cu:18-123) with ONE launch in which each group of
+// LPR lanes owns an output row:
+//   * the row's stripe (row / block_rows) has a contiguous run of blocks; the
+//     CTA finds the runs of its stripes with one binary search each;
+//   * per block the row's bits are (code >> (r % BR) * BC) & mask; the value
+//     of bit c is data[offset + popcount(code bits below it)] -- the bit-order
+//     consumption of the reference (pbr_matrix.cpp:42-55) -- decoded with
+//     __popcll / __ffsll, no bitset scan of the whole code;
+//   * then the row's remainder entries; Y is stored once (no memset, no
+//     atomics) and is correct for every K (the reference's vec kernel needs K
+//     to be a power-of-two multiple of its tile, pbr_kernel.cu:81-87).
+#include "spmm_common.cuh"
+
+namespace spmm {
+namespace {
+
+constexpr int kPbrThreads = 256;
+constexpr int kPbrRows = 32;   // rows per CTA
+
+template <typename S, typename I>
+struct PbrParams {
+    int64_t rows, cols, K, batch, nb, br, bc;
+    const uint64_t *codes;
+    const I *coords, *offsets, *rem_indptr, *rem_col;
+    const S *data, *rem_val;
+    const S *X;
+    S *Y;
+};
+
+template <typename I>
+__device__ __forceinline__ int64_t first_block_of_stripe(const I *coords, int64_t nb, int64_t row0) {
+    // blocks are grouped by stripe in ascending order; coords[2b] is the
+    // block's top row
+    int64_t lo = 0, hi = nb;
+    while (lo < hi) {
+        int64_t mid = (lo + hi) >> 1;
+        if ((int64_t)coords[2 * mid] < row0) lo = mid + 1; else hi = mid;
+    }
+    return lo;
+}
+
+template <typename S, int VEC, int VPT, int LPR>
+__device__ __forceinline__ void fma_x(Frag<S, VEC> (&acc)[VPT], S a, const S *xr, const bool (&vm)[VPT]) {
+#pragma unroll
+    for (int v = 0; v < VPT; ++v)
+        if (vm[v]) {
+            Frag<S, VEC> x = ldg_frag<S, VEC>(xr + v * LPR * VEC);
+#pragma unroll
+            for (int q = 0; q < VEC; ++q) acc[v].v[q] = fma(a, x.v[q], acc[v].v[q]);
+        }
+}
+
+template <typename S, typename I, int VEC, int VPT, int LPR>
+__global__ void __launch_bounds__(kPbrThreads)
+pbr_spmm_kernel(const PbrParams<S, I> p) {
+    constexpr int NG = kPbrThreads / LPR;
+    constexpr int RPG = kPbrRows / NG;
+    constexpr int SLAB = LPR * VPT * VEC;
+    static_assert(RPG >= 1 && RPG * NG == kPbrRows, "row mapping");
+    __shared__ int64_t stripe_blk[kPbrRows + 2];
+
+    const int tid = threadIdx.x;
+    const int g = tid / LPR, l = tid % LPR;
+    const int64_t row_base = (int64_t)blockIdx.x * kPbrRows;
+    const int64_t f0 = (int64_t)blockIdx.y * SLAB + (int64_t)l * VEC;
+    bool vm[VPT];
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) vm[v] = f0 + (int64_t)v * LPR * VEC < p.K;
+
+    // block runs of the stripes this CTA touches
+    const int64_t s_first = row_base / p.br;
+    int64_t row_last = row_base + kPbrRows - 1;
+    if (row_last >= p.rows) row_last = p.rows - 1;
+    const int64_t n_str = row_last / p.br - s_first + 1;   // <= kPbrRows
+    if (tid <= n_str) stripe_blk[tid] = first_block_of_stripe(p.coords, p.nb, (s_first + tid) * p.br);
+    __syncthreads();
+
+    const uint64_t bcmask = p.bc >= 64 ? ~0ull : ((1ull << p.bc) - 1ull);
+    for (int64_t bt = blockIdx.z; bt < p.batch; bt += gridDim.z) {
+        const S *xl = p.X + bt * p.cols * p.K + f0;
+        S *yb = p.Y + bt * p.rows * p.K;
+#pragma unroll
+        for (int i = 0; i < RPG; ++i) {
+            const int64_t r = row_base + g + i * NG;
+            if (r >= p.rows) continue;
+            Frag<S, VEC> acc[VPT];
+#pragma unroll
+            for (int v = 0; v < VPT; ++v)
+#pragma unroll
+                for (int q = 0; q < VEC; ++q) acc[v].v[q] = S(0);
+            const int64_t si = r / p.br - s_first;
+            const int rin = (int)(r % p.br);
+            const int sh = rin * (int)p.bc;
+            const uint64_t below = sh >= 64 ? ~0ull : ((1ull << sh) - 1ull);
+            for (int64_t b = stripe_blk[si]; b < stripe_blk[si + 1]; ++b) {
+                const uint64_t code = p.codes[b];
+                uint64_t bits = (sh >= 64 ? 0ull : (code >> sh)) & bcmask;
+                if (!bits) continue;
+                int64_t off = (int64_t)p.offsets[b] + __popcll(code & below);
+                const int64_t col0 = (int64_t)p.coords[2 * b + 1];
+                while (bits) {
+                    const int c = __ffsll((long long)bits) - 1;
+                    bits &= bits - 1;
+                    if (col0 + c >= p.cols) continue;   // never set by a valid build
+                    fma_x<S, VEC, VPT, LPR>(acc, p.data[off++], xl + (col0 + c) * p.K, vm);
+                }
+            }
+            const int64_t j1 = (int64_t)p.rem_indptr[r + 1];
+            int64_t j = (int64_t)p.rem_indptr[r];
+            for (; j + 2 <= j1; j += 2) {
+                const S a0 = p.rem_val[j], a1 = p.rem_val[j + 1];
+                const S *x0 = xl + (int64_t)p.rem_col[j] * p.K;
+                const S *x1 = xl + (int64_t)p.rem_col[j + 1] * p.K;
+                Frag<S, VEC> t0[VPT], t1[VPT];
+#pragma unroll
+                for (int v = 0; v < VPT; ++v)
+                    if (vm[v]) {
+                        t0[v] = ldg_frag<S, VEC>(x0 + v * LPR * VEC);
+                        t1[v] = ldg_frag<S, VEC>(x1 + v * LPR * VEC);
+                    }
+#pragma unroll
+                for (int v = 0; v < VPT; ++v)
+                    if (vm[v])
+#pragma unroll
+                        for (int q = 0; q < VEC; ++q) {
+                            acc[v].v[q] = fma(a0, t0[v].v[q], acc[v].v[q]);
+                            acc[v].v[q] = fma(a1, t1[v].v[q], acc[v].v[q]);
+                        }
+            }
+            if (j < j1) fma_x<S, VEC, VPT, LPR>(acc, p.rem_val[j], xl + (int64_t)p.rem_col[j] * p.K, vm);
+            S *yr = yb + r * p.K + f0;
+#pragma unroll
+            for (int v = 0; v < VPT; ++v)
+                if (vm[v]) st_frag<S, VEC>(yr + v * LPR * VEC, acc[v]);
+        }
+    }
+}
+
+template <typename S, typename I, int VEC, int VPT, int LPR>
+int launch_pbr(const PbrParams<S, I> &p, cudaStream_t s) {
+    constexpr int SLAB = LPR * VPT * VEC;
+    const int64_t slabs = ceil_div(p.K, SLAB);
+    const int64_t ctas = ceil_div(p.rows, kPbrRows);
+    if (slabs > 65535 || ctas > 0x7fffffffLL) return SPMM_EUNSUPPORTED;
+    dim3 grid((unsigned)ctas, (unsigned)slabs, (unsigned)(p.batch < 65535 ? p.batch : 65535));
+    pbr_spmm_kernel<S, I, VEC, VPT, LPR><<<grid, kPbrThreads, 0, s>>>(p);
+    SPMM_LAUNCH_CHECK();
+    return SPMM_OK;
+}
+
+template <typename S, typename I>
+int pbr_dispatch(const PbrParams<S, I> &p, bool aligned, cudaStream_t s) {
+    const int64_t K = p.K;
+    constexpr int V = sizeof(S) == 4 ? 4 : 2;
+    if (aligned && K % V == 0) {
+        if (K <= 8 * V) return launch_pbr<S, I, V, 1, 8>(p, s);
+        if (K <= 16 * V) return launch_pbr<S, I, V, 1, 16>(p, s);
+        if (K <= 32 * V) return launch_pbr<S, I, V, 1, 32>(p, s);
+        if (K <= 64 * V) return launch_pbr<S, I, V, 2, 32>(p, s);
+        return launch_pbr<S, I, V, 4, 32>(p, s);
+    }
+    if (K <= 32) return launch_pbr<S, I, 1, 1, 32>(p, s);
+    if (K <= 64) return launch_pbr<S, I, 1, 2, 32>(p, s);
+    return launch_pbr<S, I, 1, 4, 32>(p, s);
+}
+
+template <typename S, typename I>
+int pbr_matmul_impl(const spmm_pbr_dev *A, const void *X, void *Y, int64_t batch, int64_t K,
+                    cudaStream_t s) {
+    PbrParams<S, I> p;
+    p.rows = A->rows;
+    p.cols = A->cols;
+    p.K = K;
+    p.batch = batch;
+    p.nb = A->nb;
+    p.br = A->block_rows;
+    p.bc = A->block_cols;
+    p.codes = A->codes;
+    p.coords = (const I *)A->coords;
+    p.offsets = (const I *)A->offsets;
+    p.rem_indptr = (const I *)A->rem_indptr;
+    p.rem_col = (const I *)A->rem_col_ind;
+    p.data = (const S *)A->data;
+    p.rem_val = (const S *)A->rem_vals;
+    p.X = (const S *)X;
+    p.Y = (S *)Y;
+    const uintptr_t mis = ((uintptr_t)X | (uintptr_t)Y) & 15;
+    return pbr_dispatch<S, I>(p, mis == 0, s);
+}
+
+}  // namespace
+}  // namespace spmm
+
+using namespace spmm;
+
+extern "C" int spmm_pbr_matmul(const spmm_pbr_dev *A, const void *X, void *Y, int64_t batch, int64_t K,
+                               const spmm_launch_cfg *cfg, spmm_stream_t stream) {
+    if (!A || batch < 0 || K < 0) return SPMM_EINVAL;
+    if (cfg && cfg->version != 1) return SPMM_EINVAL;
+    if (A->scalar_type != SPMM_F32 && A->scalar_type != SPMM_F64) return SPMM_EINVAL;
+    if (A->index_type != SPMM_INDEX_I32 && A->index_type != SPMM_INDEX_I64) return SPMM_EINVAL;
+    if (A->rows < 0 || A->cols < 0 || A->nb < 0) return SPMM_EINVAL;
+    if (A->block_rows <= 0 || A->block_cols <= 0 || A->block_rows * A->block_cols > 64)
+        return SPMM_EINVAL;
+    if (batch == 0 || K == 0 || A->rows == 0) return SPMM_OK;
+    if (!Y || (A->cols && !X) || !A->rem_indptr) return SPMM_EINVAL;
+    if (A->nb && (!A->codes || !A->coords || !A->offsets || !A->data)) return SPMM_EINVAL;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (A->scalar_type == SPMM_F32) {
+        if (A->index_type == SPMM_INDEX_I32) return pbr_matmul_impl<float, int32_t>(A, X, Y, batch, K, s);
+        return pbr_matmul_impl<float, int64_t>(A, X, Y, batch, K, s);
+    }
+    if (A->index_type == SPMM_INDEX_I32) return pbr_matmul_impl<double, int32_t>(A, X, Y, batch, K, s);
+    return pbr_matmul_impl<double, int64_t>(A, X, Y, batch, K, s);
+}
