@@ -21,6 +21,8 @@ def to_device(arr, device, dtype=None) -> torch.Tensor:
     """Host array -> device tensor through pinned memory (the reference stages
     the same way, boo.py:50-51)."""
     a = np.ascontiguousarray(arr, dtype=dtype)
+    if not a.flags.writeable:
+        a = a.copy()
     t = torch.from_numpy(a)
     if t.numel() == 0:
         return torch.empty(t.shape, dtype=t.dtype, device=device)

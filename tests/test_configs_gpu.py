@@ -26,7 +26,7 @@ def _eq(a, b):
 SMALL = {
     'c1_laplacian2d': (lambda: W.laplacian2d(64), 'boo', 32, 128),
     'c2_fem3d': (lambda: W.fem3d(10), 'boo', 32, 128),
-    'c3_powerlaw': (lambda: W.powerlaw(20000), 'boo', 32, 256),
+    'c3_powerlaw': (lambda: W.powerlaw(2500), 'boo', 32, 256),
     'c4_blockdiag': (lambda: W.blockdiag(64, 64), 'boo', 64, 512),
     'c5_uniform': (lambda: W.uniform(50000), 'pbr', 32, 64),
 }

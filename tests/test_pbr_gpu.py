@@ -47,6 +47,7 @@ def test_gpu_build_and_product_match_reference_fixture(cuda, case):
     p = f"p{case['case']}/"
     g = {k[len(p):]: PBR[k] for k in PBR.files if k.startswith(p)}
     mat = sp.csr_matrix((g['data'], g['indices'], g['indptr']), shape=(case['rows'], case['cols']))
+    mat.indptr, mat.indices = g['indptr'], g['indices']   # keep the fixture's index dtype
     pbr = S.csr_to_pbr(mat, case['block_rows'], case['block_cols'], case['min_nnz'])
     ref = dict(rows=case['rows'], cols=case['cols'], block_rows=case['block_rows'],
                block_cols=case['block_cols'], **{f: g[f] for f in O.PBR_FIELDS})
