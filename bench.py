@@ -50,13 +50,18 @@ def parse():
     ap.add_argument('--format', choices=('boo', 'pbr'), default=None)
     ap.add_argument('--e2e-steps', type=int, default=5)
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--gen-kw', default=None,
+                    help='JSON overrides of the generator size (reduced cases for profiling)')
     return ap.parse_args()
 
 
-def make_matrix(cfg_name):
+def make_matrix(cfg_name, gen_kw=None):
     from spmm_b200 import workloads as W
     cfg = W.CONFIGS[cfg_name]
-    return cfg['gen'](**cfg['kw']), cfg
+    kw = dict(cfg['kw'])
+    if gen_kw:
+        kw.update(json.loads(gen_kw))
+    return cfg['gen'](**kw), cfg
 
 
 # ---------------------------------------------------------------------------
@@ -348,7 +353,7 @@ def native_arm(args):
         import datetime
         dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120), device_id=dev)
 
-    mat, cfg = make_matrix(args.config)
+    mat, cfg = make_matrix(args.config, args.gen_kw)
     fmt = args.format or cfg['fmt']
     K = cfg['K']
     t0 = time.perf_counter()
@@ -448,7 +453,8 @@ def native_arm(args):
         'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(ms_step, 5),
         'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32',
         'data': 'synthetic (seeded generator of the config)',
-        'config': {'workload': args.config, 'format': fmt,
+        'config': {'workload': args.config + (f' {args.gen_kw}' if args.gen_kw else ''),
+                   'format': fmt,
                    'grouping': 'identity' if fmt == 'boo' else '8x8 bitset blocks',
                    'target': cfg['target'] if fmt == 'boo' else None, 'rows': int(mat.shape[0]),
                    'nnz': int(mat.nnz), 'K_per_gpu': K, 'parallelism': f'feature-split x{world}',
