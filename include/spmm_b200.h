@@ -42,7 +42,8 @@ enum spmm_status {
     SPMM_ECUDA = 5,           /* a CUDA runtime call or kernel launch failed */
     SPMM_EWORKSPACE = 6,      /* workspace smaller than *_workspace_size() asked for */
     SPMM_EUNSUPPORTED = 7,    /* size or type outside what this build handles */
-    SPMM_EALIGN = 8           /* a pointer lacks the alignment its dtype requires */
+    SPMM_EALIGN = 8,          /* a pointer lacks the alignment its dtype requires */
+    SPMM_ESCRATCH = 9         /* problem larger than spmm_boo_build_noalloc's fixed scratch */
 };
 
 enum spmm_index_type { SPMM_INDEX_I32 = 0, SPMM_INDEX_I64 = 1 };
@@ -152,6 +153,28 @@ int spmm_boo_build_emit(const spmm_csr_dev *A, const int32_t *row_labels,
                         const int32_t *col_labels, int policy, int64_t threshold, int nz_order,
                         void *workspace, size_t workspace_bytes, spmm_boo_dev *out,
                         spmm_stream_t stream);
+
+/* ---- BOO build without any device allocation --------------------------
+ * No counterpart in the reference: for callers that cannot allocate device
+ * memory (a framework that owns all device memory through its own pool, a
+ * loop where an allocation may block or fail, a plugin host that forbids heap
+ * growth).  One call runs both builder phases with their scratch in a fixed
+ * 32 MiB device array compiled into the library instead of a caller
+ * workspace; nothing is allocated.  Problems whose
+ * spmm_boo_build_workspace_size() exceeds 32 MiB (about half a million
+ * nonzeros) return SPMM_ESCRATCH before any device work.
+ *   - `out` arrays are caller-allocated for the worst case: row_grp_ptr and
+ *     rem_indptr rows+1, row_ids rows, col_grp_ptr cols+1, col_ids cols,
+ *     blk_nz_ptr nnz+1, every other array nnz entries.  On return the size
+ *     fields of *out hold the real sizes.
+ *   - The first call on a device (with it current) looks up the array's device
+ *     address; make that first call before any stream capture.
+ *   - Blocks the host until the sizes are known, like the analyze phase.
+ *   - All calls share the array: calls whose GPU work overlaps race and must
+ *     be serialised by the caller. */
+int spmm_boo_build_noalloc(const spmm_csr_dev *A, const int32_t *row_labels,
+                           const int32_t *col_labels, int policy, int64_t threshold, int nz_order,
+                           spmm_boo_dev *out, spmm_stream_t stream);
 
 /* ---- PBR build (replaces csr_to_pbr, torch_fast_spdmm/pbr_matrix/
  * pbr_matrix.cpp:333-448, bound at bindings/bindings.cpp:180-183) ---------

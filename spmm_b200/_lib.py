@@ -27,8 +27,11 @@ SPMM_EALIGN = 8
 I32, I64 = 0, 1
 F32, F64 = 0, 1
 
+SPMM_ESCRATCH = 9
+
 EXPORTS = ('spmm_status_string', 'spmm_abi_version', 'spmm_boo_build_workspace_size',
-           'spmm_boo_build_analyze', 'spmm_boo_build_emit', 'spmm_pbr_build_workspace_size',
+           'spmm_boo_build_analyze', 'spmm_boo_build_emit', 'spmm_boo_build_noalloc',
+           'spmm_pbr_build_workspace_size',
            'spmm_pbr_build_analyze', 'spmm_pbr_build_emit', 'spmm_boo_matmul', 'spmm_pbr_matmul')
 
 
@@ -92,6 +95,9 @@ def lib() -> C.CDLL:
                                              C.c_int64, C.c_int, C.c_void_p, C.c_size_t,
                                              C.POINTER(BooDev), C.c_void_p]
         L.spmm_boo_build_emit.argtypes = L.spmm_boo_build_analyze.argtypes
+        L.spmm_boo_build_noalloc.argtypes = [C.POINTER(CsrDev), C.c_void_p, C.c_void_p, C.c_int,
+                                             C.c_int64, C.c_int, C.POINTER(BooDev), C.c_void_p]
+        L.spmm_boo_build_noalloc.restype = C.c_int
         L.spmm_pbr_build_analyze.argtypes = [C.POINTER(CsrDev), C.c_int64, C.c_int64, C.c_int,
                                              C.c_void_p, C.c_size_t, C.POINTER(PbrDev), C.c_void_p]
         L.spmm_pbr_build_emit.argtypes = L.spmm_pbr_build_analyze.argtypes

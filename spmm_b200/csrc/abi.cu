@@ -14,6 +14,8 @@ extern "C" const char *spmm_status_string(int status) {
         case SPMM_EWORKSPACE: return "workspace too small";
         case SPMM_EUNSUPPORTED: return "size or type not supported";
         case SPMM_EALIGN: return "misaligned pointer";
+        case SPMM_ESCRATCH:
+            return "spmm_boo_build_noalloc: problem exceeds the 32 MiB static scratch";
         default: return "unknown status";
     }
 }
