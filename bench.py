@@ -372,9 +372,14 @@ def native_arm(args):
     y = torch.empty((mat.shape[0], K), dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream(dev)
     sh = stream.cuda_stream
+    lcfg = _lib.launch_cfg('auto')
+    ws_bytes = L.spmm_boo_matmul_workspace_size(C.byref(st), 1, K, C.byref(lcfg)) if fmt == 'boo' else 0
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    lcfg.workspace, lcfg.workspace_bytes = ws.data_ptr(), ws_bytes
+    launches_per_step = 2 if ws_bytes else 1   # gather pass + tensor-core product, or one kernel
 
     def launch():
-        rc = fn(C.byref(st), x.data_ptr(), y.data_ptr(), 1, K, None, sh)
+        rc = fn(C.byref(st), x.data_ptr(), y.data_ptr(), 1, K, C.byref(lcfg), sh)
         if rc:
             raise _lib.SpmmError(rc, 'bench')
 
@@ -464,7 +469,7 @@ def native_arm(args):
                      'unit': 'GB/s', 'frac': round(achieved / peak, 4), 'traffic': traffic,
                      'peak_kind': peak_kind, 'alg_bytes_per_launch': int(alg),
                      'kernel': 'boo_spmm_kernel' if fmt == 'boo' else 'pbr_spmm_kernel'},
-        'e2e': e2e, 'gpu_launches': args.steps,
+        'e2e': e2e, 'gpu_launches': args.steps * launches_per_step,
         'clocks': clocks, 'cpu_baseline': cpu,
     }
     print(json.dumps(line), flush=True)

@@ -123,8 +123,20 @@ typedef struct {
 typedef struct {
     int32_t version;        /* must be 1 */
     int32_t slab_features;  /* features per CTA slab (0 = auto) */
-    int32_t reserved[6];
+    int32_t engine;         /* enum spmm_engine (BOO product only; PBR ignores it) */
+    int32_t reserved;
+    void *workspace;        /* optional device scratch of the tensor-core BOO product, */
+    uint64_t workspace_bytes; /* spmm_boo_matmul_workspace_size() bytes, 16-byte aligned */
 } spmm_launch_cfg;
+
+/* Which units multiply the BOO blocks.  AUTO takes the tensor cores when the
+ * matrix is float32, K is a multiple of 128 and every block fits 64 x 64
+ * (3xTF32 split: within the float32 tolerance), else the CUDA cores. */
+enum spmm_engine {
+    SPMM_ENGINE_AUTO = 0,
+    SPMM_ENGINE_CUDA_CORES = 1,   /* fp32/fp64 FMA, the reference CPU path's summation order */
+    SPMM_ENGINE_TENSOR_CORES = 2  /* tcgen05 3xTF32; SPMM_EUNSUPPORTED when not applicable */
+};
 
 /* ---- status ---------------------------------------------------------- */
 const char *spmm_status_string(int status);
@@ -198,6 +210,19 @@ int spmm_pbr_build_emit(const spmm_csr_dev *A, int64_t block_rows, int64_t block
  * the group and every Y element is written once (no memset, no atomics). */
 int spmm_boo_matmul(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch, int64_t K,
                     const spmm_launch_cfg *cfg, spmm_stream_t stream);
+
+/* Bytes of device scratch the BOO product takes through cfg->workspace (the X
+ * panels gathered by column group for the tensor cores); 0 when the
+ * CUDA-core product runs.  Without a workspace the product allocates the same
+ * amount stream-ordered (cudaMallocAsync) for the call. */
+size_t spmm_boo_matmul_workspace_size(const spmm_boo_dev *A, int64_t batch, int64_t K,
+                                      const spmm_launch_cfg *cfg);
+
+/* Status word of the tensor-core kernels (no reference counterpart): 0, or the
+ * code of the first bounded wait that expired on the device (the launch then
+ * stopped early and Y is incomplete).  Synchronises the device; `clear`
+ * resets the word.  Returns -1 when the CUDA runtime fails. */
+int spmm_tc_status(int clear);
 
 /* Y = A*X for a PBR matrix (replaces pbr_spmm_cuda_dispatch / pbr_run_into,
  * torch_fast_spdmm/bindings/bindings_kernels.cu:18-123, bound as

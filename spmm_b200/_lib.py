@@ -32,7 +32,8 @@ SPMM_ESCRATCH = 9
 EXPORTS = ('spmm_status_string', 'spmm_abi_version', 'spmm_boo_build_workspace_size',
            'spmm_boo_build_analyze', 'spmm_boo_build_emit', 'spmm_boo_build_noalloc',
            'spmm_pbr_build_workspace_size',
-           'spmm_pbr_build_analyze', 'spmm_pbr_build_emit', 'spmm_boo_matmul', 'spmm_pbr_matmul')
+           'spmm_pbr_build_analyze', 'spmm_pbr_build_emit', 'spmm_boo_matmul', 'spmm_pbr_matmul',
+           'spmm_tc_status', 'spmm_boo_matmul_workspace_size')
 
 
 class CsrDev(C.Structure):
@@ -65,7 +66,17 @@ class PbrDev(C.Structure):
 
 
 class LaunchCfg(C.Structure):
-    _fields_ = [('version', C.c_int32), ('slab_features', C.c_int32), ('reserved', C.c_int32 * 6)]
+    _fields_ = [('version', C.c_int32), ('slab_features', C.c_int32), ('engine', C.c_int32),
+                ('reserved', C.c_int32), ('workspace', C.c_void_p), ('workspace_bytes', C.c_uint64)]
+
+
+ENGINES = {'auto': 0, 'cuda_cores': 1, 'tensor_cores': 2}
+
+
+def launch_cfg(engine: str = 'auto', workspace: int = 0, workspace_bytes: int = 0) -> 'LaunchCfg':
+    if engine not in ENGINES:
+        raise ValueError(f"engine must be one of {sorted(ENGINES)}, got {engine!r}")
+    return LaunchCfg(1, 0, ENGINES[engine], 0, workspace or None, workspace_bytes)
 
 
 class SpmmError(RuntimeError):
@@ -105,6 +116,11 @@ def lib() -> C.CDLL:
                                       C.POINTER(LaunchCfg), C.c_void_p]
         L.spmm_pbr_matmul.argtypes = [C.POINTER(PbrDev), C.c_void_p, C.c_void_p, C.c_int64, C.c_int64,
                                       C.POINTER(LaunchCfg), C.c_void_p]
+        L.spmm_boo_matmul_workspace_size.argtypes = [C.POINTER(BooDev), C.c_int64, C.c_int64,
+                                                     C.POINTER(LaunchCfg)]
+        L.spmm_boo_matmul_workspace_size.restype = C.c_size_t
+        L.spmm_tc_status.argtypes = [C.c_int]
+        L.spmm_tc_status.restype = C.c_int
         for n in ('spmm_boo_build_analyze', 'spmm_boo_build_emit', 'spmm_pbr_build_analyze',
                   'spmm_pbr_build_emit', 'spmm_boo_matmul', 'spmm_pbr_matmul'):
             getattr(L, n).restype = C.c_int

@@ -418,7 +418,8 @@ def boo_to_csr(boo_mat) -> sp.csr_matrix:
 # SpMM
 # ---------------------------------------------------------------------------
 
-def _run_boo(boo_mat, meta, x: torch.Tensor) -> torch.Tensor:
+def _run_boo(boo_mat, meta, x: torch.Tensor, engine: str = 'auto') -> torch.Tensor:
+    cfg = _lib.launch_cfg(engine)
     device = x.device
     with torch.cuda.device(device):
         x3 = x if x.dim() == 3 else x.unsqueeze(0)
@@ -427,8 +428,13 @@ def _run_boo(boo_mat, meta, x: torch.Tensor) -> torch.Tensor:
         y = torch.empty((batch, boo_mat.rows, K), dtype=x.dtype, device=device)
         if y.numel():
             st = boo_mat._dev_struct(meta)
-            rc = _lib.lib().spmm_boo_matmul(C.byref(st), ptr(x3), ptr(y), batch, K, None,
-                                             stream_handle(device))
+            L = _lib.lib()
+            ws_bytes = L.spmm_boo_matmul_workspace_size(C.byref(st), batch, K, C.byref(cfg))
+            ws = torch.empty(ws_bytes, dtype=torch.uint8, device=device) if ws_bytes else None
+            if ws is not None:
+                cfg.workspace, cfg.workspace_bytes = ws.data_ptr(), ws_bytes
+            rc = L.spmm_boo_matmul(C.byref(st), ptr(x3), ptr(y), batch, K, C.byref(cfg),
+                                   stream_handle(device))
             _lib.check(rc, 'boo_matmul')
     return y
 
@@ -445,8 +451,13 @@ def boo_matmul(boo_mat, x: torch.Tensor, threads: int = 256, p: int = 64,
                csr_mode: int = 0, row_seg: Optional[bool] = None,
                launch_mode: str = 'legacy', execution_plan=None,
                features_per_thread: int = 1,
-               nnzflat_impl: Optional[str] = None) -> torch.Tensor:
+               nnzflat_impl: Optional[str] = None, *, engine: str = 'auto') -> torch.Tensor:
     """Y = A @ X (boo.py:230-354).
+
+    ``engine`` (not in the reference) picks the units that multiply the
+    blocks: 'auto' (tensor cores for float32 with K a multiple of 128 and
+    blocks up to 64 x 64, else CUDA cores), 'cuda_cores', or 'tensor_cores'
+    (an error where not applicable).
 
     The launch knobs of the reference's sm_86 kernels (``threads``, ``p``,
     ``csr_mode``, ``features_per_thread``, ``nnzflat_impl``, ``launch_mode``)
@@ -474,7 +485,7 @@ def boo_matmul(boo_mat, x: torch.Tensor, threads: int = 256, p: int = 64,
         require_cuda('boo_matmul')
         device = default_device()
         meta = boo_mat._staged_on(device)
-        y = _to_host(_run_boo(boo_mat, meta, x.to(device, non_blocking=True)), x)
+        y = _to_host(_run_boo(boo_mat, meta, x.to(device, non_blocking=True), engine), x)
         return y.squeeze(0) if x.dim() == 2 else y
 
     meta = boo_mat._gpu_meta
@@ -506,7 +517,7 @@ def boo_matmul(boo_mat, x: torch.Tensor, threads: int = 256, p: int = 64,
             raise ValueError('nnzflat (row_seg=False) supports features_per_thread 1 or 2')
         if nnzflat_impl == 'reference' and features_per_thread != 1:
             raise ValueError("nnzflat_impl='reference' is the FPT=1 kernel; use 'template'")
-    y = _run_boo(boo_mat, meta, x)
+    y = _run_boo(boo_mat, meta, x, engine)
     return y.squeeze(0) if x.dim() == 2 else y
 
 

@@ -18,6 +18,11 @@
 #include "spmm_common.cuh"
 
 namespace spmm {
+
+int boo_matmul_tc(const spmm_boo_dev *A, const float *X, float *Y, int64_t batch, int64_t K, void *ws,
+                  size_t ws_bytes, cudaStream_t s);
+size_t boo_tc_workspace(const spmm_boo_dev *A, int64_t batch, int64_t K);
+
 namespace {
 
 constexpr int kBooThreads = 256;
@@ -330,8 +335,21 @@ int boo_dispatch<double>(const BooParams<double> &p, int64_t n_rg, bool aligned,
 }
 
 template <typename S>
-int boo_matmul_impl(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch, int64_t K,
-                    cudaStream_t s) {
+int boo_matmul_impl(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch, int64_t K, int engine,
+                    const spmm_launch_cfg *cfg, cudaStream_t s) {
+    if constexpr (sizeof(S) == 4) {
+        // AUTO: the tensor-core kernel wins (measured on B200) for blocks up to
+        // 32 x 32 holding on average >= 96 nonzeros (FEM-like, 3.6 vs 4.3 ms
+        // at 786k rows, K = 128); sparser or 64 x 64 blocks stay on CUDA cores.
+        const bool tc_auto = A->max_nr <= 32 && A->max_nc <= 32 && A->nb > 0 && A->nnz_c >= 96 * A->nb;
+        if (engine == SPMM_ENGINE_TENSOR_CORES || (engine == SPMM_ENGINE_AUTO && tc_auto)) {
+            const int rc = boo_matmul_tc(A, (const float *)X, (float *)Y, batch, K, cfg ? cfg->workspace : nullptr,
+                                         cfg ? (size_t)cfg->workspace_bytes : 0, s);
+            if (rc != SPMM_EUNSUPPORTED || engine == SPMM_ENGINE_TENSOR_CORES) return rc;
+        }
+    } else {
+        if (engine == SPMM_ENGINE_TENSOR_CORES) return SPMM_EUNSUPPORTED;
+    }
     BooParams<S> p;
     p.rows = A->rows;
     p.cols = A->cols;
@@ -371,6 +389,8 @@ extern "C" int spmm_boo_matmul(const spmm_boo_dev *A, const void *X, void *Y, in
                                const spmm_launch_cfg *cfg, spmm_stream_t stream) {
     if (!A || batch < 0 || K < 0) return SPMM_EINVAL;
     if (cfg && cfg->version != 1) return SPMM_EINVAL;
+    const int engine = cfg ? cfg->engine : SPMM_ENGINE_AUTO;
+    if (engine < SPMM_ENGINE_AUTO || engine > SPMM_ENGINE_TENSOR_CORES) return SPMM_EINVAL;
     if (A->scalar_type != SPMM_F32 && A->scalar_type != SPMM_F64) return SPMM_EINVAL;
     if (A->nz_order != SPMM_BOO_ROWMAJOR && A->nz_order != SPMM_BOO_COLMAJOR) return SPMM_EINVAL;
     if (A->rows < 0 || A->cols < 0 || A->n_rg < 0 || A->nb < 0 || A->tail_nnz < 0) return SPMM_EINVAL;
@@ -384,6 +404,13 @@ extern "C" int spmm_boo_matmul(const spmm_boo_dev *A, const void *X, void *Y, in
         return SPMM_EINVAL;
     if (A->n_rg == 0) return SPMM_EINVAL;  // rows > 0 need at least one group
     cudaStream_t s = (cudaStream_t)stream;
-    if (A->scalar_type == SPMM_F32) return boo_matmul_impl<float>(A, X, Y, batch, K, s);
-    return boo_matmul_impl<double>(A, X, Y, batch, K, s);
+    if (A->scalar_type == SPMM_F32) return boo_matmul_impl<float>(A, X, Y, batch, K, engine, cfg, s);
+    return boo_matmul_impl<double>(A, X, Y, batch, K, engine, cfg, s);
+}
+
+extern "C" size_t spmm_boo_matmul_workspace_size(const spmm_boo_dev *A, int64_t batch, int64_t K,
+                                                 const spmm_launch_cfg *cfg) {
+    if (!A || batch <= 0 || K <= 0 || A->scalar_type != SPMM_F32) return 0;
+    if (cfg && (cfg->version != 1 || cfg->engine == SPMM_ENGINE_CUDA_CORES)) return 0;
+    return boo_tc_workspace(A, batch, K);
 }

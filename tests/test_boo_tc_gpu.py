@@ -1,0 +1,203 @@
+"""BOO product on the tensor cores (tcgen05 3xTF32) against the oracle.
+
+The tensor-core engine must meet the float32 bar of the CUDA-core engine:
+max|dY| <= 1e-5 * (|A||X|) elementwise, with the reference's semantics for
+non-finite values (a NaN or Inf reaches exactly the rows whose nonzeros use
+it).  Engines are forced through boo_matmul(..., engine=...)."""
+
+import numpy as np
+import pytest
+import scipy.sparse as sp
+import torch
+
+import spmm_b200 as S
+from oracle import oracle as O
+from spmm_b200 import _lib, workloads
+from tests.conftest import TOL, abs_bound, assert_spmm_close
+
+pytestmark = pytest.mark.gpu
+
+POLICIES = ['keep', 'remainder', 'tail_batch']
+
+
+def _oracle_y(boo, xn):
+    d = {f: getattr(boo, f) for f in O.BOO_FIELDS}
+    d.update(rows=boo.rows, cols=boo.cols)
+    return O.boo_matmul(d, xn)
+
+
+def _product(boo_dev, x, engine):
+    y = S.boo_matmul(boo_dev, x, engine=engine)
+    torch.cuda.synchronize()
+    assert _lib.lib().spmm_tc_status(1) == 0
+    return y
+
+
+def _check(mat, boo, x, engine='tensor_cores'):
+    got = _product(boo.to('cuda'), x.cuda(), engine).cpu().numpy()
+    xn = x.numpy()
+    ref = _oracle_y(boo, xn)
+    assert_spmm_close(got, ref, abs_bound(mat.indptr, mat.indices, mat.data, xn), TOL[np.dtype(np.float32)])
+    return got
+
+
+def _labels(n, g, rng, shuffle):
+    lab = np.arange(n) // g
+    return rng.permutation(lab) if shuffle else lab
+
+
+@pytest.mark.parametrize('seed', range(32))
+def test_tc_seeded_sweep(cuda, seed):
+    rng = np.random.default_rng(7000 + seed)
+    rows, cols = int(rng.integers(1, 3000)), int(rng.integers(1, 3000))
+    mat = sp.random(rows, cols, density=float(rng.uniform(0.002, 0.08)), format='csr',
+                    random_state=seed, dtype=np.float64)
+    mat.data = rng.standard_normal(mat.nnz)
+    mat = mat.astype(np.float32)
+    gr, gc = (int(rng.choice([1, 5, 8, 16, 31, 32, 48, 64])) for _ in range(2))
+    rl, cl = _labels(rows, gr, rng, seed % 2 == 1), _labels(cols, gc, rng, seed % 4 == 3)
+    policy = POLICIES[seed % 3]
+    order = ('rowmajor', 'colmajor')[(seed // 3) % 2]
+    boo = S.csr_to_boo(mat, row_labels=rl, col_labels=cl, small_block_policy=policy,
+                       small_block_threshold=int(rng.integers(0, 6)), nz_order=order)
+    k = int(rng.choice([128, 256, 384]))
+    batch = int(rng.integers(1, 3))
+    x = torch.from_numpy(rng.standard_normal((batch, cols, k)).astype(np.float32))
+    y_tc = _check(mat, boo, x, 'tensor_cores')
+    y_cc = _check(mat, boo, x, 'cuda_cores')
+    y_auto = _product(boo.to('cuda'), x.cuda(), 'auto').cpu().numpy()
+    dense = boo.max_nr <= 32 and boo.max_nc <= 32 and boo.compressed_nnz() >= 96 * boo.num_blocks()
+    np.testing.assert_array_equal(y_auto, y_tc if dense else y_cc)   # auto's measured crossover
+
+
+@pytest.mark.parametrize('name,gen,kw,target,k', [
+    ('fem3d', workloads.fem3d, dict(n=10), 32, 128),
+    ('laplacian2d', workloads.laplacian2d, dict(n=70), 32, 256),
+    ('blockdiag64', workloads.blockdiag, dict(n_blocks=24, b=64), 64, 512),
+    ('powerlaw', workloads.powerlaw, dict(n=3000), 32, 128),
+    ('uniform', workloads.uniform, dict(n=4000), 32, 128),
+])
+def test_tc_workload_shapes(cuda, name, gen, kw, target, k):
+    mat = gen(**kw)
+    rows, cols = mat.shape
+    boo = S.csr_to_boo(mat, row_labels=np.arange(rows) // target, col_labels=np.arange(cols) // target)
+    x = torch.from_numpy(np.random.default_rng(5).standard_normal((cols, k)).astype(np.float32))
+    _check(mat, boo, x)
+
+
+def test_tc_deterministic(cuda):
+    mat = workloads.fem3d(n=8)
+    boo = S.csr_to_boo(mat, cluster='identity', target_nr=32, target_nc=32).to('cuda')
+    x = torch.randn(mat.shape[1], 256, generator=torch.Generator().manual_seed(3)).cuda()
+    a = _product(boo, x, 'tensor_cores')
+    b = _product(boo, x, 'tensor_cores')
+    assert torch.equal(a, b)
+
+
+def test_tc_wide_dynamic_range(cuda):
+    rng = np.random.default_rng(11)
+    mat = sp.random(900, 700, density=0.05, format='csr', random_state=4, dtype=np.float64)
+    mat.data = rng.choice([-1, 1], mat.nnz) * np.exp(rng.uniform(-20, 20, mat.nnz))
+    mat = mat.astype(np.float32)
+    boo = S.csr_to_boo(mat, cluster='identity', target_nr=32, target_nc=32)
+    x = rng.choice([-1, 1], (700, 128)) * np.exp(rng.uniform(-25, 25, (700, 128)))
+    _check(mat, boo, torch.from_numpy(x.astype(np.float32)))
+
+
+@pytest.mark.parametrize('policy,threshold', [('remainder', 6), ('tail_batch', 6), ('remainder', 1000)])
+def test_tc_spills_and_empty_groups(cuda, policy, threshold):
+    """Row groups whose blocks all spilled (or that hold no nonzeros at all)
+    get only their remainder / tail entries."""
+    rng = np.random.default_rng(3)
+    dense = rng.standard_normal((640, 512)).astype(np.float32)
+    dense[rng.random(dense.shape) > 0.02] = 0
+    dense[100:164] = 0                      # two empty row groups
+    dense[300:310, :] = 0
+    mat = sp.csr_matrix(dense)
+    boo = S.csr_to_boo(mat, row_labels=np.arange(640) // 32, col_labels=np.arange(512) // 32,
+                       small_block_policy=policy, small_block_threshold=threshold)
+    x = torch.from_numpy(rng.standard_normal((2, 512, 128)).astype(np.float32))
+    if boo.num_blocks() == 0:
+        with pytest.raises(_lib.SpmmError):
+            _product(boo.to('cuda'), x.cuda(), 'tensor_cores')
+        _check(mat, boo, x, 'auto')
+    else:
+        _check(mat, boo, x)
+
+
+def _assert_same_nonfinite(got, ref, bound):
+    assert np.array_equal(np.isnan(got), np.isnan(ref))
+    assert np.array_equal(np.isposinf(got), np.isposinf(ref))
+    assert np.array_equal(np.isneginf(got), np.isneginf(ref))
+    fin = np.isfinite(ref)
+    assert_spmm_close(np.where(fin, got, 0), np.where(fin, ref, 0), np.where(fin, bound, 0),
+                      TOL[np.dtype(np.float32)])
+
+
+def test_tc_nonfinite_values(cuda):
+    """NaN / Inf in A or X propagate exactly as in the reference's CPU path:
+    0 * Inf never reaches rows that do not use the value."""
+    rng = np.random.default_rng(21)
+    mat = sp.random(512, 384, density=0.06, format='csr', random_state=9, dtype=np.float32)
+    mat.data[:] = rng.standard_normal(mat.nnz)
+    mat.data[[3, 70, 500]] = [np.inf, -np.inf, np.nan]
+    boo = S.csr_to_boo(mat, cluster='identity', target_nr=32, target_nc=32)
+    x = rng.standard_normal((384, 128)).astype(np.float32)
+    x[5, 7] = np.inf
+    x[200, :] = -np.inf
+    x[301, 64:96] = np.nan
+    got = _product(boo.to('cuda'), torch.from_numpy(x).cuda(), 'tensor_cores').cpu().numpy()
+    ref = _oracle_y(boo, x)
+    with np.errstate(invalid='ignore'):
+        bound = abs_bound(mat.indptr, mat.indices, np.nan_to_num(mat.data, posinf=0, neginf=0),
+                          np.nan_to_num(x, posinf=0, neginf=0))
+    assert np.isnan(ref).any() and np.isinf(ref).any() and np.isfinite(ref).any()
+    _assert_same_nonfinite(got, ref, bound)
+
+
+def test_tc_not_applicable(cuda):
+    mat = workloads.laplacian2d(n=20)
+    boo32 = S.csr_to_boo(mat, cluster='identity', target_nr=32, target_nc=32)
+    x = torch.randn(mat.shape[1], 64).cuda()
+    with pytest.raises(_lib.SpmmError):             # K not a multiple of 128
+        S.boo_matmul(boo32.to('cuda'), x, engine='tensor_cores')
+    y = S.boo_matmul(boo32.to('cuda'), x, engine='auto')     # falls back to CUDA cores
+    assert y.shape == (mat.shape[0], 64)
+    boo64 = S.csr_to_boo(mat.astype(np.float64), cluster='identity', target_nr=32, target_nc=32)
+    with pytest.raises(_lib.SpmmError):             # float64 has no tensor-core path
+        S.boo_matmul(boo64.to('cuda'), x.double().repeat(1, 2), engine='tensor_cores')
+    big = S.csr_to_boo(mat, row_labels=np.arange(mat.shape[0]) // 100, col_labels=np.arange(mat.shape[1]) // 100)
+    with pytest.raises(_lib.SpmmError):             # blocks larger than 64 x 64
+        S.boo_matmul(big.to('cuda'), torch.randn(mat.shape[1], 128).cuda(), engine='tensor_cores')
+    with pytest.raises(ValueError):
+        S.boo_matmul(boo32.to('cuda'), x, engine='tensor')
+
+
+def test_tc_abi_workspace_optional(cuda):
+    """Through the C ABI: no workspace (scratch from the stream-ordered
+    allocator) and a caller workspace give the same bits."""
+    import ctypes as C
+    from spmm_b200._device import stream_handle
+    mat = workloads.fem3d(n=8)
+    boo = S.csr_to_boo(mat, cluster='identity', target_nr=32, target_nc=32).to('cuda')
+    st = boo._dev_struct(boo._gpu_meta)
+    x = torch.randn(mat.shape[1], 256, generator=torch.Generator().manual_seed(9)).cuda()
+    L = _lib.lib()
+    out = []
+    for with_ws in (False, True):
+        cfg = _lib.launch_cfg('tensor_cores')
+        ws_bytes = L.spmm_boo_matmul_workspace_size(C.byref(st), 1, 256, C.byref(cfg))
+        assert ws_bytes == boo.num_col_groups() * 32 * 256 * 4
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device='cuda') if with_ws else None
+        if ws is not None:
+            cfg.workspace, cfg.workspace_bytes = ws.data_ptr(), ws_bytes
+        y = torch.empty(mat.shape[0], 256, device='cuda')
+        rc = L.spmm_boo_matmul(C.byref(st), C.c_void_p(x.data_ptr()), C.c_void_p(y.data_ptr()), 1, 256,
+                               C.byref(cfg), stream_handle(x.device))
+        assert rc == 0
+        torch.cuda.synchronize()
+        out.append(y)
+    assert L.spmm_tc_status(1) == 0
+    assert torch.equal(out[0], out[1])
+    cc = _lib.launch_cfg('cuda_cores')
+    assert L.spmm_boo_matmul_workspace_size(C.byref(st), 1, 256, C.byref(cc)) == 0
