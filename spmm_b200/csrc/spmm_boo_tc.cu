@@ -67,6 +67,14 @@ constexpr int kDescRing = 64;        // block descriptors in flight (metadata wa
 // epilogue -> MMA -> loader -> metadata-warp wait cycle closes.
 constexpr int kChunkRing = 32;
 constexpr int kATiles = 3;           // A tiles per loader warpgroup
+constexpr int kMaxChunkRgs = 8;      // row groups per chunk
+// Blocks with at least kDenseNnz nonzeros go through the tensor cores; the
+// others (and the CSR remainder) are summed on CUDA cores by the epilogue.  An
+// M = 128 MMA costs ~50 cycles whatever N is, so a 32 x 32 block needs a few
+// dozen nonzeros before 3 MMAs per 8 used columns beat per-nonzero FMAs.
+constexpr int kDenseNnz = 48;
+constexpr int kListCap = 1024;       // epilogue: staged (row, column, value) entries per pass
+constexpr int kSegs = 32;            // epilogue: segments (sparse blocks, remainder rows) per pass
 constexpr int kNzPre = 4;            // nonzeros per loader thread fetched ahead
 constexpr long long kWaitCycles = 1ll << 32;  // ~2 s at 2 GHz
 
@@ -77,6 +85,7 @@ enum : uint32_t { kFirst = 1, kLast = 2, kEnd = 4, kSpecial = 8 };
 
 struct TcParams {
     int64_t rows, cols, K, nb, n_rg, rem_nnz, tail_nnz;
+    int32_t dense_nnz;   // blocks with at least this many nonzeros use the tensor cores
     int64_t n_chunks, n_ft, n_tasks;
     int32_t chunk_rgs;
     const int32_t *row_grp_ptr, *row_ids, *col_grp_ptr, *col_ids;
@@ -101,7 +110,25 @@ struct BlockDesc {
 
 struct ChunkInfo {
     int32_t task, rg0, rg1, end;
-    uint32_t mask;  // bit i: row group rg0 + i has blocks
+    uint32_t mask;                     // bit i: row group rg0 + i has tensor-core blocks
+    int32_t bstart[kMaxChunkRgs + 1];  // first block of each row group
+    uint8_t ndense[kMaxChunkRgs];      // tensor-core blocks of each row group
+};
+
+// Epilogue scratch: the row group's CUDA-core partial sums, one copy per
+// summing warp (warp w adds entries w, w + P, ... for all 128 features, 4 per
+// lane), and one pass of staged entries.
+template <int NR>
+struct alignas(16) EpiSmem {
+    static constexpr int P = NR <= 32 ? 4 : 2;   // summing warps / partial copies
+    float ys[P][NR][kFeat];
+    int32_t lcol[kListCap];
+    float lval[kListCap];
+    uint8_t lrow[kListCap];
+    int32_t soff[kSegs + 1];   // prefix of the segments' entry counts
+    int32_t sbase[kSegs];      // first entry (block nonzero or remainder index)
+    int32_t scb[kSegs];        // block: first column of its group in col_ids; row segment: -1
+    uint32_t saux[kSegs];      // block: index shift; row segment: local row
 };
 
 struct SlotMeta {
@@ -131,7 +158,13 @@ struct TcShape {
     static constexpr int kTileBytes = NR * PW * 4;               // one of hi / lo
     static constexpr int kTilesBytes = NL * kATiles * 2 * kTileBytes;
     static constexpr int kThreads = 32 * (8 + 4 * NL);
-    static constexpr int kSmem = 1024 + kTilesBytes + (int)sizeof(TcCtl<PW, NL>);
+    // dynamic shared memory: A tiles (1024-aligned base), epilogue scratch,
+    // control block (mbarriers: 8-byte alignment), each offset 128-aligned
+    static constexpr int kEpiOff = kTilesBytes;
+    static constexpr int kCtlOff = (kEpiOff + (int)sizeof(EpiSmem<NR>) + 127) & ~127;
+    static constexpr int kSmem = 1024 + kCtlOff + (int)sizeof(TcCtl<PW, NL>);
+    static_assert(kTilesBytes % 1024 == 0 && kCtlOff % 128 == 0, "shared-memory carve-out alignment");
+    static_assert(kSmem <= 227 * 1024, "shared memory per CTA");
     static constexpr uint32_t kTmemCols = 512;
     static_assert(2 * NR + NL * 2 * PW <= (int)kTmemCols, "tensor memory budget");
     static_assert(NR % 16 == 0 && NR >= 16 && NR <= 256, "MMA N for M = 128");
@@ -259,59 +292,96 @@ __device__ __forceinline__ int64_t warp_lower_bound(const int32_t *a, int64_t n,
 template <int NR, int PW, int NL>
 __device__ void meta_role(const TcParams &p, TcCtl<PW, NL> &ctl, int lane) {
     volatile int *abort = &ctl.abort;
-    int64_t q = 0;     // descriptors issued
+    const unsigned lt_mask = (1u << lane) - 1u;
+    int64_t q = 0;     // descriptors issued (tensor-core blocks)
     int64_t cidx = 0;  // chunks issued
     bool ok = true;
     for (int64_t task = blockIdx.x; task < p.n_tasks && ok; task += gridDim.x) {
         const int64_t chunk = (task / p.n_ft) % p.n_chunks;
         const int64_t rg0 = chunk * p.chunk_rgs;
         const int64_t rg1 = rg0 + p.chunk_rgs < p.n_rg ? rg0 + p.chunk_rgs : p.n_rg;
+        const int nrg = (int)(rg1 - rg0);
         const int64_t bl = warp_lower_bound(p.blk_row_grp, p.nb, rg0, lane);
-        // Row groups of the chunk that own blocks; the epilogue gets the chunk
-        // before its descriptors so it can drain accumulators while they flow.
-        uint32_t mask = 0;
+        // Pass 1: blocks and tensor-core blocks per row group of the chunk.
+        // The epilogue gets the chunk before its descriptors, so it can drain
+        // accumulators (and sum the CUDA-core part) while they flow.
+        int call[kMaxChunkRgs], cden[kMaxChunkRgs];
+#pragma unroll
+        for (int k = 0; k < kMaxChunkRgs; ++k) call[k] = cden[k] = 0;
         for (int64_t b0 = bl;; b0 += 32) {
             const int64_t b = b0 + lane;
             const int64_t rgb = b < p.nb ? (int64_t)__ldg(p.blk_row_grp + b) : INT64_MAX;
             const bool valid = rgb < rg1;
-            if (valid) mask |= 1u << (uint32_t)(rgb - rg0);
+            const bool dense =
+                valid && __ldg(p.blk_nz_ptr + b + 1) - __ldg(p.blk_nz_ptr + b) >= p.dense_nnz;
+#pragma unroll
+            for (int k = 0; k < kMaxChunkRgs; ++k) {
+                call[k] += __popc(__ballot_sync(kFullMask, valid && rgb == rg0 + k));
+                cden[k] += __popc(__ballot_sync(kFullMask, dense && rgb == rg0 + k));
+            }
             if (__ballot_sync(kFullMask, valid) != kFullMask) break;
         }
+        ChunkInfo ci{};
+        ci.task = (int32_t)task;
+        ci.rg0 = (int32_t)rg0;
+        ci.rg1 = (int32_t)rg1;
+        ci.bstart[0] = (int32_t)bl;
 #pragma unroll
-        for (int o = 16; o; o >>= 1) mask |= __shfl_xor_sync(kFullMask, mask, o);
+        for (int k = 0; k < kMaxChunkRgs; ++k) {
+            ci.bstart[k + 1] = ci.bstart[k] + call[k];
+            ci.ndense[k] = (uint8_t)(cden[k] < 255 ? cden[k] : 255);
+            if (cden[k]) ci.mask |= 1u << k;
+        }
         if (lane == 0) {
             const int s = (int)(cidx % kChunkRing);
             ok = wait_phase(&ctl.chunkempty[s], (uint32_t)((cidx / kChunkRing) & 1) ^ 1u, abort, 2);
             if (ok) {
-                ctl.chunk[s] = ChunkInfo{(int32_t)task, (int32_t)rg0, (int32_t)rg1, 0, mask};
+                ctl.chunk[s] = ci;
                 mbar_arrive(&ctl.chunkfull[s]);
             }
         }
         ok = __shfl_sync(kFullMask, ok, 0);
         ++cidx;
         if (!ok) break;
-        int64_t b0 = bl;
-        for (;;) {
+        // Pass 2: a descriptor per tensor-core block, in block order, flagged
+        // first / last among its row group's tensor-core blocks.
+        int posted[kMaxChunkRgs];
+#pragma unroll
+        for (int k = 0; k < kMaxChunkRgs; ++k) posted[k] = 0;
+        const int64_t bend = ci.bstart[nrg < kMaxChunkRgs ? nrg : kMaxChunkRgs];
+        for (int64_t b0 = bl; b0 < bend && ok; b0 += 32) {
             const int64_t b = b0 + lane;
-            const int64_t rgb = b < p.nb ? (int64_t)__ldg(p.blk_row_grp + b) : INT64_MAX;
-            const bool valid = rgb < rg1;
+            const bool valid = b < bend;
             BlockDesc d{};
+            bool dense = false;
+            int k = 0;
             if (valid) {
-                const int32_t cg = __ldg(p.blk_col_grp + b);
                 d.k0 = __ldg(p.blk_nz_ptr + b);
                 d.k1 = __ldg(p.blk_nz_ptr + b + 1);
+                dense = d.k1 - d.k0 >= p.dense_nnz;
+                d.rg = __ldg(p.blk_row_grp + b);
+                k = (int)(d.rg - rg0);
+                d.cg = __ldg(p.blk_col_grp + b);
                 d.shift = __ldg(p.blk_shift + b);
-                const int64_t rprev = b > 0 ? (int64_t)__ldg(p.blk_row_grp + b - 1) : -1;
-                const int64_t rnext = b + 1 < p.nb ? (int64_t)__ldg(p.blk_row_grp + b + 1) : INT64_MAX;
-                d.cg = cg;
-                d.rg = (int32_t)rgb;
                 d.task = (int32_t)task;
-                d.flags = (rprev != rgb ? kFirst : 0u) | (rnext != rgb ? kLast : 0u);
             }
-            const int n = __popc(__ballot_sync(kFullMask, valid));
+            int before = 0, mine_posted = 0, mine_total = 0;
+#pragma unroll
+            for (int kk = 0; kk < kMaxChunkRgs; ++kk) {
+                const unsigned m = __ballot_sync(kFullMask, dense && k == kk);
+                if (k == kk) {
+                    before = __popc(m & lt_mask);
+                    mine_posted = posted[kk];
+                    mine_total = cden[kk];
+                }
+                posted[kk] += __popc(m);
+            }
+            const unsigned dm = __ballot_sync(kFullMask, dense);
             bool w = true;
-            if (valid) {
-                const int64_t qq = q + lane;
+            if (dense) {
+                d.flags = (mine_posted + before == 0 ? kFirst : 0u) |
+                          (mine_posted + before + 1 == mine_total ? kLast : 0u);
+                const int64_t qq = q + __popc(dm & lt_mask);
                 const int s = (int)(qq % kDescRing);
                 w = wait_phase(&ctl.descempty[s], (uint32_t)((qq / kDescRing) & 1) ^ 1u, abort, 1);
                 if (w) {
@@ -320,9 +390,7 @@ __device__ void meta_role(const TcParams &p, TcCtl<PW, NL> &ctl, int lane) {
                 }
             }
             ok = __all_sync(kFullMask, w);
-            q += n;
-            if (!ok || n < 32) break;
-            b0 += 32;
+            q += __popc(dm);
         }
     }
     if (!ok) return;
@@ -342,7 +410,9 @@ __device__ void meta_role(const TcParams &p, TcCtl<PW, NL> &ctl, int lane) {
     if (lane == 0) {
         const int s = (int)(cidx % kChunkRing);
         if (wait_phase(&ctl.chunkempty[s], (uint32_t)((cidx / kChunkRing) & 1) ^ 1u, abort, 2)) {
-            ctl.chunk[s] = ChunkInfo{0, 0, 0, 1, 0};
+            ChunkInfo ci{};
+            ci.end = 1;
+            ctl.chunk[s] = ci;
             mbar_arrive(&ctl.chunkfull[s]);
         }
     }
@@ -584,68 +654,175 @@ __device__ void mma_role(TcCtl<PW, NL> &ctl, uint32_t tmem) {
     wait_phase(&ctl.fin, 0u, abort, 7);
 }
 
-// Contributions that are not in the tensor-memory accumulator, added to the
-// Y rows of group rg after their first store, in the reference CPU path's
-// order (boo_matrix.cpp:336-396): the block products left out for a
-// non-finite operand (`special`), the CSR remainder, the COO tail.  Rolled
-// loops (no per-row unrolling): the hot epilogue stays small enough for the
-// instruction cache.  Each thread re-reads only the Y elements it stored.
-__device__ __forceinline__ void add_rest(const TcParams &p, int32_t rg, int32_t rbase, int32_t nr, bool special,
-                                      const float *xb, float *yb) {
-    if (special) {
-        int64_t lo = 0, hi = p.nb;
-        while (lo < hi) {
-            const int64_t mid = (lo + hi) >> 1;
-            if (__ldg(p.blk_row_grp + mid) < rg) lo = mid + 1; else hi = mid;
+// CUDA-core part of row group rg, summed into e.ys (thread et owns feature
+// column et): the entries of its blocks with fewer than dense_nnz nonzeros,
+// then its rows' CSR remainder (the reference's remainder kernel,
+// boo_kernel.cu:905-937).  Segments (one per block or row) are listed by warp
+// 0, their entries staged as (local row, column, value) by all 128 threads,
+// then each thread sums them for its feature with 16 X loads in flight.
+template <int NR>
+__device__ __forceinline__ void epi_cuda_part(const TcParams &p, EpiSmem<NR> &e, int32_t bs, int32_t be,
+                                              int32_t rbase, int32_t nr, const float *xb, int et) {
+    const int nblk = be - bs;
+    const int nseg = nblk + (p.rem_nnz ? nr : 0);
+    for (int s0 = 0; s0 < nseg; s0 += kSegs) {
+        if (et < 32) {
+            const int sidx = s0 + et;
+            int cnt = 0, base = 0, cb = -1;
+            uint32_t aux = 0;
+            if (sidx < nblk) {
+                const int64_t b = bs + sidx;
+                const int32_t k0 = __ldg(p.blk_nz_ptr + b), k1 = __ldg(p.blk_nz_ptr + b + 1);
+                if (k1 - k0 < p.dense_nnz) {
+                    cnt = k1 - k0;
+                    base = k0;
+                    cb = __ldg(p.col_grp_ptr + __ldg(p.blk_col_grp + b));
+                    aux = __ldg(p.blk_shift + b);
+                }
+            } else if (sidx < nseg) {
+                const int r = sidx - nblk;
+                const int32_t row = __ldg(p.row_ids + rbase + r);
+                base = __ldg(p.rem_indptr + row);
+                cnt = __ldg(p.rem_indptr + row + 1) - base;
+                aux = (uint32_t)r;
+            }
+            int incl = cnt;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int n = __shfl_up_sync(kFullMask, incl, o);
+                if (et >= o) incl += n;
+            }
+            e.soff[et + 1] = incl;
+            if (et == 0) e.soff[0] = 0;
+            e.sbase[et] = base;
+            e.scb[et] = cb;
+            e.saux[et] = aux;
         }
-        for (int64_t b = lo; b < p.nb && __ldg(p.blk_row_grp + b) == rg; ++b) {
-            const uint32_t shift = __ldg(p.blk_shift + b), cm = (1u << shift) - 1u;
-            const int32_t cbase = __ldg(p.col_grp_ptr + __ldg(p.blk_col_grp + b));
-            const int32_t k1 = __ldg(p.blk_nz_ptr + b + 1);
-            for (int32_t k = __ldg(p.blk_nz_ptr + b); k < k1; ++k) {
-                const uint32_t idx = __ldg(p.nz_idx + k);
-                const int32_t r = (int32_t)(idx >> shift);
-                const float a = __ldg(p.nz_val + k);
-                const float x = __ldg(xb + (int64_t)__ldg(p.col_ids + cbase + (int32_t)(idx & cm)) * p.K);
-                if (r < nr && (!finite(a) || !finite(x))) {
-                    float *y = yb + (int64_t)__ldg(p.row_ids + rbase + r) * p.K;
-                    *y = fmaf(a, x, *y);
+        named_bar_sync(1, 128);
+        const int total = e.soff[kSegs];
+        for (int g0 = 0; g0 < total; g0 += kListCap) {
+            const int ne = total - g0 < kListCap ? total - g0 : kListCap;
+            for (int i = et; i < ne; i += 128) {
+                const int g = g0 + i;
+                int lo = 0, hi = kSegs - 1;
+                while (lo < hi) {
+                    const int mid = (lo + hi + 1) >> 1;
+                    if (e.soff[mid] <= g) lo = mid; else hi = mid - 1;
+                }
+                const int kidx = e.sbase[lo] + (g - e.soff[lo]);
+                uint32_t r;
+                int32_t col;
+                float v;
+                if (e.scb[lo] >= 0) {
+                    const uint32_t idx = __ldg(p.nz_idx + kidx), sh = e.saux[lo];
+                    r = idx >> sh;
+                    col = __ldg(p.col_ids + e.scb[lo] + (int32_t)(idx & ((1u << sh) - 1u)));
+                    v = __ldg(p.nz_val + kidx);
+                } else {
+                    r = e.saux[lo];
+                    col = __ldg(p.rem_col + kidx);
+                    v = __ldg(p.rem_val + kidx);
+                }
+                e.lrow[i] = (uint8_t)(r < (uint32_t)NR ? r : 255u);
+                e.lcol[i] = col;
+                e.lval[i] = v;
+            }
+            named_bar_sync(1, 128);
+            constexpr int P = EpiSmem<NR>::P;
+            const int w = et >> 5, l4 = (et & 31) * 4;
+            if (w < P) {
+                // warp w: entries w, w + P, ...; lane: features 4l..4l+3
+                const float4 *x4 = reinterpret_cast<const float4 *>(xb - et + l4);
+                const int64_t k4 = p.K / 4;
+                constexpr int U = 8;
+                int i = w;
+                for (; i + (U - 1) * P < ne; i += U * P) {
+                    float4 x[U];
+#pragma unroll
+                    for (int u = 0; u < U; ++u) x[u] = __ldg(x4 + (int64_t)e.lcol[i + u * P] * k4);
+#pragma unroll
+                    for (int u = 0; u < U; ++u) {
+                        const uint32_t r = e.lrow[i + u * P];
+                        const float v = e.lval[i + u * P];
+                        if (r < (uint32_t)NR) {
+                            float4 *y = reinterpret_cast<float4 *>(&e.ys[w][r][l4]);
+                            float4 t = *y;
+                            t.x = fmaf(v, x[u].x, t.x);
+                            t.y = fmaf(v, x[u].y, t.y);
+                            t.z = fmaf(v, x[u].z, t.z);
+                            t.w = fmaf(v, x[u].w, t.w);
+                            *y = t;
+                        }
+                    }
+                }
+                for (; i < ne; i += P) {
+                    const float4 x = __ldg(x4 + (int64_t)e.lcol[i] * k4);
+                    const uint32_t r = e.lrow[i];
+                    const float v = e.lval[i];
+                    if (r < (uint32_t)NR) {
+                        float4 *y = reinterpret_cast<float4 *>(&e.ys[w][r][l4]);
+                        float4 t = *y;
+                        t.x = fmaf(v, x.x, t.x);
+                        t.y = fmaf(v, x.y, t.y);
+                        t.z = fmaf(v, x.z, t.z);
+                        t.w = fmaf(v, x.w, t.w);
+                        *y = t;
+                    }
                 }
             }
+            named_bar_sync(1, 128);  // the list is reused by the next pass
         }
-    }
-    if (!p.rem_nnz && !p.tail_nnz) return;
-    for (int32_t r = 0; r < nr; ++r) {
-        const int32_t row = __ldg(p.row_ids + rbase + r);
-        float *y = yb + (int64_t)row * p.K;
-        if (p.rem_nnz) {
-            const int32_t e1 = __ldg(p.rem_indptr + row + 1);
-            int32_t e = __ldg(p.rem_indptr + row);
-            if (e < e1) {
-                float a = *y;
-                for (; e < e1; ++e)
-                    a = fmaf(__ldg(p.rem_val + e), __ldg(xb + (int64_t)__ldg(p.rem_col + e) * p.K), a);
-                *y = a;
-            }
-        }
-        if (p.tail_nnz) {
-            int64_t lo = 0, hi = p.tail_nnz;
-            while (lo < hi) {
-                const int64_t mid = (lo + hi) >> 1;
-                if (__ldg(p.tail_row + mid) < row) lo = mid + 1; else hi = mid;
-            }
-            if (lo < p.tail_nnz && __ldg(p.tail_row + lo) == row) {
-                float a = *y;
-                for (int64_t e = lo; e < p.tail_nnz && __ldg(p.tail_row + e) == row; ++e)
-                    a = fmaf(__ldg(p.tail_val + e), __ldg(xb + (int64_t)__ldg(p.tail_col + e) * p.K), a);
-                *y = a;
-            }
-        }
+        named_bar_sync(1, 128);      // the segment table is rewritten next
     }
 }
 
+// Rare contributions, summed into e.ys by each thread for its feature: the
+// tensor-core block products left out for a non-finite operand (`special`),
+// and the COO tail (the reference's tail kernel, pbr_kernel.cu:976-1049).
+// Rolled loops, so the hot epilogue stays small for the instruction cache.
+template <int NR>
+__device__ __forceinline__ void epi_rare(const TcParams &p, EpiSmem<NR> &e, int32_t bs, int32_t be, int32_t rbase,
+                                         int32_t nr, bool special, const float *xb, int et) {
+    if (special) {
+        for (int64_t b = bs; b < be; ++b) {
+            const int32_t k0 = __ldg(p.blk_nz_ptr + b), k1 = __ldg(p.blk_nz_ptr + b + 1);
+            if (k1 - k0 < p.dense_nnz) continue;
+            const uint32_t shift = __ldg(p.blk_shift + b), cm = (1u << shift) - 1u;
+            const int32_t cbase = __ldg(p.col_grp_ptr + __ldg(p.blk_col_grp + b));
+            for (int32_t k = k0; k < k1; ++k) {
+                const uint32_t idx = __ldg(p.nz_idx + k);
+                const uint32_t r = idx >> shift;
+                const float a = __ldg(p.nz_val + k);
+                const float x = __ldg(xb + (int64_t)__ldg(p.col_ids + cbase + (int32_t)(idx & cm)) * p.K);
+                if (r < (uint32_t)NR && (!finite(a) || !finite(x))) e.ys[0][r][et] = fmaf(a, x, e.ys[0][r][et]);
+            }
+        }
+    }
+    if (!p.tail_nnz) return;
+    for (int32_t r = 0; r < nr && r < NR; ++r) {
+        const int32_t row = __ldg(p.row_ids + rbase + r);
+        int64_t lo = 0, hi = p.tail_nnz;
+        while (lo < hi) {
+            const int64_t mid = (lo + hi) >> 1;
+            if (__ldg(p.tail_row + mid) < row) lo = mid + 1; else hi = mid;
+        }
+        float a = e.ys[0][r][et];
+        for (int64_t k = lo; k < p.tail_nnz && __ldg(p.tail_row + k) == row; ++k)
+            a = fmaf(__ldg(p.tail_val + k), __ldg(xb + (int64_t)__ldg(p.tail_col + k) * p.K), a);
+        e.ys[0][r][et] = a;
+    }
+}
+
+template <int NR>
+__device__ __forceinline__ void zero_ys(EpiSmem<NR> &e, int et) {
+    float4 *z = reinterpret_cast<float4 *>(&e.ys[0][0][0]);
+    constexpr int n4 = EpiSmem<NR>::P * NR * kFeat / 4;
+#pragma unroll 4
+    for (int i = et; i < n4; i += 128) z[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
 template <int NR, int PW, int NL>
-__device__ void epilogue_role(const TcParams &p, TcCtl<PW, NL> &ctl, uint32_t tmem, int et) {
+__device__ void epilogue_role(const TcParams &p, TcCtl<PW, NL> &ctl, EpiSmem<NR> &e, uint32_t tmem, int et) {
     volatile int *abort = &ctl.abort;
     const uint32_t lane_addr = (uint32_t)((et & ~31) << 16);
     uint32_t dbuf = 0, du[2] = {0u, 0u};
@@ -662,6 +839,8 @@ __device__ void epilogue_role(const TcParams &p, TcCtl<PW, NL> &ctl, uint32_t tm
         const float *xb = p.X + bt * p.cols * p.K + ft * kFeat + et;
         float *yb = p.Y + bt * p.rows * p.K + ft * kFeat + et;
         for (int32_t rg = ci.rg0; rg < ci.rg1; ++rg) {
+            const int k = rg - ci.rg0;
+            const int32_t bs = ci.bstart[k], be = ci.bstart[k + 1];
             // row ids, one load round: lane l of every warp fetches rows
             // l, l + 32, ... and shuffles spread them
             constexpr int RH = (NR + 31) / 32;
@@ -673,11 +852,19 @@ __device__ void epilogue_role(const TcParams &p, TcCtl<PW, NL> &ctl, uint32_t tm
                 const int r = h * 32 + (et & 31);
                 myrow[h] = r < nr && r < NR ? __ldg(p.row_ids + rbase + r) : -1;
             }
+            // CUDA-core part first: it overlaps the MMAs of this row group
+            const bool cuda_part = be - bs > (int32_t)ci.ndense[k] || p.rem_nnz;
+            bool in_ys = cuda_part || p.tail_nnz;
+            if (in_ys) {
+                zero_ys<NR>(e, et);
+                named_bar_sync(1, 128);
+                if (cuda_part) epi_cuda_part<NR>(p, e, bs, be, rbase, nr, xb, et);
+            }
             float acc[NR];
 #pragma unroll
             for (int r = 0; r < NR; ++r) acc[r] = 0.f;
             bool special = false;
-            if ((ci.mask >> (uint32_t)(rg - ci.rg0)) & 1u) {
+            if ((ci.mask >> (uint32_t)k) & 1u) {
                 w = true;
                 if (et == 0) w = wait_phase(&ctl.dfull[dbuf], du[dbuf] & 1u, abort, 9);
                 if (!bar_and(1, 128, w)) return;
@@ -689,7 +876,7 @@ __device__ void epilogue_role(const TcParams &p, TcCtl<PW, NL> &ctl, uint32_t tm
                         tmem_ld16(tmem + dbuf * NR + lane_addr + h * 16, v);
                         tmem_wait_ld();
 #pragma unroll
-                        for (int e = 0; e < 16; ++e) acc[h * 16 + e] = __uint_as_float(v[e]);
+                        for (int q = 0; q < 16; ++q) acc[h * 16 + q] = __uint_as_float(v[q]);
                     }
                 }
                 special = ctl.dspecial[dbuf] != 0u;
@@ -698,17 +885,30 @@ __device__ void epilogue_role(const TcParams &p, TcCtl<PW, NL> &ctl, uint32_t tm
                 ++du[dbuf];
                 dbuf ^= 1u;
             }
+            if (special || p.tail_nnz) {
+                if (!in_ys) {
+                    zero_ys<NR>(e, et);
+                    named_bar_sync(1, 128);
+                    in_ys = true;
+                }
+                epi_rare<NR>(p, e, bs, be, rbase, nr, special, xb, et);
+            }
+            if (in_ys) named_bar_sync(1, 128);   // partials written by other warps
 #pragma unroll
             for (int r = 0; r < NR; ++r) {
                 const int32_t row = __shfl_sync(kFullMask, myrow[r / 32], r % 32);
                 if (row >= 0) {
-                    if (special || p.rem_nnz || p.tail_nnz)
-                        yb[(int64_t)row * p.K] = acc[r];   // re-read by add_rest
-                    else
-                        __stcs(yb + (int64_t)row * p.K, acc[r]);
+                    float y = acc[r];
+                    if (in_ys) {
+                        float c = e.ys[0][r][et];
+#pragma unroll
+                        for (int q = 1; q < EpiSmem<NR>::P; ++q) c += e.ys[q][r][et];
+                        y = c + y;
+                    }
+                    __stcs(yb + (int64_t)row * p.K, y);
                 }
             }
-            if (special || p.rem_nnz || p.tail_nnz) add_rest(p, rg, rbase, nr < NR ? nr : NR, special, xb, yb);
+            if (in_ys) named_bar_sync(1, 128);   // partials are zeroed for the next group
         }
     }
 }
@@ -718,7 +918,8 @@ __global__ void __launch_bounds__(TcShape<NR, PW, NL>::kThreads, 1) boo_tc_kerne
     using Shape = TcShape<NR, PW, NL>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *tiles = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    TcCtl<PW, NL> &ctl = *reinterpret_cast<TcCtl<PW, NL> *>(tiles + Shape::kTilesBytes);
+    EpiSmem<NR> &epi = *reinterpret_cast<EpiSmem<NR> *>(tiles + Shape::kEpiOff);
+    TcCtl<PW, NL> &ctl = *reinterpret_cast<TcCtl<PW, NL> *>(tiles + Shape::kCtlOff);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     if (tid == 0) {
@@ -754,7 +955,7 @@ __global__ void __launch_bounds__(TcShape<NR, PW, NL>::kThreads, 1) boo_tc_kerne
     } else if (warp == 1) {
         meta_role<NR, PW, NL>(p, ctl, lane);
     } else if (warp >= 4 && warp < 8) {
-        epilogue_role<NR, PW, NL>(p, ctl, tmem, tid - 128);
+        epilogue_role<NR, PW, NL>(p, ctl, epi, tmem, tid - 128);
     } else if (warp >= 8) {
         loader_role<NR, PW, NL>(p, ctl, tiles, tmem, (warp - 8) >> 2, tid - 256 - ((warp - 8) >> 2) * 128);
     }
@@ -870,6 +1071,7 @@ size_t boo_tc_workspace(const spmm_boo_dev *A, int64_t batch, int64_t K) {
 int boo_matmul_tc(const spmm_boo_dev *A, const float *X, float *Y, int64_t batch, int64_t K, void *ws,
                   size_t ws_bytes, cudaStream_t s) {
     if (!tc_applicable(A, K)) return SPMM_EUNSUPPORTED;
+    if ((uintptr_t)X & 15) return SPMM_EUNSUPPORTED;  // 16-byte X loads
     if (!A->col_grp_ptr || !A->col_ids) return SPMM_EINVAL;
     TcParams p{};
     p.rows = A->rows;
@@ -898,8 +1100,9 @@ int boo_matmul_tc(const spmm_boo_dev *A, const float *X, float *Y, int64_t batch
     p.X = X;
     p.Y = Y;
     p.n_cg = A->n_cg;
+    p.dense_nnz = kDenseNnz;
     if (A->max_nr <= 32 && A->max_nc <= 32) return launch_tc<32, 32, 4>(p, batch, ws, ws_bytes, s);
-    return launch_tc<64, 64, 2>(p, batch, ws, ws_bytes, s);
+    return launch_tc<64, 64, 1>(p, batch, ws, ws_bytes, s);
 }
 
 }  // namespace spmm
