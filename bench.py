@@ -9,10 +9,15 @@ larger than the 126 MB L2, so no flush is needed between steps).
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
                   [--config c2_fem3d] [--format boo|pbr]
 
-Multi-GPU (torchrun, one process per GPU): the feature columns are split --
-every rank holds the replicated A and its own 128-column slab of X / Y, so the
-timed region has no collective (weak scaling: total K = N * 128).  The time is
-the max over ranks of the device-measured duration.
+Multi-GPU (torchrun, one process per GPU), two partitionings:
+  --split features (default): A is built once on rank 0 and broadcast over
+    NCCL (outside timing); every rank multiplies its own 128-column slab of X
+    / Y, so the timed region has no collective (weak scaling: total K = N*128).
+  --split rows: row groups partitioned by nonzero balance; every rank builds
+    the format of its own rows; X is broadcast once (timed separately, in
+    `x_broadcast_ms`); Y shards stay local.  Weak scaling (rows = N * rows of
+    the config) for generators with a linear size, else strong scaling.
+The time is the max over ranks of the device-measured duration.
 
 ``--impl reference`` times the reference's own CPU implementation
 (boo_batched_matmul_cpu of the reference core built into oracle/_ref, else the
@@ -52,7 +57,14 @@ def parse():
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--gen-kw', default=None,
                     help='JSON overrides of the generator size (reduced cases for profiling)')
+    ap.add_argument('--split', choices=('features', 'rows'), default='features',
+                    help='multi-GPU partitioning (ignored at --gpus 1)')
     return ap.parse_args()
+
+
+def W_CONFIG_KW(cfg_name):
+    from spmm_b200 import workloads as W
+    return W.CONFIGS[cfg_name]['kw']
 
 
 def make_matrix(cfg_name, gen_kw=None):
@@ -344,21 +356,43 @@ def native_arm(args):
     from spmm_b200 import _lib
     from spmm_b200 import workloads as W
 
+    from spmm_b200 import distributed as D
+
     world = int(os.environ.get('WORLD_SIZE', '1'))
     rank = int(os.environ.get('RANK', '0'))
     local = int(os.environ.get('LOCAL_RANK', '0'))
     torch.cuda.set_device(local)
     dev = torch.device('cuda', local)
     if world > 1:
-        import datetime
-        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120), device_id=dev)
+        D.init('nccl', timeout_s=120, device=dev)
+    split = args.split if world > 1 else 'features'
 
-    mat, cfg = make_matrix(args.config, args.gen_kw)
+    gen_kw = args.gen_kw
+    if split == 'rows' and args.config in ('c3_powerlaw', 'c5_uniform'):
+        kw0 = dict(W_CONFIG_KW(args.config))
+        kw0.update(json.loads(gen_kw) if gen_kw else {})
+        kw0['n'] = kw0['n'] * world                     # weak scaling: N = world * N0
+        gen_kw = json.dumps(kw0)
+    mat, cfg = make_matrix(args.config, gen_kw)
     fmt = args.format or cfg['fmt']
+    if split == 'rows' and fmt != 'boo':
+        raise SystemExit('--split rows is implemented for the BOO format')
     K = cfg['K']
+    x_bcast_ms = None
     t0 = time.perf_counter()
-    if fmt == 'boo':
-        A = S.csr_to_boo(mat, cluster='identity', target_nr=cfg['target'], target_nc=cfg['target'])
+    if split == 'rows':
+        rows_all, cols_all = mat.shape
+        rs = D.RowSplitBOO(mat, np.arange(rows_all) // cfg['target'], np.arange(cols_all) // cfg['target'],
+                           dev)
+        A = rs.boo
+        mat_full, mat = mat, D.shard_csr(mat, rs.shard)      # this rank's rows (global columns)
+    elif fmt == 'boo':
+        A = None
+        if rank == 0:
+            A = S.csr_to_boo(mat, cluster='identity', target_nr=cfg['target'], target_nc=cfg['target'])
+            A.to(dev)
+        if world > 1:
+            A = D.broadcast_boo(A, dev)                  # built once, replicated over NCCL
     else:
         A = S.csr_to_pbr(mat, 8, 8, 4)
     torch.cuda.synchronize(dev)
@@ -368,7 +402,22 @@ def native_arm(args):
     st = A._dev_struct(meta)
     L = _lib.lib()
     fn = L.spmm_boo_matmul if fmt == 'boo' else L.spmm_pbr_matmul
-    x = W.dense_x(mat.shape[1], K, seed=rank).to(dev)
+    if split == 'rows':
+        # X once into every rank's HBM (timed on its own, not part of the step)
+        xs = W.dense_x(mat.shape[1], K, seed=0) if rank == 0 else None
+        if xs is not None:
+            xs = xs.to(dev)
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        b0 = torch.cuda.Event(enable_timing=True)
+        b1 = torch.cuda.Event(enable_timing=True)
+        b0.record()
+        x = D.broadcast_dense(xs, (mat.shape[1], K), torch.float32, dev)
+        b1.record()
+        torch.cuda.synchronize(dev)
+        x_bcast_ms = b0.elapsed_time(b1)
+    else:
+        x = W.dense_x(mat.shape[1], K, seed=rank).to(dev)
     y = torch.empty((mat.shape[0], K), dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream(dev)
     sh = stream.cuda_stream
@@ -418,7 +467,11 @@ def native_arm(args):
 
     ms_step = ms / args.steps
     flops_rank = 2.0 * mat.nnz * K
-    value = world * flops_rank / (ms_step * 1e-3) / 1e9
+    if split == 'rows':
+        flops_all = 2.0 * mat_full.nnz * K              # every rank's shard in the max time
+        value = flops_all / (ms_step * 1e-3) / 1e9
+    else:
+        value = world * flops_rank / (ms_step * 1e-3) / 1e9
 
     abytes, xbytes, ybytes = (format_bytes_boo if fmt == 'boo' else format_bytes_pbr)(A, K)
     alg = abytes + xbytes + ybytes
@@ -441,7 +494,8 @@ def native_arm(args):
         t = torch.tensor([e_s], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e_s = float(t.item())
-    e2e = {'value': round(world * flops_rank / e_s / 1e9, 3), 'unit': 'GFLOP/s',
+    e2e_flops = flops_all if split == 'rows' else world * flops_rank
+    e2e = {'value': round(e2e_flops / e_s / 1e9, 3), 'unit': 'GFLOP/s',
            'h2d_bytes_per_step': int(x_host.numel() * 4), 'd2h_bytes_per_step': int(yh.numel() * 4),
            'ms_per_step': round(e_s * 1e3, 3)}
 
@@ -461,8 +515,14 @@ def native_arm(args):
         'config': {'workload': args.config + (f' {args.gen_kw}' if args.gen_kw else ''),
                    'format': fmt,
                    'grouping': 'identity' if fmt == 'boo' else '8x8 bitset blocks',
-                   'target': cfg['target'] if fmt == 'boo' else None, 'rows': int(mat.shape[0]),
-                   'nnz': int(mat.nnz), 'K_per_gpu': K, 'parallelism': f'feature-split x{world}',
+                   'target': cfg['target'] if fmt == 'boo' else None,
+                   'rows': int(mat_full.shape[0] if split == 'rows' else mat.shape[0]),
+                   'nnz': int(mat_full.nnz if split == 'rows' else mat.nnz),
+                   'K_per_gpu': K if split != 'rows' else None,
+                   'K': K if split == 'rows' else K * world,
+                   'parallelism': (f'row-split x{world} (nnz-balanced row groups, X broadcast once)'
+                                   if split == 'rows' else f'feature-split x{world}'),
+                   'x_broadcast_ms': None if x_bcast_ms is None else round(x_bcast_ms, 3),
                    'l2': 'inputs larger than L2 (A+X+Y = %.2f GB), no flush' % (alg / 1e9),
                    'build_s': round(build_s, 3)},
         'roofline': {'bound': 'hbm', 'achieved': round(achieved, 1), 'peak': peak,
