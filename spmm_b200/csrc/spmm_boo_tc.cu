@@ -3,49 +3,52 @@
 //
 // The reference multiplies each BOO block on CUDA cores, one thread per
 // (block row, feature) with the block's X rows staged in shared memory
-// (torch_fast_spdmm/kernels/boo_kernel.cu:410-595).  Here a block is a small
-// dense product instead: for the row group's feature tile of 128 columns,
+// (torch_fast_spdmm/kernels/boo_kernel.cu:410-595).  Here a block with enough
+// nonzeros is a small dense product instead: for a 128-feature tile,
 //
 //     Yt[f][r] += sum_c  Xt[f][c] * Ablk[r][c]        (Yt = Y^T, Xt = X^T)
 //
-// is one tcgen05.mma with M = 128 features, N = NR block rows, K = the block's
-// columns in steps of 8.  Xt (the gathered X rows of the block's column group,
-// 128 features x PW columns) is the A operand and lives in tensor memory; the
-// densified block (NR x PW, zero-filled) is the B operand in 128-byte-swizzled
-// K-major shared memory; the accumulator Yt lives in tensor memory for the
-// whole row group.  fp32 accuracy comes from the split x = hi + lo with hi =
-// x truncated to tf32: Xhi*Ahi + Xlo*Ahi + Xhi*Alo (the dropped lo*lo term is
-// below 2^-20 |a||x|).
+// is a tcgen05.mma with M = 128 features, K = the block's columns in steps of
+// 8.  Xt (the block's X panel, 128 features x PW columns) is the A operand in
+// tensor memory; the densified block is the B operand in 128-byte-swizzled
+// K-major shared memory; the accumulator Yt stays in tensor memory for the
+// whole row group.  fp32 accuracy: x = hi + lo with hi = x truncated to tf32,
+// Y = Xhi*Ahi + Xlo*Ahi + Xhi*Alo (the dropped lo*lo term is below
+// 2^-20 |a||x|), issued as two MMAs per K step: Xhi * [Ahi; Alo] with N = 2 NR
+// and Xlo * Ahi with N = NR (an M = 128 MMA costs about 50 cycles up to N ~ 96,
+// so stacking saves a third of the instructions).
 //
-// One persistent CTA per SM, warp-specialised:
-//   warp 0           one thread issues the MMAs and commits slot releases;
-//   warp 1           block metadata (chunk search, block descriptors);
-//                    (low warp numbers: the schedulers favour older warps,
-//                    and these two sit on every block's critical path;
-//                    warps 2-3 are idle so the warpgroups below start on a
-//                    tensor-memory lane quadrant boundary)
-//   warps 4-7        epilogue: tensor memory -> registers, CSR remainder and
-//                    COO tail of each row (the reference's remainder and tail
-//                    kernels, boo_kernel.cu:905-937, pbr_kernel.cu:976-1049),
-//                    one coalesced store of every Y element;
-//   warps 8..8+4NL   NL loader warpgroups; loader j owns X slot j in tensor
-//                    memory and three A tiles in shared memory.  Per block it
-//                    loads the used K steps of the block's X panel (16-byte
-//                    loads from the gathered copy below), splits and stores
-//                    them to tensor memory, while the next block's nonzeros
-//                    are scattered into the next A tile.
+// Work decomposition: a CTA per SM runs NW independent row-group workers
+// (warpgroups of 128 threads, one per quadruple of tensor-memory lane
+// quadrants).  A worker owns 2 NR accumulator columns and 2 PW panel columns
+// of tensor memory and two A tiles in shared memory, and processes its row
+// groups end to end:
+//   * the row group's blocks with >= kDenseNnz nonzeros, one after another:
+//     panel loads (16-byte loads from the gathered copy below) and the scatter
+//     of the block's nonzeros into an A tile overlap the MMAs of the previous
+//     block; one elected thread issues the MMAs and commits to the worker's
+//     mbarrier;
+//   * meanwhile-free CUDA cores sum the rest -- blocks with fewer nonzeros
+//     (an M = 128 MMA per 8 used columns does not pay for them) and the CSR
+//     remainder (the reference's remainder kernel, boo_kernel.cu:905-937) --
+//     into a shared-memory accumulator, then the COO tail (pbr_kernel.cu:
+//     976-1049) and the rare products left out for non-finite operands;
+//   * the accumulator comes out of tensor memory, the two sums meet, and
+//     every Y element is stored once.
+// Workers are independent, so four row groups proceed at once per SM and the
+// tensor pipe interleaves their MMAs; there are no cross-warp queues.  Tasks
+// (batch, chunk of consecutive row groups, feature tile -- innermost) are dealt
+// round-robin to all workers, so they sweep the matrix together and the X
+// rows they share stay in L2.
+//
 // Before the product a gather pass copies X column group by column group into
 // Xt[batch][group][4-column quad][feature] (float4 of 4 columns), so that a
-// panel row is 8 coalesced 16-byte loads instead of 32 scattered 4-byte ones.
-// Work is split into tasks (batch, chunk of consecutive row groups, feature
-// tile -- innermost) dealt round-robin to the CTAs, so that the CTAs sweep the
-// matrix together: the X rows they share and the blocks of a chunk (read once
-// per feature tile) stay in L2.
+// panel row is PW/4 coalesced 16-byte loads instead of PW scattered 4-byte
+// ones.
 //
-// Every wait is bounded (clock-limited); on expiry the CTA raises an abort
-// flag, every role leaves its loop, outstanding MMAs are drained, tensor
-// memory is released and a status word readable through spmm_tc_status() is
-// set.
+// Every wait is bounded (clock-limited); on expiry the worker raises an abort
+// flag and stops, outstanding MMAs are drained, tensor memory is released and
+// a status word readable through spmm_tc_status() is set.
 #include <climits>
 
 #include "ptx.cuh"
@@ -58,30 +61,15 @@ __device__ int g_tc_status;  // 0, or the first abort code of a tensor-core laun
 namespace {
 
 constexpr int kFeat = 128;           // features per task: MMA M, tensor-memory lanes
-constexpr int kDescRing = 64;        // block descriptors in flight (metadata warp -> loaders)
-// Chunks in flight (metadata warp -> epilogue).  A loader asks for the
-// descriptor of its block i+2 before it hands block i to the MMA, so the
-// metadata warp must be able to post every chunk up to 3*NL blocks past the
-// oldest row group the epilogue still waits for, even when each chunk holds a
-// single one-block row group: the ring must exceed 3*NL + 2 entries, or the
-// epilogue -> MMA -> loader -> metadata-warp wait cycle closes.
-constexpr int kChunkRing = 32;
-constexpr int kATiles = 3;           // A tiles per loader warpgroup
-constexpr int kMaxChunkRgs = 8;      // row groups per chunk
 // Blocks with at least kDenseNnz nonzeros go through the tensor cores; the
-// others (and the CSR remainder) are summed on CUDA cores by the epilogue.  An
-// M = 128 MMA costs ~50 cycles whatever N is, so a 32 x 32 block needs a few
-// dozen nonzeros before 3 MMAs per 8 used columns beat per-nonzero FMAs.
+// others (and the CSR remainder) are summed on CUDA cores.  An M = 128 MMA
+// costs ~50 cycles whatever N is, so a 32 x 32 block needs a few dozen
+// nonzeros before two MMAs per 8 used columns beat per-nonzero FMAs.
 constexpr int kDenseNnz = 48;
-constexpr int kListCap = 1024;       // epilogue: staged (row, column, value) entries per pass
-constexpr int kSegs = 32;            // epilogue: segments (sparse blocks, remainder rows) per pass
-constexpr int kNzPre = 4;            // nonzeros per loader thread fetched ahead
+constexpr int kSegs = 32;            // blocks or rows listed per pass
+constexpr int kListCap = 512;        // staged (row, column, value) entries per pass
+constexpr int kNzPre = 4;            // nonzeros per thread fetched ahead
 constexpr long long kWaitCycles = 1ll << 32;  // ~2 s at 2 GHz
-
-// kSpecial: the block has a non-finite value in A or in a gathered X column;
-// those products were left out of the MMA and the epilogue adds them on CUDA
-// cores, so 0 * Inf never appears in rows that do not use the value.
-enum : uint32_t { kFirst = 1, kLast = 2, kEnd = 4, kSpecial = 8 };
 
 struct TcParams {
     int64_t rows, cols, K, nb, n_rg, rem_nnz, tail_nnz;
@@ -103,73 +91,42 @@ struct TcParams {
     int64_t n_cg;
 };
 
-struct BlockDesc {
-    int32_t cg, k0, k1, rg, task, pad;
-    uint32_t shift, flags;
-};
-
-struct ChunkInfo {
-    int32_t task, rg0, rg1, end;
-    uint32_t mask;                     // bit i: row group rg0 + i has tensor-core blocks
-    int32_t bstart[kMaxChunkRgs + 1];  // first block of each row group
-    uint8_t ndense[kMaxChunkRgs];      // tensor-core blocks of each row group
-};
-
-// Epilogue scratch: the row group's CUDA-core partial sums, one copy per
-// summing warp (warp w adds entries w, w + P, ... for all 128 features, 4 per
-// lane), and one pass of staged entries.
-template <int NR>
-struct alignas(16) EpiSmem {
-    static constexpr int P = NR <= 32 ? 4 : 2;   // summing warps / partial copies
-    float ys[P][NR][kFeat];
-    int32_t lcol[kListCap];
-    float lval[kListCap];
+// One worker's shared memory.
+template <int NR, int PW>
+struct alignas(1024) WorkerSmem {
+    static constexpr int kTileBytes = 2 * NR * PW * 4;   // [K atom][NR hi rows, NR lo rows]
+    uint8_t tile[2][kTileBytes];    // A tiles (1024-aligned: 128-byte swizzle atoms)
+    float ys[NR][kFeat];            // CUDA-core sums; thread f owns column f
+    int2 lent[kListCap];            // staged entries: (column, value bits)
     uint8_t lrow[kListCap];
-    int32_t soff[kSegs + 1];   // prefix of the segments' entry counts
-    int32_t sbase[kSegs];      // first entry (block nonzero or remainder index)
-    int32_t scb[kSegs];        // block: first column of its group in col_ids; row segment: -1
-    uint32_t saux[kSegs];      // block: index shift; row segment: local row
+    int32_t soff[kSegs + 1];        // segment table: prefix of entry counts,
+    int32_t sbase[kSegs];           //   first entry,
+    int32_t scb[kSegs];             //   block: col_ids base of its group; row segment: -1
+    uint32_t saux[kSegs];           //   block: index shift; row segment: local row
+    int32_t dk0[kSegs], dk1[kSegs], dcg[kSegs];  // the row group's tensor-core blocks
+    uint32_t dshift[kSegs];
+    uint64_t mma_bar;               // completes once per MMA commit
+    uint32_t kmask[2], aspecial[2];
 };
 
-struct SlotMeta {
-    uint32_t kmask, flags;
-    uint64_t bdesc;  // shared-memory descriptor of the block's A tile (hi part)
-};
-
-template <int PW, int NL>
-struct alignas(16) TcCtl {
-    uint64_t full[NL], empty[NL];
-    uint64_t dfull[2], dempty[2];
-    uint64_t descfull[kDescRing], descempty[kDescRing];
-    uint64_t chunkfull[kChunkRing], chunkempty[kChunkRing];
-    uint64_t fin;
-    uint32_t kmask[NL][2];  // K steps (8 columns) with nonzeros, per staged block
-    uint32_t aspecial[NL][2];
-    BlockDesc desc[kDescRing];
-    ChunkInfo chunk[kChunkRing];
-    SlotMeta meta[NL];
-    uint32_t dvalid[2], dspecial[2];
+struct Ctl {
     uint32_t tmem_base;
     volatile int abort;
 };
 
-template <int NR, int PW, int NL>
+template <int NR, int PW, int NW>
 struct TcShape {
-    static constexpr int kTileBytes = NR * PW * 4;               // one of hi / lo
-    static constexpr int kTilesBytes = NL * kATiles * 2 * kTileBytes;
-    static constexpr int kThreads = 32 * (8 + 4 * NL);
-    // dynamic shared memory: A tiles (1024-aligned base), epilogue scratch,
-    // control block (mbarriers: 8-byte alignment), each offset 128-aligned
-    static constexpr int kEpiOff = kTilesBytes;
-    static constexpr int kCtlOff = (kEpiOff + (int)sizeof(EpiSmem<NR>) + 127) & ~127;
-    static constexpr int kSmem = 1024 + kCtlOff + (int)sizeof(TcCtl<PW, NL>);
-    static_assert(kTilesBytes % 1024 == 0 && kCtlOff % 128 == 0, "shared-memory carve-out alignment");
-    static_assert(kSmem <= 227 * 1024, "shared memory per CTA");
+    using W = WorkerSmem<NR, PW>;
+    static constexpr int kThreads = 128 * NW;
+    static constexpr int kWorkerCols = 2 * NR + 2 * PW;   // accumulator + panel (hi, lo)
+    static constexpr int kSmem = 1024 + NW * (int)sizeof(W) + 128;
     static constexpr uint32_t kTmemCols = 512;
-    static_assert(2 * NR + NL * 2 * PW <= (int)kTmemCols, "tensor memory budget");
-    static_assert(NR % 16 == 0 && NR >= 16 && NR <= 256, "MMA N for M = 128");
+    static_assert(NW * kWorkerCols <= (int)kTmemCols, "tensor memory budget");
+    static_assert(NR % 16 == 0 && 2 * NR <= 256, "MMA N for M = 128");
     static_assert(PW % 32 == 0 && PW <= 64, "panel width");
-    static_assert(kChunkRing > 3 * NL + 2, "chunk ring shallower than the loaders' lookahead");
+    static_assert(W::kTileBytes % 1024 == 0 && sizeof(W) % 1024 == 0, "tile alignment");
+    static_assert(kSmem <= 227 * 1024, "shared memory per CTA");
+    static_assert(NW <= 4, "one worker per lane-quadrant set, named barriers 1..NW");
 };
 
 // ---- bounded waits ------------------------------------------------------
@@ -241,13 +198,15 @@ __device__ __forceinline__ bool bar_and(uint32_t id, uint32_t n, bool v) {
 
 // ---- operand layout -------------------------------------------------------
 
-// Byte offset of A(r, c) in an NR x PW tile stored K-major with the 128-byte
+// Byte offset of Ahi(r, c) in a block tile stored K-major with the 128-byte
 // swizzle: 32 columns (128 B) per row and atom of 8 rows, the 16-byte chunk
-// index XORed with the row within the atom; PW = 64 uses two such atoms.
+// index XORed with the row within the atom.  Each 32-column K atom holds the
+// NR hi rows followed by the NR lo rows (Alo(r, c) = Ahi offset + NR * 128),
+// so one descriptor spans the stacked [Ahi; Alo] operand of an N = 2 NR MMA.
 template <int NR>
 __device__ __forceinline__ uint32_t a_offset(uint32_t r, uint32_t c) {
     const uint32_t cc = c & 31u;
-    return (c >> 5) * (NR * 128u) + r * 128u + ((((cc >> 2) ^ r) & 7u) << 4) + ((cc & 3u) << 2);
+    return (c >> 5) * (2u * NR * 128u) + r * 128u + ((((cc >> 2) ^ r) & 7u) << 4) + ((cc & 3u) << 2);
 }
 
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms
@@ -287,387 +246,43 @@ __device__ __forceinline__ int64_t warp_lower_bound(const int32_t *a, int64_t n,
     return lo + __popc(__ballot_sync(kFullMask, pred));
 }
 
-// ---- roles ------------------------------------------------------------------
+// ---- the worker ----------------------------------------------------------------
 
-template <int NR, int PW, int NL>
-__device__ void meta_role(const TcParams &p, TcCtl<PW, NL> &ctl, int lane) {
-    volatile int *abort = &ctl.abort;
-    const unsigned lt_mask = (1u << lane) - 1u;
-    int64_t q = 0;     // descriptors issued (tensor-core blocks)
-    int64_t cidx = 0;  // chunks issued
-    bool ok = true;
-    for (int64_t task = blockIdx.x; task < p.n_tasks && ok; task += gridDim.x) {
-        const int64_t chunk = (task / p.n_ft) % p.n_chunks;
-        const int64_t rg0 = chunk * p.chunk_rgs;
-        const int64_t rg1 = rg0 + p.chunk_rgs < p.n_rg ? rg0 + p.chunk_rgs : p.n_rg;
-        const int nrg = (int)(rg1 - rg0);
-        const int64_t bl = warp_lower_bound(p.blk_row_grp, p.nb, rg0, lane);
-        // Pass 1: blocks and tensor-core blocks per row group of the chunk.
-        // The epilogue gets the chunk before its descriptors, so it can drain
-        // accumulators (and sum the CUDA-core part) while they flow.
-        int call[kMaxChunkRgs], cden[kMaxChunkRgs];
-#pragma unroll
-        for (int k = 0; k < kMaxChunkRgs; ++k) call[k] = cden[k] = 0;
-        for (int64_t b0 = bl;; b0 += 32) {
-            const int64_t b = b0 + lane;
-            const int64_t rgb = b < p.nb ? (int64_t)__ldg(p.blk_row_grp + b) : INT64_MAX;
-            const bool valid = rgb < rg1;
-            const bool dense =
-                valid && __ldg(p.blk_nz_ptr + b + 1) - __ldg(p.blk_nz_ptr + b) >= p.dense_nnz;
-#pragma unroll
-            for (int k = 0; k < kMaxChunkRgs; ++k) {
-                call[k] += __popc(__ballot_sync(kFullMask, valid && rgb == rg0 + k));
-                cden[k] += __popc(__ballot_sync(kFullMask, dense && rgb == rg0 + k));
-            }
-            if (__ballot_sync(kFullMask, valid) != kFullMask) break;
-        }
-        ChunkInfo ci{};
-        ci.task = (int32_t)task;
-        ci.rg0 = (int32_t)rg0;
-        ci.rg1 = (int32_t)rg1;
-        ci.bstart[0] = (int32_t)bl;
-#pragma unroll
-        for (int k = 0; k < kMaxChunkRgs; ++k) {
-            ci.bstart[k + 1] = ci.bstart[k] + call[k];
-            ci.ndense[k] = (uint8_t)(cden[k] < 255 ? cden[k] : 255);
-            if (cden[k]) ci.mask |= 1u << k;
-        }
-        if (lane == 0) {
-            const int s = (int)(cidx % kChunkRing);
-            ok = wait_phase(&ctl.chunkempty[s], (uint32_t)((cidx / kChunkRing) & 1) ^ 1u, abort, 2);
-            if (ok) {
-                ctl.chunk[s] = ci;
-                mbar_arrive(&ctl.chunkfull[s]);
-            }
-        }
-        ok = __shfl_sync(kFullMask, ok, 0);
-        ++cidx;
-        if (!ok) break;
-        // Pass 2: a descriptor per tensor-core block, in block order, flagged
-        // first / last among its row group's tensor-core blocks.
-        int posted[kMaxChunkRgs];
-#pragma unroll
-        for (int k = 0; k < kMaxChunkRgs; ++k) posted[k] = 0;
-        const int64_t bend = ci.bstart[nrg < kMaxChunkRgs ? nrg : kMaxChunkRgs];
-        for (int64_t b0 = bl; b0 < bend && ok; b0 += 32) {
-            const int64_t b = b0 + lane;
-            const bool valid = b < bend;
-            BlockDesc d{};
-            bool dense = false;
-            int k = 0;
-            if (valid) {
-                d.k0 = __ldg(p.blk_nz_ptr + b);
-                d.k1 = __ldg(p.blk_nz_ptr + b + 1);
-                dense = d.k1 - d.k0 >= p.dense_nnz;
-                d.rg = __ldg(p.blk_row_grp + b);
-                k = (int)(d.rg - rg0);
-                d.cg = __ldg(p.blk_col_grp + b);
-                d.shift = __ldg(p.blk_shift + b);
-                d.task = (int32_t)task;
-            }
-            int before = 0, mine_posted = 0, mine_total = 0;
-#pragma unroll
-            for (int kk = 0; kk < kMaxChunkRgs; ++kk) {
-                const unsigned m = __ballot_sync(kFullMask, dense && k == kk);
-                if (k == kk) {
-                    before = __popc(m & lt_mask);
-                    mine_posted = posted[kk];
-                    mine_total = cden[kk];
-                }
-                posted[kk] += __popc(m);
-            }
-            const unsigned dm = __ballot_sync(kFullMask, dense);
-            bool w = true;
-            if (dense) {
-                d.flags = (mine_posted + before == 0 ? kFirst : 0u) |
-                          (mine_posted + before + 1 == mine_total ? kLast : 0u);
-                const int64_t qq = q + __popc(dm & lt_mask);
-                const int s = (int)(qq % kDescRing);
-                w = wait_phase(&ctl.descempty[s], (uint32_t)((qq / kDescRing) & 1) ^ 1u, abort, 1);
-                if (w) {
-                    ctl.desc[s] = d;
-                    mbar_arrive(&ctl.descfull[s]);
-                }
-            }
-            ok = __all_sync(kFullMask, w);
-            q += __popc(dm);
-        }
-    }
-    if (!ok) return;
-    // End markers: one descriptor per loader warpgroup, one chunk.
-    bool w = true;
-    if (lane < NL) {
-        const int64_t qq = q + lane;
-        const int s = (int)(qq % kDescRing);
-        w = wait_phase(&ctl.descempty[s], (uint32_t)((qq / kDescRing) & 1) ^ 1u, abort, 1);
-        if (w) {
-            BlockDesc d{};
-            d.flags = kEnd;
-            ctl.desc[s] = d;
-            mbar_arrive(&ctl.descfull[s]);
-        }
-    }
-    if (lane == 0) {
-        const int s = (int)(cidx % kChunkRing);
-        if (wait_phase(&ctl.chunkempty[s], (uint32_t)((cidx / kChunkRing) & 1) ^ 1u, abort, 2)) {
-            ChunkInfo ci{};
-            ci.end = 1;
-            ctl.chunk[s] = ci;
-            mbar_arrive(&ctl.chunkfull[s]);
-        }
-    }
-    __syncwarp();
+// Waits for the phase of `bar` with the given parity, bounded by the clock
+// only (used to drain MMAs before tensor memory is released, also after an
+// abort).
+__device__ __forceinline__ bool drain_phase(uint64_t *bar, uint32_t parity) {
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity))
+        if (clock64() - t0 > kWaitCycles) return false;
+    return true;
 }
 
-template <int NR, int PW, int NL>
-__device__ void loader_role(const TcParams &p, TcCtl<PW, NL> &ctl, uint8_t *tiles, uint32_t tmem, int j, int lt) {
-    using Shape = TcShape<NR, PW, NL>;
-    constexpr int KS = PW / 8;  // K steps of a panel
-    volatile int *abort = &ctl.abort;
-    const uint32_t bar = 2 + j;
-    const uint32_t lane_addr = (uint32_t)((lt & ~31) << 16);
-    const uint32_t xslot = tmem + 2 * NR + (uint32_t)j * 2 * PW;
-    uint8_t *my_tiles = tiles + (size_t)j * kATiles * 2 * Shape::kTileBytes;
-
-    // Thread 0 waits, the warpgroup learns the (uniform) outcome at a barrier.
-    auto wg_wait = [&](uint64_t *b, uint32_t parity, int code) -> bool {
-        bool w = true;
-        if (lt == 0) w = wait_phase(b, parity, abort, code);
-        return bar_and(bar, 128, w);
-    };
-    // Reads descriptor number i of this warpgroup (uniform result).
-    auto get_desc = [&](int64_t i, BlockDesc &d) -> bool {
-        const int64_t qq = (int64_t)j + (int64_t)NL * i;
-        const int s = (int)(qq % kDescRing);
-        const bool w = wg_wait(&ctl.descfull[s], (uint32_t)((qq / kDescRing) & 1), 3);
-        if (w) d = ctl.desc[s];
-        return w;
-    };
-    auto release_desc = [&](int64_t i) {
-        const int64_t qq = (int64_t)j + (int64_t)NL * i;
-        mbar_arrive(&ctl.descempty[qq % kDescRing]);
-    };
-
-    // Stages block descriptor d into A tile `t` and mask buffer `cb`: zero
-    // the tile, scatter hi/lo, OR the mask of K steps with nonzeros.
-    // ipre/vpre hold this thread's first kNzPre nonzeros (loaded earlier).
-    auto stage = [&](const BlockDesc &d, int t, int cb, const uint16_t (&ipre)[kNzPre], const float (&vpre)[kNzPre]) {
-        uint8_t *hi = my_tiles + (size_t)t * 2 * Shape::kTileBytes;
-        float4 *z = reinterpret_cast<float4 *>(hi);
-        const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int u = 0; u < 2 * Shape::kTileBytes / 16 / 128; ++u) z[lt + 128 * u] = zero;
-        if (lt == 0) {
-            ctl.kmask[j][cb] = 0u;
-            ctl.aspecial[j][cb] = 0u;
-        }
-        named_bar_sync(bar, 128);
-        const uint32_t shift = d.shift, cm = (1u << shift) - 1u;
-        uint32_t m = 0u;
-        bool special = false;
-        auto put = [&](uint32_t idx, float v) {
-            const uint32_t r = idx >> shift, c = idx & cm;
-            if (r < (uint32_t)NR && c < (uint32_t)PW) {
-                const uint32_t off = a_offset<NR>(r, c);
-                if (!finite(v)) {
-                    special = true;
-                    v = 0.f;
-                }
-                const float h = tf32_hi(v);
-                *reinterpret_cast<float *>(hi + off) = h;
-                *reinterpret_cast<float *>(hi + Shape::kTileBytes + off) = v - h;
-                m |= 1u << (c >> 3);
-            }
-        };
-        const int n = d.k1 - d.k0;
-#pragma unroll
-        for (int u = 0; u < kNzPre; ++u)
-            if (lt + 128 * u < n) put(ipre[u], vpre[u]);
-        for (int e = lt + 128 * kNzPre; e < n; e += 128) put(__ldg(p.nz_idx + d.k0 + e), __ldg(p.nz_val + d.k0 + e));
-        m = __reduce_or_sync(kFullMask, m);
-        if ((lt & 31) == 0 && m) atomicOr(&ctl.kmask[j][cb], m);
-        if (__any_sync(kFullMask, special) && (lt & 31) == 0) ctl.aspecial[j][cb] = 1u;
-    };
-    auto prefetch = [&](const BlockDesc &d, uint16_t (&ipre)[kNzPre], float (&vpre)[kNzPre]) {
-        const int n = d.k1 - d.k0;
-#pragma unroll
-        for (int u = 0; u < kNzPre; ++u) {
-            const int e = lt + 128 * u;
-            ipre[u] = e < n ? __ldg(p.nz_idx + d.k0 + e) : (uint16_t)0;
-            vpre[u] = e < n ? __ldg(p.nz_val + d.k0 + e) : 0.f;
-        }
-    };
-
-    // Software pipeline over this warpgroup's blocks i = 0, 1, ...: while
-    // block i's panel loads are in flight, block i+1 (nonzeros fetched one
-    // iteration earlier) is scattered into its A tile and block i+2's
-    // nonzeros are fetched.
-    BlockDesc cur{}, nxt{}, nx2{};
-    uint16_t i1[kNzPre], i2[kNzPre];
-    float v1[kNzPre], v2[kNzPre];
-    if (!get_desc(0, cur)) return;
-    if (!(cur.flags & kEnd)) {
-        prefetch(cur, i1, v1);
-        stage(cur, 0, 0, i1, v1);
-    }
-    named_bar_sync(bar, 128);
-    if (lt == 0) release_desc(0);  // every thread has its copy
-    nxt.flags = kEnd;
-    if (!(cur.flags & kEnd)) {
-        if (!get_desc(1, nxt)) return;
-        if (!(nxt.flags & kEnd)) prefetch(nxt, i1, v1);
-        named_bar_sync(bar, 128);
-        if (lt == 0) release_desc(1);
-    }
-
-    for (int64_t i = 0;; ++i) {
-        const int t = (int)(i % kATiles), cb = (int)(i & 1);
-        if (cur.flags & kEnd) {
-            const bool w = i == 0 || wg_wait(&ctl.empty[j], (uint32_t)((i - 1) & 1), 4);
-            if (w && lt == 0) {
-                ctl.meta[j] = SlotMeta{0u, kEnd, 0ull};
-                mbar_arrive(&ctl.full[j]);
-            }
-            return;
-        }
-        // 1. load the panel of the current block: this thread's feature of
-        // the group's columns, 4 columns per 16-byte load, used K steps only
-        const uint32_t kmask = ctl.kmask[j][cb];
-        const bool aspecial = ctl.aspecial[j][cb] != 0u;
-        const int64_t task = cur.task;
-        const int64_t ft = task % p.n_ft, bt = task / (p.n_chunks * p.n_ft);
-        const float4 *xq = p.Xt + ((bt * p.n_cg + cur.cg) * (PW / 4)) * p.K + ft * kFeat + lt;
-        float x[PW];
-#pragma unroll
-        for (int ks = 0; ks < KS; ++ks) {
-            float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
-            if (kmask & (1u << ks)) {
-                a = __ldg(xq + (2 * ks) * p.K);
-                b = __ldg(xq + (2 * ks + 1) * p.K);
-            }
-            x[ks * 8 + 0] = a.x; x[ks * 8 + 1] = a.y; x[ks * 8 + 2] = a.z; x[ks * 8 + 3] = a.w;
-            x[ks * 8 + 4] = b.x; x[ks * 8 + 5] = b.y; x[ks * 8 + 6] = b.z; x[ks * 8 + 7] = b.w;
-        }
-        // 2. descriptor and nonzeros of block i+2
-        const bool more = !(nxt.flags & kEnd);
-        nx2.flags = kEnd;
-        if (more) {
-            if (!get_desc(i + 2, nx2)) return;
-            if (!(nx2.flags & kEnd)) prefetch(nx2, i2, v2);
-        }
-        // 3. block i+1 into the next A tile
-        if (more) stage(nxt, (int)((i + 1) % kATiles), (int)((i + 1) & 1), i1, v1);
-        // 4. wait until the MMAs of this slot's previous block are done
-        const bool w = i == 0 || wg_wait(&ctl.empty[j], (uint32_t)((i - 1) & 1), 4);
-        if (!w) return;
-        if (more && lt == 0) release_desc(i + 2);  // every thread has its copy
-        tc_fence_after();
-        // 5. split and store the panel: hi at xslot, lo at xslot + PW
-        bool xspecial = false;
-#pragma unroll
-        for (int ks = 0; ks < KS; ++ks) {
-            if (kmask & (1u << ks)) {
-                uint32_t h[8], l[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    float v = x[ks * 8 + e];
-                    if (!finite(v)) {
-                        xspecial = true;
-                        v = 0.f;
-                    }
-                    const float hv = tf32_hi(v);
-                    h[e] = __float_as_uint(hv);
-                    l[e] = __float_as_uint(v - hv);
-                }
-                tmem_st8(xslot + lane_addr + ks * 8, h);
-                tmem_st8(xslot + lane_addr + PW + ks * 8, l);
-            }
-        }
-        tmem_wait_st();
-        tc_fence_before();
-        fence_proxy_async_smem();
-        const bool special = bar_or(bar, 128, xspecial) || aspecial;
-        if (lt == 0) {
-            const uint32_t tile = smem_u32(my_tiles + (size_t)t * 2 * Shape::kTileBytes);
-            ctl.meta[j] = SlotMeta{kmask, cur.flags | (special ? kSpecial : 0u), b_desc_sw128(tile)};
-            mbar_arrive(&ctl.full[j]);
-        }
-        cur = nxt;
-        nxt = nx2;
-#pragma unroll
-        for (int u = 0; u < kNzPre; ++u) {
-            i1[u] = i2[u];
-            v1[u] = v2[u];
-        }
+// One past the last block of row group rg, scanning forward from b (the
+// first block with row group >= rg); row groups hold a handful of blocks.
+__device__ __forceinline__ int64_t group_end(const int32_t *blk_row_grp, int64_t nb, int64_t b, int64_t rg,
+                                             int lane) {
+    for (;; b += 32) {
+        const int64_t i = b + lane;
+        const bool in = i < nb && (int64_t)__ldg(blk_row_grp + i) <= rg;
+        const unsigned m = __ballot_sync(kFullMask, in);
+        if (m != kFullMask) return b + __popc(m);   // the group's blocks are a prefix
     }
 }
 
-template <int NR, int PW, int NL>
-__device__ void mma_role(TcCtl<PW, NL> &ctl, uint32_t tmem) {
-    using Shape = TcShape<NR, PW, NL>;
-    constexpr int KS = PW / 8;
-    constexpr uint32_t idesc = idesc_tf32<NR>();
-    constexpr uint64_t kLoDesc = Shape::kTileBytes >> 4;  // hi tile -> lo tile, descriptor units
-    volatile int *abort = &ctl.abort;
-    uint32_t dbuf = 0, du[2] = {0u, 0u};
-    uint32_t started = 0, special = 0;
-    // One thread issues; the tensor pipe takes an M = 128 MMA about every 50
-    // cycles, so the loop keeps per-MMA work to an add and the instruction:
-    // descriptors come precomputed and K-step offsets are constants.
-    for (uint32_t q = 0;; ++q) {
-        const uint32_t j = q % NL;
-        if (!wait_phase(&ctl.full[j], (q / NL) & 1u, abort, 5)) break;
-        tc_fence_after();
-        const SlotMeta m = ctl.meta[j];
-        if (m.flags & kEnd) break;
-        if (m.flags & kFirst) {
-            if (!wait_phase(&ctl.dempty[dbuf], (du[dbuf] & 1u) ^ 1u, abort, 6)) break;
-            tc_fence_after();
-            started = 0;
-            special = 0;
-        }
-        special |= m.flags & kSpecial;
-        const uint32_t d = tmem + dbuf * NR;
-        const uint32_t xa = tmem + 2 * NR + j * 2 * PW;
-#pragma unroll
-        for (int ks = 0; ks < KS; ++ks) {
-            if (m.kmask & (1u << ks)) {
-                const uint64_t bh = m.bdesc + (uint64_t)(((ks >> 2) * (NR * 128) + (ks & 3) * 32) >> 4);
-                mma_tf32_ts(d, xa + ks * 8, bh, idesc, started);
-                mma_tf32_ts(d, xa + PW + ks * 8, bh, idesc, 1u);
-                mma_tf32_ts(d, xa + ks * 8, bh + kLoDesc, idesc, 1u);
-                started = 1;
-            }
-        }
-        mma_commit(&ctl.empty[j]);
-        if (m.flags & kLast) {
-            ctl.dvalid[dbuf] = started;
-            ctl.dspecial[dbuf] = special;
-            mbar_arrive(&ctl.dfull[dbuf]);
-            mma_commit(&ctl.dfull[dbuf]);
-            ++du[dbuf];
-            dbuf ^= 1u;
-        }
-    }
-    // drain every MMA issued above before tensor memory is released
-    mma_commit(&ctl.fin);
-    wait_phase(&ctl.fin, 0u, abort, 7);
-}
-
-// CUDA-core part of row group rg, summed into e.ys (thread et owns feature
-// column et): the entries of its blocks with fewer than dense_nnz nonzeros,
-// then its rows' CSR remainder (the reference's remainder kernel,
-// boo_kernel.cu:905-937).  Segments (one per block or row) are listed by warp
-// 0, their entries staged as (local row, column, value) by all 128 threads,
-// then each thread sums them for its feature with 16 X loads in flight.
-template <int NR>
-__device__ __forceinline__ void epi_cuda_part(const TcParams &p, EpiSmem<NR> &e, int32_t bs, int32_t be,
-                                              int32_t rbase, int32_t nr, const float *xb, int et) {
-    const int nblk = be - bs;
-    const int nseg = nblk + (p.rem_nnz ? nr : 0);
+// CUDA-core part of a row group, summed into w.ys (thread f owns column f):
+// the entries of its blocks with fewer than dense_nnz nonzeros, then its
+// rows' CSR remainder.  Segments (one per block or row) are listed by warp 0,
+// their entries staged as (local row, column, value) by the warpgroup, then
+// each thread sums them for its feature with 16 X loads in flight.
+template <int NR, int PW>
+__device__ __forceinline__ void cuda_part(const TcParams &p, WorkerSmem<NR, PW> &w, int64_t bs, int64_t be,
+                                          int32_t rbase, int32_t nr, const float *xb, int wt, uint32_t bar) {
+    const int nblk = (int)(be - bs);
+    const int nseg = nblk + (p.rem_nnz ? (nr < NR ? nr : NR) : 0);
     for (int s0 = 0; s0 < nseg; s0 += kSegs) {
-        if (et < 32) {
-            const int sidx = s0 + et;
+        if (wt < 32) {
+            const int sidx = s0 + wt;
             int cnt = 0, base = 0, cb = -1;
             uint32_t aux = 0;
             if (sidx < nblk) {
@@ -690,99 +305,91 @@ __device__ __forceinline__ void epi_cuda_part(const TcParams &p, EpiSmem<NR> &e,
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
                 const int n = __shfl_up_sync(kFullMask, incl, o);
-                if (et >= o) incl += n;
+                if (wt >= o) incl += n;
             }
-            e.soff[et + 1] = incl;
-            if (et == 0) e.soff[0] = 0;
-            e.sbase[et] = base;
-            e.scb[et] = cb;
-            e.saux[et] = aux;
+            w.soff[wt + 1] = incl;
+            if (wt == 0) w.soff[0] = 0;
+            w.sbase[wt] = base;
+            w.scb[wt] = cb;
+            w.saux[wt] = aux;
         }
-        named_bar_sync(1, 128);
-        const int total = e.soff[kSegs];
+        named_bar_sync(bar, 128);
+        const int total = w.soff[kSegs];
         for (int g0 = 0; g0 < total; g0 += kListCap) {
             const int ne = total - g0 < kListCap ? total - g0 : kListCap;
-            for (int i = et; i < ne; i += 128) {
+            for (int i = wt; i < ne; i += 128) {
                 const int g = g0 + i;
                 int lo = 0, hi = kSegs - 1;
                 while (lo < hi) {
                     const int mid = (lo + hi + 1) >> 1;
-                    if (e.soff[mid] <= g) lo = mid; else hi = mid - 1;
+                    if (w.soff[mid] <= g) lo = mid; else hi = mid - 1;
                 }
-                const int kidx = e.sbase[lo] + (g - e.soff[lo]);
+                const int kidx = w.sbase[lo] + (g - w.soff[lo]);
                 uint32_t r;
                 int32_t col;
                 float v;
-                if (e.scb[lo] >= 0) {
-                    const uint32_t idx = __ldg(p.nz_idx + kidx), sh = e.saux[lo];
+                if (w.scb[lo] >= 0) {
+                    const uint32_t idx = __ldg(p.nz_idx + kidx), sh = w.saux[lo];
                     r = idx >> sh;
-                    col = __ldg(p.col_ids + e.scb[lo] + (int32_t)(idx & ((1u << sh) - 1u)));
+                    col = __ldg(p.col_ids + w.scb[lo] + (int32_t)(idx & ((1u << sh) - 1u)));
                     v = __ldg(p.nz_val + kidx);
                 } else {
-                    r = e.saux[lo];
+                    r = w.saux[lo];
                     col = __ldg(p.rem_col + kidx);
                     v = __ldg(p.rem_val + kidx);
                 }
-                e.lrow[i] = (uint8_t)(r < (uint32_t)NR ? r : 255u);
-                e.lcol[i] = col;
-                e.lval[i] = v;
+                w.lrow[i] = (uint8_t)(r < (uint32_t)NR ? r : 255u);
+                w.lent[i] = make_int2(col, __float_as_int(v));
             }
-            named_bar_sync(1, 128);
-            constexpr int P = EpiSmem<NR>::P;
-            const int w = et >> 5, l4 = (et & 31) * 4;
-            if (w < P) {
-                // warp w: entries w, w + P, ...; lane: features 4l..4l+3
-                const float4 *x4 = reinterpret_cast<const float4 *>(xb - et + l4);
-                const int64_t k4 = p.K / 4;
-                constexpr int U = 8;
-                int i = w;
-                for (; i + (U - 1) * P < ne; i += U * P) {
-                    float4 x[U];
-#pragma unroll
-                    for (int u = 0; u < U; ++u) x[u] = __ldg(x4 + (int64_t)e.lcol[i + u * P] * k4);
-#pragma unroll
-                    for (int u = 0; u < U; ++u) {
-                        const uint32_t r = e.lrow[i + u * P];
-                        const float v = e.lval[i + u * P];
-                        if (r < (uint32_t)NR) {
-                            float4 *y = reinterpret_cast<float4 *>(&e.ys[w][r][l4]);
-                            float4 t = *y;
-                            t.x = fmaf(v, x[u].x, t.x);
-                            t.y = fmaf(v, x[u].y, t.y);
-                            t.z = fmaf(v, x[u].z, t.z);
-                            t.w = fmaf(v, x[u].w, t.w);
-                            *y = t;
-                        }
-                    }
+            named_bar_sync(bar, 128);
+            // Entries of a block arrive row by row: a running sum per row run,
+            // added to ys when the row changes (no shared-memory dependency
+            // chain between consecutive entries); 16 X loads in flight.
+            constexpr int U = 16;
+            uint32_t cur = 255u;
+            float run = 0.f;
+            auto add = [&](uint32_t r, float v, float x) {
+                if (r != cur) {
+                    if (cur < (uint32_t)NR) w.ys[cur][wt] += run;
+                    cur = r;
+                    run = 0.f;
                 }
-                for (; i < ne; i += P) {
-                    const float4 x = __ldg(x4 + (int64_t)e.lcol[i] * k4);
-                    const uint32_t r = e.lrow[i];
-                    const float v = e.lval[i];
-                    if (r < (uint32_t)NR) {
-                        float4 *y = reinterpret_cast<float4 *>(&e.ys[w][r][l4]);
-                        float4 t = *y;
-                        t.x = fmaf(v, x.x, t.x);
-                        t.y = fmaf(v, x.y, t.y);
-                        t.z = fmaf(v, x.z, t.z);
-                        t.w = fmaf(v, x.w, t.w);
-                        *y = t;
-                    }
+                run = fmaf(v, x, run);
+            };
+            int i = 0;
+            for (; i + U <= ne; i += U) {
+                float x[U];
+                int2 en[U];
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    en[u] = w.lent[i + u];
+                    x[u] = __ldg(xb + (int64_t)en[u].x * p.K);
+                }
+#pragma unroll
+                for (int u = 0; u < U; u += 4) {
+                    const uint32_t r4 = *reinterpret_cast<const uint32_t *>(&w.lrow[i + u]);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) add((r4 >> (8 * q)) & 0xFFu, __int_as_float(en[u + q].y), x[u + q]);
                 }
             }
-            named_bar_sync(1, 128);  // the list is reused by the next pass
+            for (; i < ne; ++i) {
+                const int2 en = w.lent[i];
+                add(w.lrow[i], __int_as_float(en.y), __ldg(xb + (int64_t)en.x * p.K));
+            }
+            if (cur < (uint32_t)NR) w.ys[cur][wt] += run;
+            named_bar_sync(bar, 128);  // the list is reused by the next pass
         }
-        named_bar_sync(1, 128);      // the segment table is rewritten next
+        named_bar_sync(bar, 128);      // the segment table is rewritten next
     }
 }
 
-// Rare contributions, summed into e.ys by each thread for its feature: the
+// Rare contributions, summed into w.ys by each thread for its feature: the
 // tensor-core block products left out for a non-finite operand (`special`),
 // and the COO tail (the reference's tail kernel, pbr_kernel.cu:976-1049).
-// Rolled loops, so the hot epilogue stays small for the instruction cache.
-template <int NR>
-__device__ __forceinline__ void epi_rare(const TcParams &p, EpiSmem<NR> &e, int32_t bs, int32_t be, int32_t rbase,
-                                         int32_t nr, bool special, const float *xb, int et) {
+// Rolled loops: the hot path stays small for the instruction cache.
+template <int NR, int PW>
+__device__ __forceinline__ void rare_part(const TcParams &p, WorkerSmem<NR, PW> &w, int64_t bs, int64_t be,
+                                          int32_t rbase, int32_t nr, bool special, const float *xb, int wt) {
     if (special) {
         for (int64_t b = bs; b < be; ++b) {
             const int32_t k0 = __ldg(p.blk_nz_ptr + b), k1 = __ldg(p.blk_nz_ptr + b + 1);
@@ -794,7 +401,7 @@ __device__ __forceinline__ void epi_rare(const TcParams &p, EpiSmem<NR> &e, int3
                 const uint32_t r = idx >> shift;
                 const float a = __ldg(p.nz_val + k);
                 const float x = __ldg(xb + (int64_t)__ldg(p.col_ids + cbase + (int32_t)(idx & cm)) * p.K);
-                if (r < (uint32_t)NR && (!finite(a) || !finite(x))) e.ys[0][r][et] = fmaf(a, x, e.ys[0][r][et]);
+                if (r < (uint32_t)NR && (!finite(a) || !finite(x))) w.ys[r][wt] = fmaf(a, x, w.ys[r][wt]);
             }
         }
     }
@@ -806,140 +413,262 @@ __device__ __forceinline__ void epi_rare(const TcParams &p, EpiSmem<NR> &e, int3
             const int64_t mid = (lo + hi) >> 1;
             if (__ldg(p.tail_row + mid) < row) lo = mid + 1; else hi = mid;
         }
-        float a = e.ys[0][r][et];
+        float a = w.ys[r][wt];
         for (int64_t k = lo; k < p.tail_nnz && __ldg(p.tail_row + k) == row; ++k)
             a = fmaf(__ldg(p.tail_val + k), __ldg(xb + (int64_t)__ldg(p.tail_col + k) * p.K), a);
-        e.ys[0][r][et] = a;
+        w.ys[r][wt] = a;
     }
 }
 
-template <int NR>
-__device__ __forceinline__ void zero_ys(EpiSmem<NR> &e, int et) {
-    float4 *z = reinterpret_cast<float4 *>(&e.ys[0][0][0]);
-    constexpr int n4 = EpiSmem<NR>::P * NR * kFeat / 4;
-#pragma unroll 4
-    for (int i = et; i < n4; i += 128) z[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-}
-
-template <int NR, int PW, int NL>
-__device__ void epilogue_role(const TcParams &p, TcCtl<PW, NL> &ctl, EpiSmem<NR> &e, uint32_t tmem, int et) {
+// One row-group worker (a warpgroup; wt = thread in the worker, tensor-memory
+// lane wt).  `tcol`: first of its 2 NR accumulator + 2 PW panel columns.
+template <int NR, int PW>
+__device__ void worker(const TcParams &p, WorkerSmem<NR, PW> &w, Ctl &ctl, uint32_t tcol, int64_t wid,
+                       int64_t nworkers, int wt, uint32_t bar) {
+    constexpr int KS = PW / 8;
+    constexpr int RH = (NR + 31) / 32;
+    constexpr uint32_t idesc1 = idesc_tf32<NR>();       // N = NR: Xlo * Ahi
+    constexpr uint32_t idesc2 = idesc_tf32<2 * NR>();   // N = 2 NR: Xhi * [Ahi; Alo]
     volatile int *abort = &ctl.abort;
-    const uint32_t lane_addr = (uint32_t)((et & ~31) << 16);
-    uint32_t dbuf = 0, du[2] = {0u, 0u};
-    for (int64_t c = 0;; ++c) {
-        const int s = (int)(c % kChunkRing);
-        bool w = true;
-        if (et == 0) w = wait_phase(&ctl.chunkfull[s], (uint32_t)((c / kChunkRing) & 1), abort, 8);
-        if (!bar_and(1, 128, w)) return;
-        const ChunkInfo ci = ctl.chunk[s];
-        named_bar_sync(1, 128);
-        if (et == 0) mbar_arrive(&ctl.chunkempty[s]);
-        if (ci.end) return;
-        const int64_t ft = ci.task % p.n_ft, bt = ci.task / (p.n_chunks * p.n_ft);
-        const float *xb = p.X + bt * p.cols * p.K + ft * kFeat + et;
-        float *yb = p.Y + bt * p.rows * p.K + ft * kFeat + et;
-        for (int32_t rg = ci.rg0; rg < ci.rg1; ++rg) {
-            const int k = rg - ci.rg0;
-            const int32_t bs = ci.bstart[k], be = ci.bstart[k + 1];
-            // row ids, one load round: lane l of every warp fetches rows
-            // l, l + 32, ... and shuffles spread them
-            constexpr int RH = (NR + 31) / 32;
+    const int lane = wt & 31;
+    const uint32_t lane_addr = (uint32_t)((wt & ~31) << 16);
+    const uint32_t dacc = tcol, xslot = tcol + 2 * NR;
+    uint32_t ncommit = 0;   // commits to w.mma_bar (one per tensor-core block)
+    bool ok = true;
+
+    // Thread 0 waits, the warpgroup learns the (uniform) outcome at a barrier.
+    auto wait_commit = [&](uint32_t c) -> bool {
+        bool r = true;
+        if (wt == 0) r = wait_phase(&w.mma_bar, c & 1u, abort, 4);
+        return bar_and(bar, 128, r);
+    };
+    auto prefetch = [&](int i, uint16_t (&ip)[kNzPre], float (&vp)[kNzPre]) {
+        const int32_t k0 = w.dk0[i], n = w.dk1[i] - k0;
+#pragma unroll
+        for (int u = 0; u < kNzPre; ++u) {
+            const int e = wt + 128 * u;
+            ip[u] = e < n ? __ldg(p.nz_idx + k0 + e) : (uint16_t)0;
+            vp[u] = e < n ? __ldg(p.nz_val + k0 + e) : 0.f;
+        }
+    };
+
+    for (int64_t task = wid; task < p.n_tasks && ok; task += nworkers) {
+        const int64_t ft = task % p.n_ft, chunk = (task / p.n_ft) % p.n_chunks;
+        const int64_t bt = task / (p.n_ft * p.n_chunks);
+        const int64_t rg0 = chunk * p.chunk_rgs;
+        const int64_t rg1 = rg0 + p.chunk_rgs < p.n_rg ? rg0 + p.chunk_rgs : p.n_rg;
+        const float *xb = p.X + bt * p.cols * p.K + ft * kFeat + wt;
+        float *yb = p.Y + bt * p.rows * p.K + ft * kFeat + wt;
+        const float4 *xt = p.Xt + bt * p.n_cg * (PW / 4) * p.K + ft * kFeat + wt;
+        int64_t b = warp_lower_bound(p.blk_row_grp, p.nb, rg0, lane);   // every warp: same answer
+        for (int64_t rg = rg0; rg < rg1 && ok; ++rg) {
+            const int64_t be = group_end(p.blk_row_grp, p.nb, b, rg, lane);
             const int32_t rbase = __ldg(p.row_grp_ptr + rg);
             const int32_t nr = __ldg(p.row_grp_ptr + rg + 1) - rbase;
             int32_t myrow[RH];
 #pragma unroll
             for (int h = 0; h < RH; ++h) {
-                const int r = h * 32 + (et & 31);
+                const int r = h * 32 + lane;
                 myrow[h] = r < nr && r < NR ? __ldg(p.row_ids + rbase + r) : -1;
             }
-            // CUDA-core part first: it overlaps the MMAs of this row group
-            const bool cuda_part = be - bs > (int32_t)ci.ndense[k] || p.rem_nnz;
-            bool in_ys = cuda_part || p.tail_nnz;
-            if (in_ys) {
-                zero_ys<NR>(e, et);
-                named_bar_sync(1, 128);
-                if (cuda_part) epi_cuda_part<NR>(p, e, bs, be, rbase, nr, xb, et);
+            uint32_t started = 0;
+            bool special = false, sparse = false;
+            // ---- tensor-core blocks, listed kSegs blocks at a time ----
+            for (int64_t b0 = b; b0 < be && ok; b0 += kSegs) {
+                const int nblk = be - b0 < kSegs ? (int)(be - b0) : kSegs;
+                int nd;
+                {
+                    const int64_t bb = b0 + lane;
+                    int32_t k0 = 0, k1 = 0;
+                    if (lane < nblk) {
+                        k0 = __ldg(p.blk_nz_ptr + bb);
+                        k1 = __ldg(p.blk_nz_ptr + bb + 1);
+                    }
+                    const bool dense = lane < nblk && k1 - k0 >= p.dense_nnz;
+                    const unsigned dm = __ballot_sync(kFullMask, dense);
+                    nd = __popc(dm);
+                    if (wt < 32 && dense) {
+                        const int slot = __popc(dm & ((1u << lane) - 1u));
+                        w.dk0[slot] = k0;
+                        w.dk1[slot] = k1;
+                        w.dcg[slot] = __ldg(p.blk_col_grp + bb);
+                        w.dshift[slot] = __ldg(p.blk_shift + bb);
+                    }
+                }
+                if (nd < nblk) sparse = true;
+                named_bar_sync(bar, 128);
+                uint16_t i1[kNzPre], i2[kNzPre];
+                float v1[kNzPre], v2[kNzPre];
+                if (nd > 0) prefetch(0, i1, v1);
+                for (int i = 0; i < nd; ++i) {
+                    const int t = (int)(ncommit & 1u);
+                    uint8_t *tile = w.tile[t];
+                    // 1. this block's panel: 16-byte loads of the group's columns
+                    const float4 *xq = xt + (int64_t)w.dcg[i] * (PW / 4) * p.K;
+                    float x[PW];
+#pragma unroll
+                    for (int q = 0; q < PW / 4; ++q) {
+                        const float4 a = __ldg(xq + q * p.K);
+                        x[4 * q] = a.x; x[4 * q + 1] = a.y; x[4 * q + 2] = a.z; x[4 * q + 3] = a.w;
+                    }
+                    // 2. next block's nonzeros
+                    if (i + 1 < nd) prefetch(i + 1, i2, v2);
+                    // 3. zero the tile (its MMAs, two blocks back, are complete) and scatter
+                    {
+                        float4 *z = reinterpret_cast<float4 *>(tile);
+#pragma unroll
+                        for (int u = 0; u < WorkerSmem<NR, PW>::kTileBytes / 16 / 128; ++u)
+                            z[wt + 128 * u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                        if (wt == 0) {
+                            w.kmask[t] = 0u;
+                            w.aspecial[t] = 0u;
+                        }
+                        named_bar_sync(bar, 128);
+                        const uint32_t shift = w.dshift[i], cm = (1u << shift) - 1u;
+                        uint32_t m = 0u;
+                        bool asp = false;
+                        auto put = [&](uint32_t idx, float v) {
+                            const uint32_t r = idx >> shift, c = idx & cm;
+                            if (r < (uint32_t)NR && c < (uint32_t)PW) {
+                                if (!finite(v)) {
+                                    asp = true;
+                                    v = 0.f;
+                                }
+                                const uint32_t off = a_offset<NR>(r, c);
+                                const float h = tf32_hi(v);
+                                *reinterpret_cast<float *>(tile + off) = h;
+                                *reinterpret_cast<float *>(tile + NR * 128 + off) = v - h;
+                                m |= 1u << (c >> 3);
+                            }
+                        };
+                        const int32_t k0 = w.dk0[i];
+                        const int n = w.dk1[i] - k0;
+#pragma unroll
+                        for (int u = 0; u < kNzPre; ++u)
+                            if (wt + 128 * u < n) put(i1[u], v1[u]);
+                        for (int e = wt + 128 * kNzPre; e < n; e += 128)
+                            put(__ldg(p.nz_idx + k0 + e), __ldg(p.nz_val + k0 + e));
+                        m = __reduce_or_sync(kFullMask, m);
+                        if (lane == 0 && m) atomicOr(&w.kmask[t], m);
+                        if (__any_sync(kFullMask, asp) && lane == 0) w.aspecial[t] = 1u;
+                    }
+                    // 4. the previous block's MMAs are done: the panel slot is free
+                    if (ncommit > 0 && !(ok = wait_commit(ncommit - 1))) break;
+                    if (ncommit == 0) named_bar_sync(bar, 128);
+                    tc_fence_after();
+                    const uint32_t kmask = w.kmask[t];
+                    // 5. split and store the panel: hi at xslot, lo at xslot + PW
+                    bool xsp = false;
+#pragma unroll
+                    for (int ks = 0; ks < KS; ++ks) {
+                        if (kmask & (1u << ks)) {
+                            uint32_t h[8], l[8];
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) {
+                                float v = x[ks * 8 + e];
+                                if (!finite(v)) {
+                                    xsp = true;
+                                    v = 0.f;
+                                }
+                                const float hv = tf32_hi(v);
+                                h[e] = __float_as_uint(hv);
+                                l[e] = __float_as_uint(v - hv);
+                            }
+                            tmem_st8(xslot + lane_addr + ks * 8, h);
+                            tmem_st8(xslot + lane_addr + PW + ks * 8, l);
+                        }
+                    }
+                    tmem_wait_st();
+                    tc_fence_before();
+                    fence_proxy_async_smem();
+                    if (bar_or(bar, 128, xsp) || w.aspecial[t]) special = true;
+                    // 6. MMAs of the block, issued by one thread
+                    if (wt == 0) {
+                        tc_fence_after();
+                        const uint64_t bd = b_desc_sw128(smem_u32(tile));
+                        uint32_t accum = started;   // 0: the first MMA of the group overwrites
+#pragma unroll
+                        for (int ks = 0; ks < KS; ++ks) {
+                            if (kmask & (1u << ks)) {
+                                const uint64_t bh =
+                                    bd + (uint64_t)(((ks >> 2) * (2 * NR * 128) + (ks & 3) * 32) >> 4);
+                                mma_tf32_ts(dacc, xslot + ks * 8, bh, idesc2, accum);
+                                mma_tf32_ts(dacc, xslot + PW + ks * 8, bh, idesc1, 1u);
+                                accum = 1;
+                            }
+                        }
+                        mma_commit(&w.mma_bar);
+                    }
+                    if (kmask) started = 1;   // uniform: every thread read kmask
+                    ++ncommit;
+#pragma unroll
+                    for (int u = 0; u < kNzPre; ++u) {
+                        i1[u] = i2[u];
+                        v1[u] = v2[u];
+                    }
+                }
             }
+            if (!ok) break;
+            const bool any_dense = started != 0;
+            // ---- CUDA-core part (overlaps the last block's MMAs) ----
+            const bool cpart = sparse || p.rem_nnz;
+            bool in_ys = cpart || p.tail_nnz;
+            if (in_ys) {
+#pragma unroll
+                for (int r = 0; r < NR; ++r) w.ys[r][wt] = 0.f;
+                if (cpart) cuda_part<NR, PW>(p, w, b, be, rbase, nr, xb, wt, bar);
+            }
+            // ---- the accumulator ----
             float acc[NR];
 #pragma unroll
             for (int r = 0; r < NR; ++r) acc[r] = 0.f;
-            bool special = false;
-            if ((ci.mask >> (uint32_t)k) & 1u) {
-                w = true;
-                if (et == 0) w = wait_phase(&ctl.dfull[dbuf], du[dbuf] & 1u, abort, 9);
-                if (!bar_and(1, 128, w)) return;
+            if (any_dense) {
+                if (!(ok = wait_commit(ncommit - 1))) break;
                 tc_fence_after();
-                if (ctl.dvalid[dbuf]) {
 #pragma unroll
-                    for (int h = 0; h < NR / 16; ++h) {
-                        uint32_t v[16];
-                        tmem_ld16(tmem + dbuf * NR + lane_addr + h * 16, v);
-                        tmem_wait_ld();
+                for (int h = 0; h < NR / 16; ++h) {
+                    uint32_t v[16], u[16];
+                    const uint32_t a0 = dacc + lane_addr + h * 16;
+                    tmem_ld16(a0, v);
+                    tmem_ld16(a0 + NR, u);
+                    tmem_wait_ld();
 #pragma unroll
-                        for (int q = 0; q < 16; ++q) acc[h * 16 + q] = __uint_as_float(v[q]);
-                    }
+                    for (int q = 0; q < 16; ++q) acc[h * 16 + q] = __uint_as_float(v[q]) + __uint_as_float(u[q]);
                 }
-                special = ctl.dspecial[dbuf] != 0u;
                 tc_fence_before();
-                mbar_arrive(&ctl.dempty[dbuf]);
-                ++du[dbuf];
-                dbuf ^= 1u;
             }
             if (special || p.tail_nnz) {
                 if (!in_ys) {
-                    zero_ys<NR>(e, et);
-                    named_bar_sync(1, 128);
+#pragma unroll
+                    for (int r = 0; r < NR; ++r) w.ys[r][wt] = 0.f;
                     in_ys = true;
                 }
-                epi_rare<NR>(p, e, bs, be, rbase, nr, special, xb, et);
+                rare_part<NR, PW>(p, w, b, be, rbase, nr, special, xb, wt);
             }
-            if (in_ys) named_bar_sync(1, 128);   // partials written by other warps
 #pragma unroll
             for (int r = 0; r < NR; ++r) {
                 const int32_t row = __shfl_sync(kFullMask, myrow[r / 32], r % 32);
-                if (row >= 0) {
-                    float y = acc[r];
-                    if (in_ys) {
-                        float c = e.ys[0][r][et];
-#pragma unroll
-                        for (int q = 1; q < EpiSmem<NR>::P; ++q) c += e.ys[q][r][et];
-                        y = c + y;
-                    }
-                    __stcs(yb + (int64_t)row * p.K, y);
-                }
+                if (row >= 0) __stcs(yb + (int64_t)row * p.K, in_ys ? w.ys[r][wt] + acc[r] : acc[r]);
             }
-            if (in_ys) named_bar_sync(1, 128);   // partials are zeroed for the next group
+            b = be;
         }
     }
+    // drain: every MMA issued by this worker completes before tensor memory is released
+    if (wt == 0 && ncommit > 0) drain_phase(&w.mma_bar, (ncommit - 1) & 1u);
 }
 
-template <int NR, int PW, int NL>
-__global__ void __launch_bounds__(TcShape<NR, PW, NL>::kThreads, 1) boo_tc_kernel(const TcParams p) {
-    using Shape = TcShape<NR, PW, NL>;
+template <int NR, int PW, int NW>
+__global__ void __launch_bounds__(TcShape<NR, PW, NW>::kThreads, 1) boo_tc_kernel(const TcParams p) {
+    using Shape = TcShape<NR, PW, NW>;
+    using W = WorkerSmem<NR, PW>;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t *tiles = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    EpiSmem<NR> &epi = *reinterpret_cast<EpiSmem<NR> *>(tiles + Shape::kEpiOff);
-    TcCtl<PW, NL> &ctl = *reinterpret_cast<TcCtl<PW, NL> *>(tiles + Shape::kCtlOff);
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    uint8_t *base = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    W *ws = reinterpret_cast<W *>(base);
+    Ctl &ctl = *reinterpret_cast<Ctl *>(base + NW * sizeof(W));
+    const int tid = threadIdx.x, warp = tid >> 5, wk = warp >> 2;
 
     if (tid == 0) {
-        for (int j = 0; j < NL; ++j) {
-            mbar_init(&ctl.full[j], 1);
-            mbar_init(&ctl.empty[j], 1);
-        }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(&ctl.dfull[b], 2);
-            mbar_init(&ctl.dempty[b], 128);
-        }
-        for (int s = 0; s < kDescRing; ++s) {
-            mbar_init(&ctl.descfull[s], 1);
-            mbar_init(&ctl.descempty[s], 1);
-        }
-        for (int s = 0; s < kChunkRing; ++s) {
-            mbar_init(&ctl.chunkfull[s], 1);
-            mbar_init(&ctl.chunkempty[s], 1);
-        }
-        mbar_init(&ctl.fin, 1);
+        for (int k = 0; k < NW; ++k) mbar_init(&ws[k].mma_bar, 1);
         ctl.abort = 0;
         fence_mbar_init();
     }
@@ -949,16 +678,8 @@ __global__ void __launch_bounds__(TcShape<NR, PW, NL>::kThreads, 1) boo_tc_kerne
     tc_fence_after();
     const uint32_t tmem = ctl.tmem_base;
 
-    if (warp == 0) {
-        if (lane == 0) mma_role<NR, PW, NL>(ctl, tmem);
-        __syncwarp();
-    } else if (warp == 1) {
-        meta_role<NR, PW, NL>(p, ctl, lane);
-    } else if (warp >= 4 && warp < 8) {
-        epilogue_role<NR, PW, NL>(p, ctl, epi, tmem, tid - 128);
-    } else if (warp >= 8) {
-        loader_role<NR, PW, NL>(p, ctl, tiles, tmem, (warp - 8) >> 2, tid - 256 - ((warp - 8) >> 2) * 128);
-    }
+    worker<NR, PW>(p, ws[wk], ctl, tmem + (uint32_t)(wk * Shape::kWorkerCols), (int64_t)blockIdx.x * NW + wk,
+                   (int64_t)gridDim.x * NW, tid & 127, 1u + (uint32_t)wk);
 
     tc_fence_before();
     __syncthreads();
@@ -1008,9 +729,9 @@ size_t gather_bytes(const spmm_boo_dev *A, int64_t batch, int64_t K) {
     return (size_t)batch * (size_t)A->n_cg * PW * (size_t)K * sizeof(float);
 }
 
-template <int NR, int PW, int NL>
+template <int NR, int PW, int NW>
 int launch_tc(TcParams p, int64_t batch, void *ws, size_t ws_bytes, cudaStream_t s) {
-    using Shape = TcShape<NR, PW, NL>;
+    using Shape = TcShape<NR, PW, NW>;
     const int sms = sm_count();
     if (sms <= 0) return SPMM_ECUDA;
     const int64_t gather_rows = batch * p.n_cg * (PW / 4);
@@ -1023,15 +744,17 @@ int launch_tc(TcParams p, int64_t batch, void *ws, size_t ws_bytes, cudaStream_t
     }
     p.Xt = (const float4 *)ws;
     p.n_ft = p.K / kFeat;
-    // chunks of consecutive row groups: at least ~4 tasks per CTA, <= 8 groups
-    int64_t c = p.n_rg / (4 * (int64_t)sms * p.n_ft * batch);
+    // chunks of consecutive row groups, small enough for ~16 tasks per worker
+    const int64_t workers = (int64_t)sms * NW;
+    int64_t c = p.n_rg / (16 * workers * p.n_ft * batch);
     c = c < 1 ? 1 : (c > 8 ? 8 : c);
     p.chunk_rgs = (int32_t)c;
     p.n_chunks = ceil_div(p.n_rg, c);
     p.n_tasks = p.n_chunks * p.n_ft * batch;
     if (p.n_tasks > 0x7fffffffLL) return SPMM_EUNSUPPORTED;
-    const int grid = (int)(p.n_tasks < sms ? p.n_tasks : sms);
-    auto kern = boo_tc_kernel<NR, PW, NL>;
+    const int64_t ctas = ceil_div(p.n_tasks, (int64_t)NW);
+    const int grid = (int)(ctas < sms ? ctas : sms);
+    auto kern = boo_tc_kernel<NR, PW, NW>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Shape::kSmem);
     if (e == cudaSuccess && gather_rows > 0) {
         boo_gather_kernel<PW><<<(unsigned)gather_rows, 128, 0, s>>>(p);
@@ -1102,7 +825,7 @@ int boo_matmul_tc(const spmm_boo_dev *A, const float *X, float *Y, int64_t batch
     p.n_cg = A->n_cg;
     p.dense_nnz = kDenseNnz;
     if (A->max_nr <= 32 && A->max_nc <= 32) return launch_tc<32, 32, 4>(p, batch, ws, ws_bytes, s);
-    return launch_tc<64, 64, 1>(p, batch, ws, ws_bytes, s);
+    return launch_tc<64, 64, 2>(p, batch, ws, ws_bytes, s);
 }
 
 }  // namespace spmm
