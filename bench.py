@@ -57,6 +57,9 @@ def parse():
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--gen-kw', default=None,
                     help='JSON overrides of the generator size (reduced cases for profiling)')
+    ap.add_argument('--no-cusparse', action='store_true', help='skip the cuSPARSE reference timing')
+    ap.add_argument('--engine', choices=('auto', 'cuda_cores', 'tensor_cores'), default='auto',
+                    help="units that multiply the BOO blocks (spmm_launch_cfg.engine)")
     ap.add_argument('--split', choices=('features', 'rows'), default='features',
                     help='multi-GPU partitioning (ignored at --gpus 1)')
     return ap.parse_args()
@@ -421,7 +424,7 @@ def native_arm(args):
     y = torch.empty((mat.shape[0], K), dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream(dev)
     sh = stream.cuda_stream
-    lcfg = _lib.launch_cfg('auto')
+    lcfg = _lib.launch_cfg(args.engine)
     ws_bytes = L.spmm_boo_matmul_workspace_size(C.byref(st), 1, K, C.byref(lcfg)) if fmt == 'boo' else 0
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
     lcfg.workspace, lcfg.workspace_bytes = ws.data_ptr(), ws_bytes
@@ -477,17 +480,48 @@ def native_arm(args):
     alg = abytes + xbytes + ybytes
     peak, peak_kind = load_peaks()
     achieved = alg / (ms_step * 1e-3) / 1e9
-    tag = f'{args.config}:{fmt}'
+    engine = 'tc' if ws_bytes else 'cc'
+    tag = f'{args.config}:{fmt}:{engine}'
     traffic = load_traffic(tag)
+    kernel_name = {'tc': 'boo_gather_kernel + boo_tc_kernel (one spmm_boo_matmul call)',
+                   'cc': 'boo_spmm_kernel'}[engine] if fmt == 'boo' else 'pbr_spmm_kernel'
+
+    # cuSPARSE reference point (benchmark only): torch's CSR x dense product on
+    # the same matrix and X, which runs cusparseSpMM
+    cusparse = None
+    if world == 1 and not args.no_cusparse:
+        try:
+            At = torch.sparse_csr_tensor(torch.from_numpy(mat.indptr.astype(np.int32)),
+                                         torch.from_numpy(mat.indices.astype(np.int32)),
+                                         torch.from_numpy(mat.data.astype(np.float32)), size=mat.shape,
+                                         device=dev)
+            for _ in range(3):
+                yc = torch.sparse.mm(At, x)
+            torch.cuda.synchronize(dev)
+            c0 = torch.cuda.Event(enable_timing=True)
+            c1 = torch.cuda.Event(enable_timing=True)
+            nrep = max(5, min(args.steps, 50))
+            c0.record(stream)
+            for _ in range(nrep):
+                yc = torch.sparse.mm(At, x)
+            c1.record(stream)
+            torch.cuda.synchronize(dev)
+            cms = c0.elapsed_time(c1) / nrep
+            cusparse = {'ms_per_step': round(cms, 4), 'value': round(flops_rank / (cms * 1e-3) / 1e9, 3),
+                        'unit': 'GFLOP/s', 'what': 'torch.sparse.mm (cusparseSpMM) on the same CSR, X',
+                        'speedup_of_this': round(cms / ms_step, 3)}
+            del At, yc
+        except Exception as e:   # noqa: BLE001 -- reported, not fatal
+            cusparse = {'unavailable': f'{type(e).__name__}: {e}'[:200]}
 
     # e2e: the public API with host operands (pinned H2D of X, D2H of Y per step)
     x_host = x.cpu().pin_memory()
     for _ in range(2):
-        (S.boo_matmul if fmt == 'boo' else S.pbr_matmul)(A, x_host)
+        (S.boo_matmul(A, x_host, engine=args.engine) if fmt == 'boo' else S.pbr_matmul(A, x_host))
     torch.cuda.synchronize(dev)
     e0 = time.perf_counter()
     for _ in range(args.e2e_steps):
-        yh = (S.boo_matmul if fmt == 'boo' else S.pbr_matmul)(A, x_host)
+        yh = S.boo_matmul(A, x_host, engine=args.engine) if fmt == 'boo' else S.pbr_matmul(A, x_host)
     torch.cuda.synchronize(dev)
     e_s = (time.perf_counter() - e0) / args.e2e_steps
     if world > 1:
@@ -528,7 +562,8 @@ def native_arm(args):
         'roofline': {'bound': 'hbm', 'achieved': round(achieved, 1), 'peak': peak,
                      'unit': 'GB/s', 'frac': round(achieved / peak, 4), 'traffic': traffic,
                      'peak_kind': peak_kind, 'alg_bytes_per_launch': int(alg),
-                     'kernel': 'boo_spmm_kernel' if fmt == 'boo' else 'pbr_spmm_kernel'},
+                     'kernel': kernel_name},
+        'cusparse': cusparse,
         'e2e': e2e, 'gpu_launches': args.steps * launches_per_step,
         'clocks': clocks, 'cpu_baseline': cpu,
     }
