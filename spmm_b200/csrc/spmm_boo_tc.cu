@@ -546,8 +546,20 @@ __device__ void worker(const TcParams &p, WorkerSmem<NR, PW> &w, Ctl &ctl, uint3
 #pragma unroll
                         for (int u = 0; u < kNzPre; ++u)
                             if (wt + 128 * u < n) put(i1[u], v1[u]);
-                        for (int e = wt + 128 * kNzPre; e < n; e += 128)
-                            put(__ldg(p.nz_idx + k0 + e), __ldg(p.nz_val + k0 + e));
+                        // large blocks: the rest in batches of 8 loads in flight
+                        for (int e0 = wt + 128 * kNzPre; e0 < n; e0 += 128 * 8) {
+                            uint16_t ib[8];
+                            float vb[8];
+#pragma unroll
+                            for (int u = 0; u < 8; ++u) {
+                                const int e = e0 + 128 * u;
+                                ib[u] = e < n ? __ldg(p.nz_idx + k0 + e) : (uint16_t)0;
+                                vb[u] = e < n ? __ldg(p.nz_val + k0 + e) : 0.f;
+                            }
+#pragma unroll
+                            for (int u = 0; u < 8; ++u)
+                                if (e0 + 128 * u < n) put(ib[u], vb[u]);
+                        }
                         m = __reduce_or_sync(kFullMask, m);
                         if (lane == 0 && m) atomicOr(&w.kmask[t], m);
                         if (__any_sync(kFullMask, asp) && lane == 0) w.aspecial[t] = 1u;
@@ -558,18 +570,27 @@ __device__ void worker(const TcParams &p, WorkerSmem<NR, PW> &w, Ctl &ctl, uint3
                     tc_fence_after();
                     const uint32_t kmask = w.kmask[t];
                     // 5. split and store the panel: hi at xslot, lo at xslot + PW
-                    bool xsp = false;
+                    // x * 0 is NaN exactly for a non-finite x: one FMA per value
+                    // detects them; the rare panel that has one is cleaned
+                    float chk = 0.f;
+#pragma unroll
+                    for (int ks = 0; ks < KS; ++ks)
+                        if (kmask & (1u << ks))
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) chk = fmaf(x[ks * 8 + e], 0.f, chk);
+                    const bool xsp = chk != chk;
+                    if (xsp) {
+#pragma unroll
+                        for (int c = 0; c < PW; ++c)
+                            if (!finite(x[c])) x[c] = 0.f;
+                    }
 #pragma unroll
                     for (int ks = 0; ks < KS; ++ks) {
                         if (kmask & (1u << ks)) {
                             uint32_t h[8], l[8];
 #pragma unroll
                             for (int e = 0; e < 8; ++e) {
-                                float v = x[ks * 8 + e];
-                                if (!finite(v)) {
-                                    xsp = true;
-                                    v = 0.f;
-                                }
+                                const float v = x[ks * 8 + e];
                                 const float hv = tf32_hi(v);
                                 h[e] = __float_as_uint(hv);
                                 l[e] = __float_as_uint(v - hv);
@@ -690,30 +711,34 @@ __global__ void __launch_bounds__(TcShape<NR, PW, NW>::kThreads, 1) boo_tc_kerne
 }
 
 // Gather pass: Xt[bt][g][q][f] = (X[bt][col 4q..4q+3 of group g][f]) as one
-// float4, zeros past the group's size.  One CTA per (bt, g, q) row of Xt;
-// reads and writes are coalesced over f.  HBM-bound streaming copy.
+// float4, zeros past the group's size.  One CTA per (bt, g): the group's row
+// pointers in shared memory, then each thread writes float4s of two quads at
+// a time (16 X loads in flight per thread at K = 128); reads and writes are
+// coalesced over f.  HBM-bound streaming copy.
 template <int PW>
-__global__ void __launch_bounds__(128) boo_gather_kernel(const TcParams p) {
+__global__ void __launch_bounds__(256) boo_gather_kernel(const TcParams p) {
     constexpr int QW = PW / 4;
-    const int64_t row = blockIdx.x;
-    const int q = (int)(row % QW);
-    const int64_t g = (row / QW) % p.n_cg, bt = row / (QW * p.n_cg);
-    const int32_t cbase = __ldg(p.col_grp_ptr + g);
-    const int32_t nc = __ldg(p.col_grp_ptr + g + 1) - cbase;
-    const float *xr[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int c = 4 * q + i;
-        xr[i] = c < nc ? p.X + (bt * p.cols + __ldg(p.col_ids + cbase + c)) * p.K : nullptr;
+    __shared__ const float *xr[PW];
+    const int64_t g = blockIdx.x % p.n_cg, bt = blockIdx.x / p.n_cg;
+    if (threadIdx.x < PW) {
+        const int32_t cbase = __ldg(p.col_grp_ptr + g);
+        const int32_t nc = __ldg(p.col_grp_ptr + g + 1) - cbase;
+        const int c = threadIdx.x;
+        xr[c] = c < nc ? p.X + (bt * p.cols + __ldg(p.col_ids + cbase + c)) * p.K : nullptr;
     }
-    float4 *out = const_cast<float4 *>(p.Xt) + row * p.K;
-    for (int64_t f = threadIdx.x; f < p.K; f += 128) {
-        float4 v;
-        v.x = xr[0] ? __ldg(xr[0] + f) : 0.f;
-        v.y = xr[1] ? __ldg(xr[1] + f) : 0.f;
-        v.z = xr[2] ? __ldg(xr[2] + f) : 0.f;
-        v.w = xr[3] ? __ldg(xr[3] + f) : 0.f;
-        out[f] = v;
+    __syncthreads();
+    float4 *out = const_cast<float4 *>(p.Xt) + (bt * p.n_cg + g) * QW * p.K;
+#pragma unroll
+    for (int q = threadIdx.x >> 7; q < QW; q += 2) {
+        const float *r0 = xr[4 * q], *r1 = xr[4 * q + 1], *r2 = xr[4 * q + 2], *r3 = xr[4 * q + 3];
+        for (int64_t f = threadIdx.x & 127; f < p.K; f += 128) {
+            float4 v;
+            v.x = r0 ? __ldg(r0 + f) : 0.f;
+            v.y = r1 ? __ldg(r1 + f) : 0.f;
+            v.z = r2 ? __ldg(r2 + f) : 0.f;
+            v.w = r3 ? __ldg(r3 + f) : 0.f;
+            out[q * p.K + f] = v;
+        }
     }
 }
 
@@ -757,7 +782,7 @@ int launch_tc(TcParams p, int64_t batch, void *ws, size_t ws_bytes, cudaStream_t
     auto kern = boo_tc_kernel<NR, PW, NW>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Shape::kSmem);
     if (e == cudaSuccess && gather_rows > 0) {
-        boo_gather_kernel<PW><<<(unsigned)gather_rows, 128, 0, s>>>(p);
+        boo_gather_kernel<PW><<<(unsigned)(batch * p.n_cg), 256, 0, s>>>(p);
         e = cudaGetLastError();
     }
     if (e == cudaSuccess) {

@@ -66,7 +66,7 @@ def test_tc_seeded_sweep(cuda, seed):
     y_tc = _check(mat, boo, x, 'tensor_cores')
     y_cc = _check(mat, boo, x, 'cuda_cores')
     y_auto = _product(boo.to('cuda'), x.cuda(), 'auto').cpu().numpy()
-    dense = boo.max_nr <= 32 and boo.max_nc <= 32 and boo.compressed_nnz() >= 96 * boo.num_blocks()
+    dense = boo.max_nr <= 64 and boo.max_nc <= 64 and boo.compressed_nnz() >= 96 * boo.num_blocks()
     np.testing.assert_array_equal(y_auto, y_tc if dense else y_cc)   # auto's measured crossover
 
 
