@@ -45,6 +45,8 @@ struct BooParams {
     const S *X;
     S *Y;
     int rowmajor;
+    int skip_rem;   // remainder-major: Y already holds the CSR remainder (load-balanced
+                    // kernels ran first); add blocks and tail to it, skip other groups
 };
 
 // first index in a[0..n) with a[i] >= key (a ascending)
@@ -147,6 +149,7 @@ boo_spmm_kernel(const BooParams<S> p) {
     }
     __syncthreads();
     const int64_t blk_lo = sm.blk_lo, blk_hi = sm.blk_hi;
+    if (p.skip_rem && blk_lo == blk_hi && p.tail_nnz == 0) return;   // nothing to add
 
     for (int64_t bt = blockIdx.z; bt < p.batch; bt += gridDim.z) {
         const S *xl = p.X + bt * p.cols * p.K + f0;
@@ -272,8 +275,9 @@ boo_spmm_kernel(const BooParams<S> p) {
                 const int q = g + i * NG;
                 if (q < R) {
                     const int32_t row = p.row_ids[rbase + r0 + q];
-                    accumulate<S, VEC, VPT, LPR, U>(acc[i], p.rem_col, p.rem_val, p.rem_indptr[row],
-                                                    p.rem_indptr[row + 1], xl, p.K, vm);
+                    if (!p.skip_rem)
+                        accumulate<S, VEC, VPT, LPR, U>(acc[i], p.rem_col, p.rem_val, p.rem_indptr[row],
+                                                        p.rem_indptr[row + 1], xl, p.K, vm);
                     if (p.tail_nnz) {
                         const int64_t t0 = lower_bound_i32(p.tail_row, p.tail_nnz, row);
                         const int64_t t1 = lower_bound_i32(p.tail_row, p.tail_nnz, (int64_t)row + 1);
@@ -283,7 +287,14 @@ boo_spmm_kernel(const BooParams<S> p) {
                     S *yr = yb + (int64_t)row * p.K + f0;
 #pragma unroll
                     for (int v = 0; v < VPT; ++v)
-                        if (vm[v]) st_frag<S, VEC>(yr + v * LPR * VEC, acc[i][v]);
+                        if (vm[v]) {
+                            if (p.skip_rem) {   // Y holds the row's remainder sum
+                                const Frag<S, VEC> y0 = ldg_frag<S, VEC>(yr + v * LPR * VEC);
+#pragma unroll
+                                for (int q = 0; q < VEC; ++q) acc[i][v].v[q] = y0.v[q] + acc[i][v].v[q];
+                            }
+                            st_frag<S, VEC>(yr + v * LPR * VEC, acc[i][v]);
+                        }
                 }
             }
         }
@@ -299,6 +310,233 @@ int launch_boo_n(const BooParams<S> &p, int64_t n_rg, cudaStream_t s) {
     boo_spmm_kernel<S, VEC, VPT, LPR><<<grid, kBooThreads, 0, s>>>(p);
     SPMM_LAUNCH_CHECK();
     return SPMM_OK;
+}
+
+// ---- load-balanced CSR remainder ------------------------------------------
+//
+// For matrices whose nonzeros are mostly in the CSR remainder (power-law
+// graphs, uniform random; the reference's remainder kernel,
+// boo_kernel.cu:905-937, runs one thread block per row) rows are skewed: up to
+// tens of thousands of entries next to a median of ~20.  Three launches on the
+// stream, each Y element written once and then updated once at most:
+//   * rem_tile_kernel: warp tiles of 32 consecutive rows dealt round-robin to
+//     all warps; the tile's row pointers in one coalesced load; per row the
+//     (column, value) pairs are fetched 32 at a time by the lanes (the next
+//     row's first chunk while the current row's X rows are in flight) and
+//     broadcast by shuffles, 8 / VPT X rows in flight per warp; stores Y for
+//     every row of at most kLongRow entries (zeros for empty rows);
+//   * rem_long_kernel: a CTA per tile of 256 rows takes every longer row of
+//     its tile; its 8 warps each sum a contiguous eighth of the row and the CTA
+//     adds the 8 partials in warp order and stores Y;
+//   * the block kernel then adds blocks and tail entries into the row groups
+//     that have any (skip_rem).
+// Every result is deterministic.
+constexpr int kLongRow = 1024;
+constexpr int kRemWarps = 8;
+
+// acc += sum over entries [e0, e1) of val * X[col]; (c, v) = this lane's
+// entry e0 + lane (already loaded by the caller).
+template <typename S, int VEC, int VPT>
+__device__ __forceinline__ void rem_span(Frag<S, VEC> (&acc)[VPT], const int32_t *col, const S *val, int64_t e0,
+                                         int64_t e1, int32_t c, S v, const S *xl, int64_t K,
+                                         const bool (&vm)[VPT], int lane) {
+    constexpr int STR = 32 * VEC;
+    constexpr int U = 8 / VPT;   // X rows in flight per warp
+    for (int64_t b = e0; b < e1; b += 32) {
+        if (b != e0) {
+            const int64_t e = b + lane;
+            c = e < e1 ? __ldg(col + e) : 0;
+            v = e < e1 ? __ldg(val + e) : S(0);
+        }
+        const int n = e1 - b < 32 ? (int)(e1 - b) : 32;
+        int j = 0;
+        for (; j + U <= n; j += U) {
+            Frag<S, VEC> x[U][VPT];
+            S a[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int32_t cu = __shfl_sync(kFullMask, c, j + u);
+                a[u] = __shfl_sync(kFullMask, v, j + u);
+                const S *xr = xl + (int64_t)cu * K;
+#pragma unroll
+                for (int q = 0; q < VPT; ++q)
+                    if (vm[q]) x[u][q] = ldg_frag<S, VEC>(xr + q * STR);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+#pragma unroll
+                for (int q = 0; q < VPT; ++q)
+                    if (vm[q])
+#pragma unroll
+                        for (int t = 0; t < VEC; ++t) acc[q].v[t] = fma(a[u], x[u][q].v[t], acc[q].v[t]);
+        }
+        for (; j < n; ++j) {
+            const int32_t cu = __shfl_sync(kFullMask, c, j);
+            const S au = __shfl_sync(kFullMask, v, j);
+            const S *xr = xl + (int64_t)cu * K;
+#pragma unroll
+            for (int q = 0; q < VPT; ++q)
+                if (vm[q]) {
+                    const Frag<S, VEC> x = ldg_frag<S, VEC>(xr + q * STR);
+#pragma unroll
+                    for (int t = 0; t < VEC; ++t) acc[q].v[t] = fma(au, x.v[t], acc[q].v[t]);
+                }
+        }
+    }
+}
+
+template <typename S, int VEC, int VPT>
+__device__ __forceinline__ void rem_store_row(S *yr, const Frag<S, VEC> (&acc)[VPT], const bool (&vm)[VPT]) {
+    constexpr int STR = 32 * VEC;
+#pragma unroll
+    for (int q = 0; q < VPT; ++q)
+        if (vm[q]) st_frag<S, VEC>(yr + q * STR, acc[q]);
+}
+
+template <typename S, int VEC, int VPT>
+__global__ void __launch_bounds__(32 * kRemWarps, 2) rem_tile_kernel(const BooParams<S> p) {
+    constexpr int SLAB = 32 * VPT * VEC;
+    const int lane = threadIdx.x & 31;
+    const int64_t f0 = (int64_t)blockIdx.y * SLAB + (int64_t)lane * VEC;
+    bool vm[VPT];
+#pragma unroll
+    for (int q = 0; q < VPT; ++q) vm[q] = f0 + (int64_t)q * 32 * VEC < p.K;
+    const int64_t nwarps = (int64_t)gridDim.x * kRemWarps;
+    const int64_t ntiles = (p.rows + 31) / 32;
+    for (int64_t bt = blockIdx.z; bt < p.batch; bt += gridDim.z) {
+        const S *xl = p.X + bt * p.cols * p.K + f0;
+        S *yb = p.Y + bt * p.rows * p.K + f0;
+        for (int64_t t = (int64_t)blockIdx.x * kRemWarps + (threadIdx.x >> 5); t < ntiles; t += nwarps) {
+            const int64_t r0 = t * 32;
+            const int nrow = p.rows - r0 < 32 ? (int)(p.rows - r0) : 32;
+            // row pointers of the tile: lane l holds rows r0 + l's [e0, e1)
+            const int64_t me0 = lane < nrow ? (int64_t)__ldg(p.rem_indptr + r0 + lane) : 0;
+            const int64_t me1 = lane < nrow ? (int64_t)__ldg(p.rem_indptr + r0 + lane + 1) : 0;
+            // first chunk of the first row
+            int64_t e0 = __shfl_sync(kFullMask, me0, 0), e1 = __shfl_sync(kFullMask, me1, 0);
+            int32_t c = e0 + lane < e1 ? __ldg(p.rem_col + e0 + lane) : 0;
+            S v = e0 + lane < e1 ? __ldg(p.rem_val + e0 + lane) : S(0);
+            for (int j = 0; j < nrow; ++j) {
+                // the next row's first chunk, loaded while this row runs
+                int64_t n0 = 0, n1 = 0;
+                int32_t nc = 0;
+                S nv = S(0);
+                if (j + 1 < nrow) {
+                    n0 = __shfl_sync(kFullMask, me0, j + 1);
+                    n1 = __shfl_sync(kFullMask, me1, j + 1);
+                    if (n1 - n0 <= kLongRow && n0 + lane < n1) {
+                        nc = __ldg(p.rem_col + n0 + lane);
+                        nv = __ldg(p.rem_val + n0 + lane);
+                    }
+                }
+                if (e1 - e0 <= kLongRow) {   // longer rows: rem_long_kernel
+                    Frag<S, VEC> acc[VPT];
+#pragma unroll
+                    for (int q = 0; q < VPT; ++q)
+#pragma unroll
+                        for (int u = 0; u < VEC; ++u) acc[q].v[u] = S(0);
+                    rem_span<S, VEC, VPT>(acc, p.rem_col, p.rem_val, e0, e1, c, v, xl, p.K, vm, lane);
+                    rem_store_row<S, VEC, VPT>(yb + (r0 + j) * p.K, acc, vm);
+                }
+                e0 = n0;
+                e1 = n1;
+                c = nc;
+                v = nv;
+            }
+        }
+    }
+}
+
+template <typename S, int VEC, int VPT>
+__global__ void __launch_bounds__(32 * kRemWarps, 2) rem_long_kernel(const BooParams<S> p) {
+    constexpr int SLAB = 32 * VPT * VEC;
+    __shared__ Frag<S, VEC> part[kRemWarps][VPT][32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t f0 = (int64_t)blockIdx.y * SLAB + (int64_t)lane * VEC;
+    bool vm[VPT];
+#pragma unroll
+    for (int q = 0; q < VPT; ++q) vm[q] = f0 + (int64_t)q * 32 * VEC < p.K;
+    const int64_t r0 = (int64_t)blockIdx.x * 32 * kRemWarps;
+    const int64_t myrow = r0 + threadIdx.x;
+    const bool is_long = myrow < p.rows &&
+                         __ldg(p.rem_indptr + myrow + 1) - __ldg(p.rem_indptr + myrow) > kLongRow;
+    if (!__syncthreads_or(is_long)) return;
+    for (int64_t bt = blockIdx.z; bt < p.batch; bt += gridDim.z) {
+        const S *xl = p.X + bt * p.cols * p.K + f0;
+        S *yb = p.Y + bt * p.rows * p.K + f0;
+        for (int64_t row = r0; row < r0 + 32 * kRemWarps && row < p.rows; ++row) {
+            const int64_t e0 = __ldg(p.rem_indptr + row), e1 = __ldg(p.rem_indptr + row + 1);
+            if (e1 - e0 <= kLongRow) continue;
+            // warp w: entries [e0 + w*len/8, e0 + (w+1)*len/8)
+            const int64_t len = e1 - e0;
+            const int64_t a = e0 + len * warp / kRemWarps, b = e0 + len * (warp + 1) / kRemWarps;
+            Frag<S, VEC> acc[VPT];
+#pragma unroll
+            for (int q = 0; q < VPT; ++q)
+#pragma unroll
+                for (int t = 0; t < VEC; ++t) acc[q].v[t] = S(0);
+            const int32_t c = a + lane < b ? __ldg(p.rem_col + a + lane) : 0;
+            const S v = a + lane < b ? __ldg(p.rem_val + a + lane) : S(0);
+            rem_span<S, VEC, VPT>(acc, p.rem_col, p.rem_val, a, b, c, v, xl, p.K, vm, lane);
+#pragma unroll
+            for (int q = 0; q < VPT; ++q) part[warp][q][lane] = acc[q];
+            __syncthreads();
+            if (warp == 0) {
+#pragma unroll
+                for (int q = 0; q < VPT; ++q) {
+                    Frag<S, VEC> t = part[0][q][lane];
+#pragma unroll
+                    for (int w = 1; w < kRemWarps; ++w)
+#pragma unroll
+                        for (int u = 0; u < VEC; ++u) t.v[u] += part[w][q][lane].v[u];
+                    acc[q] = t;
+                }
+                rem_store_row<S, VEC, VPT>(yb + row * p.K, acc, vm);
+            }
+            __syncthreads();
+        }
+    }
+}
+
+template <typename S, int VEC, int VPT>
+int launch_rem(const BooParams<S> &p, cudaStream_t s) {
+    constexpr int SLAB = 32 * VPT * VEC;
+    const int64_t slabs = ceil_div(p.K, SLAB);
+    if (slabs > 65535) return SPMM_EUNSUPPORTED;
+    int dev = 0, sms = 0;
+    SPMM_CUDA_TRY(cudaGetDevice(&dev));
+    SPMM_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const unsigned bz = (unsigned)(p.batch < 65535 ? p.batch : 65535);
+    const int64_t tile_ctas = ceil_div(ceil_div(p.rows, (int64_t)32), (int64_t)kRemWarps);
+    const int64_t g1 = tile_ctas < (int64_t)sms * 8 ? tile_ctas : (int64_t)sms * 8;
+    rem_tile_kernel<S, VEC, VPT><<<dim3((unsigned)g1, (unsigned)slabs, bz), 32 * kRemWarps, 0, s>>>(p);
+    SPMM_LAUNCH_CHECK();
+    const int64_t g2 = ceil_div(p.rows, (int64_t)(32 * kRemWarps));
+    if (g2 > 0x7fffffffLL) return SPMM_EUNSUPPORTED;
+    rem_long_kernel<S, VEC, VPT><<<dim3((unsigned)g2, (unsigned)slabs, bz), 32 * kRemWarps, 0, s>>>(p);
+    SPMM_LAUNCH_CHECK();
+    return SPMM_OK;
+}
+
+template <typename S>
+int rem_dispatch(const BooParams<S> &p, bool aligned, cudaStream_t s);
+
+template <>
+int rem_dispatch<float>(const BooParams<float> &p, bool aligned, cudaStream_t s) {
+    if (aligned && p.K % 4 == 0) {
+        if (p.K <= 128) return launch_rem<float, 4, 1>(p, s);
+        return launch_rem<float, 4, 2>(p, s);
+    }
+    return launch_rem<float, 1, 4>(p, s);
+}
+
+template <>
+int rem_dispatch<double>(const BooParams<double> &p, bool aligned, cudaStream_t s) {
+    if (aligned && p.K % 2 == 0) {
+        if (p.K <= 64) return launch_rem<double, 2, 1>(p, s);
+        return launch_rem<double, 2, 2>(p, s);
+    }
+    return launch_rem<double, 1, 4>(p, s);
 }
 
 template <typename S>
@@ -334,16 +572,21 @@ int boo_dispatch<double>(const BooParams<double> &p, int64_t n_rg, bool aligned,
     return launch_boo_n<double, 1, 4, 32>(p, n_rg, s);
 }
 
+// AUTO: the tensor-core kernel wins (measured on B200) when blocks (up to
+// 64 x 64) hold on average >= 96 nonzeros: FEM 786k rows 1.83 vs 4.28 ms, 4096
+// dense 64 x 64 blocks at K = 512 1.82 vs 3.12 ms; a 2-D Laplacian (~53 per
+// block) stays on CUDA cores (0.105 vs 0.130 ms).
+bool tc_selected(const spmm_boo_dev *A, int engine) {
+    if (A->scalar_type != SPMM_F32 || engine == SPMM_ENGINE_CUDA_CORES) return false;
+    if (engine == SPMM_ENGINE_TENSOR_CORES) return true;
+    return A->max_nr <= 64 && A->max_nc <= 64 && A->nb > 0 && A->nnz_c >= 96 * A->nb;
+}
+
 template <typename S>
 int boo_matmul_impl(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch, int64_t K, int engine,
                     const spmm_launch_cfg *cfg, cudaStream_t s) {
     if constexpr (sizeof(S) == 4) {
-        // AUTO: the tensor-core kernel wins (measured on B200) when blocks
-        // (up to 64 x 64) hold on average >= 96 nonzeros: FEM 786k rows 1.87 vs
-        // 4.28 ms, 4096 dense 64 x 64 blocks at K = 512 1.83 vs 3.13 ms; a 2-D
-        // Laplacian (~53 per block) stays on CUDA cores (0.105 vs 0.130 ms).
-        const bool tc_auto = A->max_nr <= 64 && A->max_nc <= 64 && A->nb > 0 && A->nnz_c >= 96 * A->nb;
-        if (engine == SPMM_ENGINE_TENSOR_CORES || (engine == SPMM_ENGINE_AUTO && tc_auto)) {
+        if (tc_selected(A, engine)) {
             const int rc = boo_matmul_tc(A, (const float *)X, (float *)Y, batch, K, cfg ? cfg->workspace : nullptr,
                                          cfg ? (size_t)cfg->workspace_bytes : 0, s);
             if (rc != SPMM_EUNSUPPORTED || engine == SPMM_ENGINE_TENSOR_CORES) return rc;
@@ -378,7 +621,14 @@ int boo_matmul_impl(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch
     p.Y = (S *)Y;
     p.rowmajor = A->nz_order == SPMM_BOO_ROWMAJOR;
     const uintptr_t mis = ((uintptr_t)X | (uintptr_t)Y) & 15;
-    return boo_dispatch<S>(p, A->n_rg, mis == 0, s);
+    // remainder-major matrices: the load-balanced remainder kernels write Y,
+    // then the block kernel adds blocks and tail where a row group has any
+    p.skip_rem = A->rem_nnz > 0 && 2 * A->rem_nnz >= A->total_nnz;
+    if (p.skip_rem) {
+        const int rc = rem_dispatch<S>(p, mis == 0, s);   // Y = remainder (every row)
+        if (rc != SPMM_OK) return rc;
+    }
+    return boo_dispatch<S>(p, A->n_rg, mis == 0, s);      // (+)= blocks and tail
 }
 
 }  // namespace
@@ -412,6 +662,7 @@ extern "C" int spmm_boo_matmul(const spmm_boo_dev *A, const void *X, void *Y, in
 extern "C" size_t spmm_boo_matmul_workspace_size(const spmm_boo_dev *A, int64_t batch, int64_t K,
                                                  const spmm_launch_cfg *cfg) {
     if (!A || batch <= 0 || K <= 0 || A->scalar_type != SPMM_F32) return 0;
-    if (cfg && (cfg->version != 1 || cfg->engine == SPMM_ENGINE_CUDA_CORES)) return 0;
+    if (cfg && cfg->version != 1) return 0;
+    if (!tc_selected(A, cfg ? cfg->engine : SPMM_ENGINE_AUTO)) return 0;
     return boo_tc_workspace(A, batch, K);
 }

@@ -1,0 +1,69 @@
+"""Remainder-major BOO products (the load-balanced remainder kernels) against
+the oracle: skewed rows (including rows longer than the 1,024-entry long-row
+threshold), fp32 and fp64, vector and scalar K, batched X, tail entries."""
+
+import numpy as np
+import pytest
+import scipy.sparse as sp
+import torch
+
+import spmm_b200 as S
+from oracle import oracle as O
+from tests.conftest import TOL, abs_bound, assert_spmm_close
+
+pytestmark = pytest.mark.gpu
+
+
+def _skewed(rows, cols, seed, dtype, long_rows=(0, 7, 300), long_len=3000):
+    rng = np.random.default_rng(seed)
+    lens = np.minimum(rng.zipf(2.0, rows), 200)
+    for r in long_rows:
+        if r < rows:
+            lens[r] = min(long_len, cols)
+    indptr = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
+    indices = np.concatenate([np.sort(rng.choice(cols, n, replace=False)) for n in lens]).astype(np.int64)
+    data = rng.standard_normal(indptr[-1]).astype(dtype)
+    return sp.csr_matrix((data, indices, indptr), shape=(rows, cols))
+
+
+def _check(mat, boo, x):
+    got = S.boo_matmul(boo.to('cuda'), x.cuda()).cpu().numpy()
+    d = {f: getattr(boo, f) for f in O.BOO_FIELDS}
+    d.update(rows=boo.rows, cols=boo.cols)
+    xn = x.numpy()
+    ref = O.boo_matmul(d, xn)
+    assert_spmm_close(got, ref, abs_bound(mat.indptr, mat.indices, mat.data, xn), TOL[np.dtype(mat.dtype)])
+
+
+@pytest.mark.parametrize('dtype', [np.float32, np.float64])
+@pytest.mark.parametrize('k', [1, 7, 64, 128, 256, 300])
+def test_remainder_major_skewed_rows(cuda, dtype, k):
+    mat = _skewed(1200, 5000, 11 + k, dtype)
+    boo = S.csr_to_boo(mat, cluster="identity", target_nr=32, target_nc=32, small_block_threshold=64)
+    assert 2 * boo.remainder_nnz() >= boo.total_nnz       # the remainder-major path
+    assert np.diff(boo.rem_indptr).max() > 1024           # long rows present
+    tdt = torch.float32 if dtype == np.float32 else torch.float64
+    x = torch.from_numpy(np.random.default_rng(k).standard_normal((2, 5000, k))).to(tdt)
+    _check(mat, boo, x)
+
+
+@pytest.mark.parametrize('policy', ['remainder', 'tail_batch'])
+def test_remainder_major_with_blocks_and_tail(cuda, policy):
+    rng = np.random.default_rng(5)
+    skew = _skewed(640, 2048, 3, np.float32, long_rows=(1, 600), long_len=1500)
+    dense = sp.random(640, 2048, density=0.002, format='csr', random_state=1, dtype=np.float32)
+    dense[:64, :64] = rng.standard_normal((64, 64)).astype(np.float32)   # a few kept blocks
+    mat = (skew + dense).tocsr()
+    mat.sort_indices()
+    boo = S.csr_to_boo(mat, cluster='identity', target_nr=32, target_nc=32,
+                       small_block_policy=policy, small_block_threshold=8)
+    assert boo.num_blocks() > 0
+    x = torch.from_numpy(rng.standard_normal((2048, 96)).astype(np.float32))
+    _check(mat, boo, x)
+
+
+def test_remainder_major_deterministic(cuda):
+    mat = _skewed(900, 3000, 8, np.float32)
+    boo = S.csr_to_boo(mat, cluster='identity', target_nr=32, target_nc=32).to('cuda')
+    x = torch.randn(3000, 256, generator=torch.Generator().manual_seed(0)).cuda()
+    assert torch.equal(S.boo_matmul(boo, x), S.boo_matmul(boo, x))
