@@ -60,6 +60,9 @@ def parse():
     ap.add_argument('--no-cusparse', action='store_true', help='skip the cuSPARSE reference timing')
     ap.add_argument('--engine', choices=('auto', 'cuda_cores', 'tensor_cores'), default='auto',
                     help="units that multiply the BOO blocks (spmm_launch_cfg.engine)")
+    ap.add_argument('--slab-features', type=int, default=0,
+                    help='features per pass of the remainder kernels (spmm_launch_cfg.slab_features; '
+                         '0 = auto, <0 = full width)')
     ap.add_argument('--split', choices=('features', 'rows'), default='features',
                     help='multi-GPU partitioning (ignored at --gpus 1)')
     return ap.parse_args()
@@ -424,11 +427,10 @@ def native_arm(args):
     y = torch.empty((mat.shape[0], K), dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream(dev)
     sh = stream.cuda_stream
-    lcfg = _lib.launch_cfg(args.engine)
+    lcfg = _lib.launch_cfg(args.engine, slab_features=args.slab_features)
     ws_bytes = L.spmm_boo_matmul_workspace_size(C.byref(st), 1, K, C.byref(lcfg)) if fmt == 'boo' else 0
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
     lcfg.workspace, lcfg.workspace_bytes = ws.data_ptr(), ws_bytes
-    launches_per_step = 2 if ws_bytes else 1   # gather pass + tensor-core product, or one kernel
 
     def launch():
         rc = fn(C.byref(st), x.data_ptr(), y.data_ptr(), 1, K, C.byref(lcfg), sh)
@@ -454,10 +456,12 @@ def native_arm(args):
     torch.cuda.synchronize(dev)
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
+    n_launch0 = L.spmm_product_launches()
     ev0.record(stream)
     for _ in range(args.steps):
         launch()
     ev1.record(stream)
+    gpu_launches = int(L.spmm_product_launches() - n_launch0)   # counted by the library
     torch.cuda.synchronize(dev)
     ms = ev0.elapsed_time(ev1)
     if world > 1:
@@ -481,10 +485,14 @@ def native_arm(args):
     peak, peak_kind = load_peaks()
     achieved = alg / (ms_step * 1e-3) / 1e9
     engine = 'tc' if ws_bytes else 'cc'
+    if fmt == 'boo' and engine == 'cc' and 2 * A._sizes['rem_nnz'] >= A._sizes['total_nnz']:
+        engine = 'rem'                                  # remainder-major product
     tag = f'{args.config}:{fmt}:{engine}'
     traffic = load_traffic(tag)
     kernel_name = {'tc': 'boo_gather_kernel + boo_tc_kernel (one spmm_boo_matmul call)',
-                   'cc': 'boo_spmm_kernel'}[engine] if fmt == 'boo' else 'pbr_spmm_kernel'
+                   'cc': 'boo_spmm_kernel',
+                   'rem': 'rem_tile_kernel + rem_long_kernel + boo_spmm_kernel (one spmm_boo_matmul call)',
+                   }[engine] if fmt == 'boo' else 'pbr_spmm_kernel'
 
     # cuSPARSE reference point (benchmark only): torch's CSR x dense product on
     # the same matrix and X, which runs cusparseSpMM
@@ -517,11 +525,11 @@ def native_arm(args):
     # e2e: the public API with host operands (pinned H2D of X, D2H of Y per step)
     x_host = x.cpu().pin_memory()
     for _ in range(2):
-        (S.boo_matmul(A, x_host, engine=args.engine) if fmt == 'boo' else S.pbr_matmul(A, x_host))
+        (S.boo_matmul(A, x_host, engine=args.engine, slab_features=args.slab_features) if fmt == 'boo' else S.pbr_matmul(A, x_host))
     torch.cuda.synchronize(dev)
     e0 = time.perf_counter()
     for _ in range(args.e2e_steps):
-        yh = S.boo_matmul(A, x_host, engine=args.engine) if fmt == 'boo' else S.pbr_matmul(A, x_host)
+        yh = S.boo_matmul(A, x_host, engine=args.engine, slab_features=args.slab_features) if fmt == 'boo' else S.pbr_matmul(A, x_host)
     torch.cuda.synchronize(dev)
     e_s = (time.perf_counter() - e0) / args.e2e_steps
     if world > 1:
@@ -564,7 +572,7 @@ def native_arm(args):
                      'peak_kind': peak_kind, 'alg_bytes_per_launch': int(alg),
                      'kernel': kernel_name},
         'cusparse': cusparse,
-        'e2e': e2e, 'gpu_launches': args.steps * launches_per_step,
+        'e2e': e2e, 'gpu_launches': gpu_launches,
         'clocks': clocks, 'cpu_baseline': cpu,
     }
     print(json.dumps(line), flush=True)

@@ -122,7 +122,10 @@ typedef struct {
  * 58-99) have no counterpart here. */
 typedef struct {
     int32_t version;        /* must be 1 */
-    int32_t slab_features;  /* features per CTA slab (0 = auto) */
+    int32_t slab_features;  /* remainder-major BOO products: features per pass over A
+                             * (<= 0 = full width, the default and the faster on
+                             * B200; > 0 = the widest supported slab not above
+                             * it, 8 / 16 / 32 floats, 4 / 8 / 16 doubles) */
     int32_t engine;         /* enum spmm_engine (BOO product only; PBR ignores it) */
     int32_t reserved;
     void *workspace;        /* optional device scratch of the tensor-core BOO product, */
@@ -223,6 +226,11 @@ size_t spmm_boo_matmul_workspace_size(const spmm_boo_dev *A, int64_t batch, int6
  * stopped early and Y is incomplete).  Synchronises the device; `clear`
  * resets the word.  Returns -1 when the CUDA runtime fails. */
 int spmm_tc_status(int clear);
+
+/* Product kernels (BOO and PBR SpMM, the tensor-core gather pass included)
+ * this library has launched since it was loaded, counted on the host after
+ * each successful launch (no reference counterpart; a measurement aid). */
+uint64_t spmm_product_launches(void);
 
 /* Y = A*X for a PBR matrix (replaces pbr_spmm_cuda_dispatch / pbr_run_into,
  * torch_fast_spdmm/bindings/bindings_kernels.cu:18-123, bound as

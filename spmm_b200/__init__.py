@@ -11,6 +11,7 @@ from .boo import (BOOInfo, BOOMatrixInt32Double, BOOMatrixInt32Float, BOOMatrixI
                   BOOMatrixInt64Float, BooNzOrder, BooSmallBlockPolicy, NZ_ORDERS,
                   SMALL_BLOCK_POLICIES, boo_arena_bytes, boo_info, boo_matmul, boo_to_csr,
                   csr_to_boo)
+from .boo_plan import BOOExecutionPlan, prepare_boo_cuda
 from .clustering import CLUSTER_METHODS, cluster_axes, cluster_axis
 from .pbr import (BlockFillStats, BlockStripeStats, DataOrder, PBRInfo, PBRMatrixInt32Double,
                   PBRMatrixInt32Float, PBRMatrixInt64Double, PBRMatrixInt64Float, csr_to_pbr,
@@ -24,5 +25,5 @@ __all__ = [
     'csr_to_pbr', 'pbr_to_csr', 'pbr_analyze_csr', 'pbr_info', 'PBRInfo', 'BlockFillStats',
     'BlockStripeStats', 'pbr_matmul', 'pbr_batched_matmul_cpu', 'pbr_batched_matmul_cuda',
     'pbr_batched_matmul_chunkcols_cuda', 'pbr_batched_matmul_nnzflat_cuda',
-    'pbr_batched_matmul_variant_cuda',
+    'pbr_batched_matmul_variant_cuda', 'BOOExecutionPlan', 'prepare_boo_cuda',
 ]

@@ -33,7 +33,7 @@ EXPORTS = ('spmm_status_string', 'spmm_abi_version', 'spmm_boo_build_workspace_s
            'spmm_boo_build_analyze', 'spmm_boo_build_emit', 'spmm_boo_build_noalloc',
            'spmm_pbr_build_workspace_size',
            'spmm_pbr_build_analyze', 'spmm_pbr_build_emit', 'spmm_boo_matmul', 'spmm_pbr_matmul',
-           'spmm_tc_status', 'spmm_boo_matmul_workspace_size')
+           'spmm_tc_status', 'spmm_boo_matmul_workspace_size', 'spmm_product_launches')
 
 
 class CsrDev(C.Structure):
@@ -73,10 +73,11 @@ class LaunchCfg(C.Structure):
 ENGINES = {'auto': 0, 'cuda_cores': 1, 'tensor_cores': 2}
 
 
-def launch_cfg(engine: str = 'auto', workspace: int = 0, workspace_bytes: int = 0) -> 'LaunchCfg':
+def launch_cfg(engine: str = 'auto', workspace: int = 0, workspace_bytes: int = 0,
+               slab_features: int = 0) -> 'LaunchCfg':
     if engine not in ENGINES:
         raise ValueError(f"engine must be one of {sorted(ENGINES)}, got {engine!r}")
-    return LaunchCfg(1, 0, ENGINES[engine], 0, workspace or None, workspace_bytes)
+    return LaunchCfg(1, int(slab_features), ENGINES[engine], 0, workspace or None, workspace_bytes)
 
 
 class SpmmError(RuntimeError):
@@ -121,6 +122,8 @@ def lib() -> C.CDLL:
         L.spmm_boo_matmul_workspace_size.restype = C.c_size_t
         L.spmm_tc_status.argtypes = [C.c_int]
         L.spmm_tc_status.restype = C.c_int
+        L.spmm_product_launches.argtypes = []
+        L.spmm_product_launches.restype = C.c_uint64
         for n in ('spmm_boo_build_analyze', 'spmm_boo_build_emit', 'spmm_pbr_build_analyze',
                   'spmm_pbr_build_emit', 'spmm_boo_matmul', 'spmm_pbr_matmul'):
             getattr(L, n).restype = C.c_int

@@ -418,8 +418,8 @@ def boo_to_csr(boo_mat) -> sp.csr_matrix:
 # SpMM
 # ---------------------------------------------------------------------------
 
-def _run_boo(boo_mat, meta, x: torch.Tensor, engine: str = 'auto') -> torch.Tensor:
-    cfg = _lib.launch_cfg(engine)
+def _run_boo(boo_mat, meta, x: torch.Tensor, engine: str = 'auto', slab_features: int = 0) -> torch.Tensor:
+    cfg = _lib.launch_cfg(engine, slab_features=slab_features)
     device = x.device
     with torch.cuda.device(device):
         x3 = x if x.dim() == 3 else x.unsqueeze(0)
@@ -451,13 +451,17 @@ def boo_matmul(boo_mat, x: torch.Tensor, threads: int = 256, p: int = 64,
                csr_mode: int = 0, row_seg: Optional[bool] = None,
                launch_mode: str = 'legacy', execution_plan=None,
                features_per_thread: int = 1,
-               nnzflat_impl: Optional[str] = None, *, engine: str = 'auto') -> torch.Tensor:
+               nnzflat_impl: Optional[str] = None, *, engine: str = 'auto',
+               slab_features: int = 0) -> torch.Tensor:
     """Y = A @ X (boo.py:230-354).
 
     ``engine`` (not in the reference) picks the units that multiply the
     blocks: 'auto' (tensor cores for float32 with K a multiple of 128 and
     blocks up to 64 x 64, else CUDA cores), 'cuda_cores', or 'tensor_cores'
-    (an error where not applicable).
+    (an error where not applicable).  ``slab_features`` (not in the
+    reference) sets the features per pass of the remainder kernels of a
+    remainder-major matrix: 0 or less is full width (the default, faster on
+    B200), a positive value the widest supported slab not above it.
 
     The launch knobs of the reference's sm_86 kernels (``threads``, ``p``,
     ``csr_mode``, ``features_per_thread``, ``nnzflat_impl``, ``launch_mode``)
@@ -478,14 +482,13 @@ def boo_matmul(boo_mat, x: torch.Tensor, threads: int = 256, p: int = 64,
         _BOO_TYPE_MAP[type(boo_mat).__name__][1]]
     if x.dtype != expected_dtype:
         raise TypeError(f'X dtype must match BOO values ({expected_dtype}), got {x.dtype}')
-    if execution_plan is not None:
-        raise NotImplementedError('BOO execution plans are not supported: the fused kernel '
-                                  'needs no size-class buckets or row tables')
+    if execution_plan is not None and not x.is_cuda:
+        raise ValueError('BOO execution plans require CUDA inputs')
     if not x.is_cuda:
         require_cuda('boo_matmul')
         device = default_device()
         meta = boo_mat._staged_on(device)
-        y = _to_host(_run_boo(boo_mat, meta, x.to(device, non_blocking=True), engine), x)
+        y = _to_host(_run_boo(boo_mat, meta, x.to(device, non_blocking=True), engine, slab_features), x)
         return y.squeeze(0) if x.dim() == 2 else y
 
     meta = boo_mat._gpu_meta
@@ -517,7 +520,14 @@ def boo_matmul(boo_mat, x: torch.Tensor, threads: int = 256, p: int = 64,
             raise ValueError('nnzflat (row_seg=False) supports features_per_thread 1 or 2')
         if nnzflat_impl == 'reference' and features_per_thread != 1:
             raise ValueError("nnzflat_impl='reference' is the FPT=1 kernel; use 'template'")
-    y = _run_boo(boo_mat, meta, x, engine)
+    if execution_plan is not None:   # validated as boo.py:334-340; the product needs no tables
+        from .boo_plan import BOOExecutionPlan
+        plan = execution_plan
+        if not isinstance(plan, BOOExecutionPlan) or plan.matrix is not boo_mat or plan.source_meta is not meta:
+            raise ValueError('Execution plan does not match this matrix and its current CUDA staging')
+        if launch_mode != 'auto' or not row_seg or p != plan.p:
+            raise ValueError('Execution plans require launch_mode="auto", row_seg=True and the prepared p')
+    y = _run_boo(boo_mat, meta, x, engine, slab_features)
     return y.squeeze(0) if x.dim() == 2 else y
 
 

@@ -1,5 +1,8 @@
 // abi.cu -- status text and ABI version of the spmm_b200 C interface.
+#include <atomic>
+
 #include "../../include/spmm_b200.h"
+#include "common.cuh"
 
 extern "C" const char *spmm_status_string(int status) {
     switch (status) {
@@ -21,3 +24,10 @@ extern "C" const char *spmm_status_string(int status) {
 }
 
 extern "C" int spmm_abi_version(void) { return 1; }
+
+namespace spmm {
+static std::atomic<uint64_t> g_product_launches{0};
+void note_product_launch() { g_product_launches.fetch_add(1, std::memory_order_relaxed); }
+}  // namespace spmm
+
+extern "C" uint64_t spmm_product_launches(void) { return spmm::g_product_launches.load(std::memory_order_relaxed); }

@@ -26,6 +26,16 @@ constexpr unsigned kFullMask = 0xffffffffu;
         }                                                     \
     } while (0)
 
+// Host-side count of product-kernel launches (spmm_product_launches).
+void note_product_launch();
+
+// SPMM_LAUNCH_CHECK for a product kernel: also counts the launch.
+#define SPMM_PRODUCT_LAUNCHED()      \
+    do {                             \
+        SPMM_LAUNCH_CHECK();         \
+        ::spmm::note_product_launch(); \
+    } while (0)
+
 #define SPMM_TRY(...)              \
     do {                           \
         int _s = (__VA_ARGS__);    \

@@ -308,7 +308,7 @@ int launch_boo_n(const BooParams<S> &p, int64_t n_rg, cudaStream_t s) {
     if (slabs > 65535 || n_rg > 0x7fffffffLL) return SPMM_EUNSUPPORTED;
     dim3 grid((unsigned)n_rg, (unsigned)slabs, (unsigned)(p.batch < 65535 ? p.batch : 65535));
     boo_spmm_kernel<S, VEC, VPT, LPR><<<grid, kBooThreads, 0, s>>>(p);
-    SPMM_LAUNCH_CHECK();
+    SPMM_PRODUCT_LAUNCHED();
     return SPMM_OK;
 }
 
@@ -319,29 +319,41 @@ int launch_boo_n(const BooParams<S> &p, int64_t n_rg, cudaStream_t s) {
 // boo_kernel.cu:905-937, runs one thread block per row) rows are skewed: up to
 // tens of thousands of entries next to a median of ~20.  Three launches on the
 // stream, each Y element written once and then updated once at most:
-//   * rem_tile_kernel: warp tiles of 32 consecutive rows dealt round-robin to
-//     all warps; the tile's row pointers in one coalesced load; per row the
-//     (column, value) pairs are fetched 32 at a time by the lanes (the next
-//     row's first chunk while the current row's X rows are in flight) and
-//     broadcast by shuffles, 8 / VPT X rows in flight per warp; stores Y for
-//     every row of at most kLongRow entries (zeros for empty rows);
-//   * rem_long_kernel: a CTA per tile of 256 rows takes every longer row of
-//     its tile; its 8 warps each sum a contiguous eighth of the row and the CTA
-//     adds the 8 partials in warp order and stores Y;
+//   * the rows of at most kLongRow entries, by one of two kernels:
+//     - rem_tile_kernel (the default): warp tiles of 32
+//       consecutive rows dealt round-robin to all warps; the tile's row
+//       pointers in one coalesced load; per row the (column, value) pairs are
+//       fetched 32 at a time by the lanes (the next row's first chunk while the
+//       current row's X rows are in flight) and broadcast by shuffles, 8 / VPT
+//       X rows in flight per warp;
+//     - rem_slab_kernel (spmm_launch_cfg::slab_features > 0): the same warp tiles, but each
+//       launch slice covers a narrow slab of W features, so the slab of every
+//       X row fits in L2 and the reuse of popular columns hits there (A is read
+//       once per slab).  A group of LPE lanes covers one row's slab; the
+//       warp's 32 / LPE groups take the tile's rows greedily, a group that
+//       finishes a row claiming the next one, so rows of any length share the
+//       warp without padding;
+//     both store Y for every such row (zeros for empty rows);
+//   * rem_long_kernel: a CTA per tile of 512 rows takes every longer row of
+//     its tile; its 16 warps each sum a contiguous sixteenth of the row and the
+//     CTA adds the partials in warp order and stores Y;
 //   * the block kernel then adds blocks and tail entries into the row groups
 //     that have any (skip_rem).
 // Every result is deterministic.
 constexpr int kLongRow = 1024;
-constexpr int kRemWarps = 8;
+constexpr int kRemWarps = 8;    // warps per CTA of the tile kernel
+constexpr int kLongWarps = 16;  // warps sharing one long row, 16 / VPT X rows in flight each
+// resident CTAs per SM of the slab kernel (register budget: LPE X slabs in flight)
+template <int LPE>
+constexpr int slab_blocks() { return LPE >= 8 ? 2 : 4; }
 
 // acc += sum over entries [e0, e1) of val * X[col]; (c, v) = this lane's
 // entry e0 + lane (already loaded by the caller).
-template <typename S, int VEC, int VPT>
+template <typename S, int VEC, int VPT, int U>
 __device__ __forceinline__ void rem_span(Frag<S, VEC> (&acc)[VPT], const int32_t *col, const S *val, int64_t e0,
                                          int64_t e1, int32_t c, S v, const S *xl, int64_t K,
                                          const bool (&vm)[VPT], int lane) {
-    constexpr int STR = 32 * VEC;
-    constexpr int U = 8 / VPT;   // X rows in flight per warp
+    constexpr int STR = 32 * VEC;   // U: X rows in flight per warp
     for (int64_t b = e0; b < e1; b += 32) {
         if (b != e0) {
             const int64_t e = b + lane;
@@ -435,7 +447,7 @@ __global__ void __launch_bounds__(32 * kRemWarps, 2) rem_tile_kernel(const BooPa
                     for (int q = 0; q < VPT; ++q)
 #pragma unroll
                         for (int u = 0; u < VEC; ++u) acc[q].v[u] = S(0);
-                    rem_span<S, VEC, VPT>(acc, p.rem_col, p.rem_val, e0, e1, c, v, xl, p.K, vm, lane);
+                    rem_span<S, VEC, VPT, 8 / VPT>(acc, p.rem_col, p.rem_val, e0, e1, c, v, xl, p.K, vm, lane);
                     rem_store_row<S, VEC, VPT>(yb + (r0 + j) * p.K, acc, vm);
                 }
                 e0 = n0;
@@ -447,16 +459,115 @@ __global__ void __launch_bounds__(32 * kRemWarps, 2) rem_tile_kernel(const BooPa
     }
 }
 
+// Rows of at most kLongRow entries over slab blockIdx.y of W = LPE * VEC
+// features.  Each step a group's lanes hold LPE (column, value) pairs of its
+// row (the next step's pairs are fetched while this step's X slabs are in
+// flight), broadcast them within the group and each fetch LPE X slabs.
+template <typename S, int VEC, int LPE>
+__global__ void __launch_bounds__(32 * kRemWarps, slab_blocks<LPE>()) rem_slab_kernel(const BooParams<S> p) {
+    constexpr int W = LPE * VEC;
+    constexpr int G = 32 / LPE;   // rows in flight per warp
+    __shared__ int32_t sptr[kRemWarps][33];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int lig = lane % LPE, gl = lane - lig;   // lane in group, group's first lane
+    const unsigned before = (1u << gl) - 1u;       // lanes of the groups before this one
+    const int64_t f0 = (int64_t)blockIdx.y * W + (int64_t)lig * VEC;
+    const bool fm = f0 < p.K;
+    int32_t *sp = sptr[warp];
+    const int64_t nwarps = (int64_t)gridDim.x * kRemWarps;
+    const int64_t ntiles = (p.rows + 31) / 32;
+    for (int64_t bt = blockIdx.z; bt < p.batch; bt += gridDim.z) {
+        const S *xl = p.X + bt * p.cols * p.K + f0;
+        S *yb = p.Y + bt * p.rows * p.K + f0;
+        for (int64_t t = (int64_t)blockIdx.x * kRemWarps + warp; t < ntiles; t += nwarps) {
+            const int64_t r0 = t * 32;
+            const int nrow = p.rows - r0 < 32 ? (int)(p.rows - r0) : 32;
+            __syncwarp();
+            if (lane < nrow) sp[lane] = __ldg(p.rem_indptr + r0 + lane);
+            if (lane == 0) sp[nrow] = __ldg(p.rem_indptr + r0 + nrow);
+            __syncwarp();
+            int row = 0, next = G;
+            int64_t e = 0, eend = 0;
+            bool keep = false;   // false: empty slot, or a long row (rem_long_kernel stores it)
+            auto open = [&](int r) {
+                row = r;
+                e = eend = 0;
+                keep = false;
+                if (r < nrow) {
+                    e = sp[r];
+                    eend = sp[r + 1];
+                    keep = eend - e <= kLongRow;
+                    if (!keep) e = eend;
+                }
+            };
+            open(gl / LPE);
+            int32_t c = 0;
+            S v = S(0);
+            if (e + lig < eend) {
+                c = __ldg(p.rem_col + e + lig);
+                v = __ldg(p.rem_val + e + lig);
+            }
+            Frag<S, VEC> acc;
+#pragma unroll
+            for (int q = 0; q < VEC; ++q) acc.v[q] = S(0);
+            while (__any_sync(kFullMask, row < nrow)) {
+                int32_t cn = 0;
+                S vn = S(0);
+                if (e + LPE + lig < eend) {
+                    cn = __ldg(p.rem_col + e + LPE + lig);
+                    vn = __ldg(p.rem_val + e + LPE + lig);
+                }
+                Frag<S, VEC> x[LPE];
+                S a[LPE];
+#pragma unroll
+                for (int u = 0; u < LPE; ++u) {
+                    const int32_t cu = __shfl_sync(kFullMask, c, gl + u);
+                    a[u] = __shfl_sync(kFullMask, v, gl + u);
+                    if (fm && e + u < eend) {
+                        x[u] = ldg_frag<S, VEC>(xl + (int64_t)cu * p.K);
+                    } else {
+#pragma unroll
+                        for (int q = 0; q < VEC; ++q) x[u].v[q] = S(0);
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < LPE; ++u)
+#pragma unroll
+                    for (int q = 0; q < VEC; ++q) acc.v[q] = fma(a[u], x[u].v[q], acc.v[q]);
+                e += LPE;
+                const bool fin = row < nrow && e >= eend;
+                if (fin && keep && fm) st_frag<S, VEC>(yb + (r0 + row) * p.K, acc);
+                const unsigned fb = __ballot_sync(kFullMask, fin && lig == 0);
+                if (fin) {
+#pragma unroll
+                    for (int q = 0; q < VEC; ++q) acc.v[q] = S(0);
+                    open(next + __popc(fb & before));
+                    c = 0;
+                    v = S(0);
+                    if (e + lig < eend) {
+                        c = __ldg(p.rem_col + e + lig);
+                        v = __ldg(p.rem_val + e + lig);
+                    }
+                } else {
+                    c = cn;
+                    v = vn;
+                }
+                next += __popc(fb);
+            }
+        }
+    }
+}
+
 template <typename S, int VEC, int VPT>
-__global__ void __launch_bounds__(32 * kRemWarps, 2) rem_long_kernel(const BooParams<S> p) {
+__global__ void __launch_bounds__(32 * kLongWarps, 1) rem_long_kernel(const BooParams<S> p) {
     constexpr int SLAB = 32 * VPT * VEC;
-    __shared__ Frag<S, VEC> part[kRemWarps][VPT][32];
+    __shared__ Frag<S, VEC> part[kLongWarps][VPT][32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int64_t f0 = (int64_t)blockIdx.y * SLAB + (int64_t)lane * VEC;
     bool vm[VPT];
 #pragma unroll
     for (int q = 0; q < VPT; ++q) vm[q] = f0 + (int64_t)q * 32 * VEC < p.K;
-    const int64_t r0 = (int64_t)blockIdx.x * 32 * kRemWarps;
+    const int64_t r0 = (int64_t)blockIdx.x * 32 * kLongWarps;
     const int64_t myrow = r0 + threadIdx.x;
     const bool is_long = myrow < p.rows &&
                          __ldg(p.rem_indptr + myrow + 1) - __ldg(p.rem_indptr + myrow) > kLongRow;
@@ -464,12 +575,12 @@ __global__ void __launch_bounds__(32 * kRemWarps, 2) rem_long_kernel(const BooPa
     for (int64_t bt = blockIdx.z; bt < p.batch; bt += gridDim.z) {
         const S *xl = p.X + bt * p.cols * p.K + f0;
         S *yb = p.Y + bt * p.rows * p.K + f0;
-        for (int64_t row = r0; row < r0 + 32 * kRemWarps && row < p.rows; ++row) {
+        for (int64_t row = r0; row < r0 + 32 * kLongWarps && row < p.rows; ++row) {
             const int64_t e0 = __ldg(p.rem_indptr + row), e1 = __ldg(p.rem_indptr + row + 1);
             if (e1 - e0 <= kLongRow) continue;
-            // warp w: entries [e0 + w*len/8, e0 + (w+1)*len/8)
+            // warp w: entries [e0 + w*len/W, e0 + (w+1)*len/W)
             const int64_t len = e1 - e0;
-            const int64_t a = e0 + len * warp / kRemWarps, b = e0 + len * (warp + 1) / kRemWarps;
+            const int64_t a = e0 + len * warp / kLongWarps, b = e0 + len * (warp + 1) / kLongWarps;
             Frag<S, VEC> acc[VPT];
 #pragma unroll
             for (int q = 0; q < VPT; ++q)
@@ -477,7 +588,7 @@ __global__ void __launch_bounds__(32 * kRemWarps, 2) rem_long_kernel(const BooPa
                 for (int t = 0; t < VEC; ++t) acc[q].v[t] = S(0);
             const int32_t c = a + lane < b ? __ldg(p.rem_col + a + lane) : 0;
             const S v = a + lane < b ? __ldg(p.rem_val + a + lane) : S(0);
-            rem_span<S, VEC, VPT>(acc, p.rem_col, p.rem_val, a, b, c, v, xl, p.K, vm, lane);
+            rem_span<S, VEC, VPT, 16 / VPT>(acc, p.rem_col, p.rem_val, a, b, c, v, xl, p.K, vm, lane);
 #pragma unroll
             for (int q = 0; q < VPT; ++q) part[warp][q][lane] = acc[q];
             __syncthreads();
@@ -486,7 +597,7 @@ __global__ void __launch_bounds__(32 * kRemWarps, 2) rem_long_kernel(const BooPa
                 for (int q = 0; q < VPT; ++q) {
                     Frag<S, VEC> t = part[0][q][lane];
 #pragma unroll
-                    for (int w = 1; w < kRemWarps; ++w)
+                    for (int w = 1; w < kLongWarps; ++w)
 #pragma unroll
                         for (int u = 0; u < VEC; ++u) t.v[u] += part[w][q][lane].v[u];
                     acc[q] = t;
@@ -498,8 +609,39 @@ __global__ void __launch_bounds__(32 * kRemWarps, 2) rem_long_kernel(const BooPa
     }
 }
 
+// Slab width of the remainder pass: 0 for full-width tiles, else W features
+// per launch slice (W = LPE * VEC, LPE in {2, 4, 8}), the widest not above
+// spmm_launch_cfg::slab_features.  Full width unless asked: on B200 the narrow
+// slabs lose for every remainder-major shape measured (power-law 2M x 2M,
+// K = 256: 12.1 ms full width, 22-24 ms at W = 16 / 32, 52 ms at W = 8) --
+// a slab of a row-major X fills half an L2 line, so the X slabs do not stay
+// resident (L2 hit rate 37% against 20%), and the K / W times more memory
+// requests leave the kernel latency-bound.
+template <typename S, int VEC>
+int rem_slab_width(const BooParams<S> &p, int requested) {
+    if (p.K % VEC || requested <= 0) return 0;
+    int w = 0;
+    for (int lpe = 8; lpe >= 2; lpe >>= 1)
+        if (!w && lpe * VEC <= requested) w = lpe * VEC;
+    return w < p.K ? w : 0;
+}
+
+template <typename S, int VEC, int LPE>
+int launch_rem_slab(const BooParams<S> &p, int sms, unsigned bz, cudaStream_t s) {
+    const int64_t slabs = ceil_div(p.K, (int64_t)(LPE * VEC));
+    if (slabs > 65535) return SPMM_EUNSUPPORTED;
+    const int64_t tile_ctas = ceil_div(ceil_div(p.rows, (int64_t)32), (int64_t)kRemWarps);
+    const int64_t cap = (int64_t)sms * slab_blocks<LPE>() * 2;
+    const int64_t g1 = tile_ctas < cap ? tile_ctas : cap;
+    rem_slab_kernel<S, VEC, LPE><<<dim3((unsigned)g1, (unsigned)slabs, bz), 32 * kRemWarps, 0, s>>>(p);
+    SPMM_PRODUCT_LAUNCHED();
+    return SPMM_OK;
+}
+
+// Rows of at most kLongRow entries in slabs of `slab_w` features (0: full
+// width, 32 * VPT * VEC per slice), then the long rows at full width.
 template <typename S, int VEC, int VPT>
-int launch_rem(const BooParams<S> &p, cudaStream_t s) {
+int launch_rem(const BooParams<S> &p, int slab_w, cudaStream_t s) {
     constexpr int SLAB = 32 * VPT * VEC;
     const int64_t slabs = ceil_div(p.K, SLAB);
     if (slabs > 65535) return SPMM_EUNSUPPORTED;
@@ -507,36 +649,53 @@ int launch_rem(const BooParams<S> &p, cudaStream_t s) {
     SPMM_CUDA_TRY(cudaGetDevice(&dev));
     SPMM_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const unsigned bz = (unsigned)(p.batch < 65535 ? p.batch : 65535);
-    const int64_t tile_ctas = ceil_div(ceil_div(p.rows, (int64_t)32), (int64_t)kRemWarps);
-    const int64_t g1 = tile_ctas < (int64_t)sms * 8 ? tile_ctas : (int64_t)sms * 8;
-    rem_tile_kernel<S, VEC, VPT><<<dim3((unsigned)g1, (unsigned)slabs, bz), 32 * kRemWarps, 0, s>>>(p);
-    SPMM_LAUNCH_CHECK();
-    const int64_t g2 = ceil_div(p.rows, (int64_t)(32 * kRemWarps));
+    bool slabbed = false;
+    if constexpr (VEC > 1) {
+        slabbed = true;
+        if (slab_w == 8 * VEC) {
+            SPMM_TRY(launch_rem_slab<S, VEC, 8>(p, sms, bz, s));
+        } else if (slab_w == 4 * VEC) {
+            SPMM_TRY(launch_rem_slab<S, VEC, 4>(p, sms, bz, s));
+        } else if (slab_w == 2 * VEC) {
+            SPMM_TRY(launch_rem_slab<S, VEC, 2>(p, sms, bz, s));
+        } else {
+            slabbed = false;
+        }
+    }
+    if (!slabbed) {
+        const int64_t tile_ctas = ceil_div(ceil_div(p.rows, (int64_t)32), (int64_t)kRemWarps);
+        const int64_t g1 = tile_ctas < (int64_t)sms * 8 ? tile_ctas : (int64_t)sms * 8;
+        rem_tile_kernel<S, VEC, VPT><<<dim3((unsigned)g1, (unsigned)slabs, bz), 32 * kRemWarps, 0, s>>>(p);
+        SPMM_PRODUCT_LAUNCHED();
+    }
+    const int64_t g2 = ceil_div(p.rows, (int64_t)(32 * kLongWarps));
     if (g2 > 0x7fffffffLL) return SPMM_EUNSUPPORTED;
-    rem_long_kernel<S, VEC, VPT><<<dim3((unsigned)g2, (unsigned)slabs, bz), 32 * kRemWarps, 0, s>>>(p);
-    SPMM_LAUNCH_CHECK();
+    rem_long_kernel<S, VEC, VPT><<<dim3((unsigned)g2, (unsigned)slabs, bz), 32 * kLongWarps, 0, s>>>(p);
+    SPMM_PRODUCT_LAUNCHED();
     return SPMM_OK;
 }
 
 template <typename S>
-int rem_dispatch(const BooParams<S> &p, bool aligned, cudaStream_t s);
+int rem_dispatch(const BooParams<S> &p, bool aligned, int slab_req, cudaStream_t s);
 
 template <>
-int rem_dispatch<float>(const BooParams<float> &p, bool aligned, cudaStream_t s) {
+int rem_dispatch<float>(const BooParams<float> &p, bool aligned, int slab_req, cudaStream_t s) {
     if (aligned && p.K % 4 == 0) {
-        if (p.K <= 128) return launch_rem<float, 4, 1>(p, s);
-        return launch_rem<float, 4, 2>(p, s);
+        const int w = rem_slab_width<float, 4>(p, slab_req);
+        if (p.K <= 128) return launch_rem<float, 4, 1>(p, w, s);
+        return launch_rem<float, 4, 2>(p, w, s);
     }
-    return launch_rem<float, 1, 4>(p, s);
+    return launch_rem<float, 1, 4>(p, 0, s);
 }
 
 template <>
-int rem_dispatch<double>(const BooParams<double> &p, bool aligned, cudaStream_t s) {
+int rem_dispatch<double>(const BooParams<double> &p, bool aligned, int slab_req, cudaStream_t s) {
     if (aligned && p.K % 2 == 0) {
-        if (p.K <= 64) return launch_rem<double, 2, 1>(p, s);
-        return launch_rem<double, 2, 2>(p, s);
+        const int w = rem_slab_width<double, 2>(p, slab_req);
+        if (p.K <= 64) return launch_rem<double, 2, 1>(p, w, s);
+        return launch_rem<double, 2, 2>(p, w, s);
     }
-    return launch_rem<double, 1, 4>(p, s);
+    return launch_rem<double, 1, 4>(p, 0, s);
 }
 
 template <typename S>
@@ -625,7 +784,7 @@ int boo_matmul_impl(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch
     // then the block kernel adds blocks and tail where a row group has any
     p.skip_rem = A->rem_nnz > 0 && 2 * A->rem_nnz >= A->total_nnz;
     if (p.skip_rem) {
-        const int rc = rem_dispatch<S>(p, mis == 0, s);   // Y = remainder (every row)
+        const int rc = rem_dispatch<S>(p, mis == 0, cfg ? cfg->slab_features : 0, s);   // Y = remainder
         if (rc != SPMM_OK) return rc;
     }
     return boo_dispatch<S>(p, A->n_rg, mis == 0, s);      // (+)= blocks and tail

@@ -272,111 +272,127 @@ __device__ __forceinline__ int64_t group_end(const int32_t *blk_row_grp, int64_t
 
 // CUDA-core part of a row group, summed into w.ys (thread f owns column f):
 // the entries of its blocks with fewer than dense_nnz nonzeros, then its
-// rows' CSR remainder.  Segments (one per block or row) are listed by warp 0,
-// their entries staged as (local row, column, value) by the warpgroup, then
-// each thread sums them for its feature with 16 X loads in flight.
+// rows' CSR remainder.  Segments (one per block or row) are listed by warp 0
+// (seg_table), their entries staged as (local row, column, value) by the
+// warpgroup (stage), and each thread sums them for its feature (sum_range).
+
+// Segment table for segments [s0, s0 + kSegs) of the row group (warp 0).
+template <int NR, int PW>
+__device__ __forceinline__ void seg_table(const TcParams &p, WorkerSmem<NR, PW> &w, int64_t bs, int nblk, int nseg,
+                                          int32_t rbase, int s0, int wt) {
+    if (wt >= 32) return;
+    const int sidx = s0 + wt;
+    int cnt = 0, base = 0, cb = -1;
+    uint32_t aux = 0;
+    if (sidx < nblk) {
+        const int64_t b = bs + sidx;
+        const int32_t k0 = __ldg(p.blk_nz_ptr + b), k1 = __ldg(p.blk_nz_ptr + b + 1);
+        if (k1 - k0 < p.dense_nnz) {
+            cnt = k1 - k0;
+            base = k0;
+            cb = __ldg(p.col_grp_ptr + __ldg(p.blk_col_grp + b));
+            aux = __ldg(p.blk_shift + b);
+        }
+    } else if (sidx < nseg) {
+        const int r = sidx - nblk;
+        const int32_t row = __ldg(p.row_ids + rbase + r);
+        base = __ldg(p.rem_indptr + row);
+        cnt = __ldg(p.rem_indptr + row + 1) - base;
+        aux = (uint32_t)r;
+    }
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(kFullMask, incl, o);
+        if (wt >= o) incl += n;
+    }
+    w.soff[wt + 1] = incl;
+    if (wt == 0) w.soff[0] = 0;
+    w.sbase[wt] = base;
+    w.scb[wt] = cb;
+    w.saux[wt] = aux;
+}
+
+// Entries [g0, g0 + ne) of the current segment table into the list.
+template <int NR, int PW>
+__device__ __forceinline__ void stage(const TcParams &p, WorkerSmem<NR, PW> &w, int g0, int ne, int wt) {
+    for (int i = wt; i < ne; i += 128) {
+        const int g = g0 + i;
+        int lo = 0, hi = kSegs - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (w.soff[mid] <= g) lo = mid; else hi = mid - 1;
+        }
+        const int kidx = w.sbase[lo] + (g - w.soff[lo]);
+        uint32_t r;
+        int32_t col;
+        float v;
+        if (w.scb[lo] >= 0) {
+            const uint32_t idx = __ldg(p.nz_idx + kidx), sh = w.saux[lo];
+            r = idx >> sh;
+            col = __ldg(p.col_ids + w.scb[lo] + (int32_t)(idx & ((1u << sh) - 1u)));
+            v = __ldg(p.nz_val + kidx);
+        } else {
+            r = w.saux[lo];
+            col = __ldg(p.rem_col + kidx);
+            v = __ldg(p.rem_val + kidx);
+        }
+        w.lrow[i] = (uint8_t)(r < (uint32_t)NR ? r : 255u);
+        w.lent[i] = make_int2(col, __float_as_int(v));
+    }
+}
+
+// List entries [i0, i1) into ys for this thread's feature.  Entries of a
+// block arrive row by row: a running sum per row run, added to ys when the
+// row changes (no shared-memory dependency chain between consecutive
+// entries); 16 X loads in flight.
+template <int NR, int PW>
+__device__ __forceinline__ void sum_range(const TcParams &p, WorkerSmem<NR, PW> &w, int i0, int i1, const float *xb,
+                                          int wt) {
+    constexpr int U = 16;
+    uint32_t cur = 255u;
+    float run = 0.f;
+    auto add = [&](uint32_t r, float v, float x) {
+        if (r != cur) {
+            if (cur < (uint32_t)NR) w.ys[cur][wt] += run;
+            cur = r;
+            run = 0.f;
+        }
+        run = fmaf(v, x, run);
+    };
+    int i = i0;
+    for (; i + U <= i1; i += U) {
+        float x[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) x[u] = __ldg(xb + (int64_t)w.lent[i + u].x * p.K);
+#pragma unroll
+        for (int u = 0; u < U; u += 4)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) add(w.lrow[i + u + q], __int_as_float(w.lent[i + u + q].y), x[u + q]);
+    }
+    for (; i < i1; ++i) {
+        const int2 en = w.lent[i];
+        add(w.lrow[i], __int_as_float(en.y), __ldg(xb + (int64_t)en.x * p.K));
+    }
+    if (cur < (uint32_t)NR) w.ys[cur][wt] += run;
+}
+
+// The whole CUDA-core part, pass by pass (row groups whose entries do not fit
+// one segment table and list).
 template <int NR, int PW>
 __device__ __forceinline__ void cuda_part(const TcParams &p, WorkerSmem<NR, PW> &w, int64_t bs, int64_t be,
                                           int32_t rbase, int32_t nr, const float *xb, int wt, uint32_t bar) {
     const int nblk = (int)(be - bs);
     const int nseg = nblk + (p.rem_nnz ? (nr < NR ? nr : NR) : 0);
     for (int s0 = 0; s0 < nseg; s0 += kSegs) {
-        if (wt < 32) {
-            const int sidx = s0 + wt;
-            int cnt = 0, base = 0, cb = -1;
-            uint32_t aux = 0;
-            if (sidx < nblk) {
-                const int64_t b = bs + sidx;
-                const int32_t k0 = __ldg(p.blk_nz_ptr + b), k1 = __ldg(p.blk_nz_ptr + b + 1);
-                if (k1 - k0 < p.dense_nnz) {
-                    cnt = k1 - k0;
-                    base = k0;
-                    cb = __ldg(p.col_grp_ptr + __ldg(p.blk_col_grp + b));
-                    aux = __ldg(p.blk_shift + b);
-                }
-            } else if (sidx < nseg) {
-                const int r = sidx - nblk;
-                const int32_t row = __ldg(p.row_ids + rbase + r);
-                base = __ldg(p.rem_indptr + row);
-                cnt = __ldg(p.rem_indptr + row + 1) - base;
-                aux = (uint32_t)r;
-            }
-            int incl = cnt;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int n = __shfl_up_sync(kFullMask, incl, o);
-                if (wt >= o) incl += n;
-            }
-            w.soff[wt + 1] = incl;
-            if (wt == 0) w.soff[0] = 0;
-            w.sbase[wt] = base;
-            w.scb[wt] = cb;
-            w.saux[wt] = aux;
-        }
+        seg_table<NR, PW>(p, w, bs, nblk, nseg, rbase, s0, wt);
         named_bar_sync(bar, 128);
         const int total = w.soff[kSegs];
         for (int g0 = 0; g0 < total; g0 += kListCap) {
             const int ne = total - g0 < kListCap ? total - g0 : kListCap;
-            for (int i = wt; i < ne; i += 128) {
-                const int g = g0 + i;
-                int lo = 0, hi = kSegs - 1;
-                while (lo < hi) {
-                    const int mid = (lo + hi + 1) >> 1;
-                    if (w.soff[mid] <= g) lo = mid; else hi = mid - 1;
-                }
-                const int kidx = w.sbase[lo] + (g - w.soff[lo]);
-                uint32_t r;
-                int32_t col;
-                float v;
-                if (w.scb[lo] >= 0) {
-                    const uint32_t idx = __ldg(p.nz_idx + kidx), sh = w.saux[lo];
-                    r = idx >> sh;
-                    col = __ldg(p.col_ids + w.scb[lo] + (int32_t)(idx & ((1u << sh) - 1u)));
-                    v = __ldg(p.nz_val + kidx);
-                } else {
-                    r = w.saux[lo];
-                    col = __ldg(p.rem_col + kidx);
-                    v = __ldg(p.rem_val + kidx);
-                }
-                w.lrow[i] = (uint8_t)(r < (uint32_t)NR ? r : 255u);
-                w.lent[i] = make_int2(col, __float_as_int(v));
-            }
+            stage<NR, PW>(p, w, g0, ne, wt);
             named_bar_sync(bar, 128);
-            // Entries of a block arrive row by row: a running sum per row run,
-            // added to ys when the row changes (no shared-memory dependency
-            // chain between consecutive entries); 16 X loads in flight.
-            constexpr int U = 16;
-            uint32_t cur = 255u;
-            float run = 0.f;
-            auto add = [&](uint32_t r, float v, float x) {
-                if (r != cur) {
-                    if (cur < (uint32_t)NR) w.ys[cur][wt] += run;
-                    cur = r;
-                    run = 0.f;
-                }
-                run = fmaf(v, x, run);
-            };
-            int i = 0;
-            for (; i + U <= ne; i += U) {
-                float x[U];
-                int2 en[U];
-#pragma unroll
-                for (int u = 0; u < U; ++u) {
-                    en[u] = w.lent[i + u];
-                    x[u] = __ldg(xb + (int64_t)en[u].x * p.K);
-                }
-#pragma unroll
-                for (int u = 0; u < U; u += 4) {
-                    const uint32_t r4 = *reinterpret_cast<const uint32_t *>(&w.lrow[i + u]);
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) add((r4 >> (8 * q)) & 0xFFu, __int_as_float(en[u + q].y), x[u + q]);
-                }
-            }
-            for (; i < ne; ++i) {
-                const int2 en = w.lent[i];
-                add(w.lrow[i], __int_as_float(en.y), __ldg(xb + (int64_t)en.x * p.K));
-            }
-            if (cur < (uint32_t)NR) w.ys[cur][wt] += run;
+            sum_range<NR, PW>(p, w, 0, ne, xb, wt);
             named_bar_sync(bar, 128);  // the list is reused by the next pass
         }
         named_bar_sync(bar, 128);      // the segment table is rewritten next
@@ -784,10 +800,12 @@ int launch_tc(TcParams p, int64_t batch, void *ws, size_t ws_bytes, cudaStream_t
     if (e == cudaSuccess && gather_rows > 0) {
         boo_gather_kernel<PW><<<(unsigned)(batch * p.n_cg), 256, 0, s>>>(p);
         e = cudaGetLastError();
+        if (e == cudaSuccess) note_product_launch();
     }
     if (e == cudaSuccess) {
         kern<<<grid, Shape::kThreads, Shape::kSmem, s>>>(p);
         e = cudaGetLastError();
+        if (e == cudaSuccess) note_product_launch();
     }
     if (own) {
         const cudaError_t f = cudaFreeAsync(own, s);

@@ -149,7 +149,7 @@ int launch_pbr(const PbrParams<S, I> &p, cudaStream_t s) {
     if (slabs > 65535 || ctas > 0x7fffffffLL) return SPMM_EUNSUPPORTED;
     dim3 grid((unsigned)ctas, (unsigned)slabs, (unsigned)(p.batch < 65535 ? p.batch : 65535));
     pbr_spmm_kernel<S, I, VEC, VPT, LPR><<<grid, kPbrThreads, 0, s>>>(p);
-    SPMM_LAUNCH_CHECK();
+    SPMM_PRODUCT_LAUNCHED();
     return SPMM_OK;
 }
 

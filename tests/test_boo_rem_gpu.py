@@ -26,13 +26,21 @@ def _skewed(rows, cols, seed, dtype, long_rows=(0, 7, 300), long_len=3000):
     return sp.csr_matrix((data, indices, indptr), shape=(rows, cols))
 
 
-def _check(mat, boo, x):
-    got = S.boo_matmul(boo.to('cuda'), x.cuda()).cpu().numpy()
+def _check(mat, boo, x, slabs=(0,)):
     d = {f: getattr(boo, f) for f in O.BOO_FIELDS}
     d.update(rows=boo.rows, cols=boo.cols)
     xn = x.numpy()
     ref = O.boo_matmul(d, xn)
-    assert_spmm_close(got, ref, abs_bound(mat.indptr, mat.indices, mat.data, xn), TOL[np.dtype(mat.dtype)])
+    bound = abs_bound(mat.indptr, mat.indices, mat.data, xn)
+    dev, xd = boo.to('cuda'), x.cuda()
+    for slab in slabs:
+        got = S.boo_matmul(dev, xd, slab_features=slab)
+        assert_spmm_close(got.cpu().numpy(), ref, bound, TOL[np.dtype(mat.dtype)])
+        assert torch.equal(got, S.boo_matmul(dev, xd, slab_features=slab))   # deterministic
+
+
+# slab_features: auto, full width, and each narrow slab width of the dtype
+SLABS = {np.float32: (0, -1, 8, 16, 32), np.float64: (0, -1, 4, 8, 16)}
 
 
 @pytest.mark.parametrize('dtype', [np.float32, np.float64])
@@ -44,7 +52,7 @@ def test_remainder_major_skewed_rows(cuda, dtype, k):
     assert np.diff(boo.rem_indptr).max() > 1024           # long rows present
     tdt = torch.float32 if dtype == np.float32 else torch.float64
     x = torch.from_numpy(np.random.default_rng(k).standard_normal((2, 5000, k))).to(tdt)
-    _check(mat, boo, x)
+    _check(mat, boo, x, SLABS[dtype])
 
 
 @pytest.mark.parametrize('policy', ['remainder', 'tail_batch'])
@@ -59,7 +67,7 @@ def test_remainder_major_with_blocks_and_tail(cuda, policy):
                        small_block_policy=policy, small_block_threshold=8)
     assert boo.num_blocks() > 0
     x = torch.from_numpy(rng.standard_normal((2048, 96)).astype(np.float32))
-    _check(mat, boo, x)
+    _check(mat, boo, x, SLABS[np.float32])
 
 
 def test_remainder_major_deterministic(cuda):
@@ -67,3 +75,23 @@ def test_remainder_major_deterministic(cuda):
     boo = S.csr_to_boo(mat, cluster='identity', target_nr=32, target_nc=32).to('cuda')
     x = torch.randn(3000, 256, generator=torch.Generator().manual_seed(0)).cuda()
     assert torch.equal(S.boo_matmul(boo, x), S.boo_matmul(boo, x))
+
+
+def test_product_launch_counter(cuda):
+    """spmm_product_launches counts the kernels each product launches: three
+    for a remainder-major BOO matrix, two for the tensor-core product (gather
+    pass + worker kernel), one for the CUDA-core block kernel."""
+    from spmm_b200 import _lib, workloads
+    L = _lib.lib()
+    mat = _skewed(1200, 5000, 2, np.float32)
+    rem = S.csr_to_boo(mat, cluster='identity', target_nr=32, target_nc=32, small_block_threshold=64).to('cuda')
+    fem = workloads.fem3d(n=6)
+    blk = S.csr_to_boo(fem, cluster='identity', target_nr=32, target_nc=32).to('cuda')
+    cases = [(rem, torch.randn(5000, 128, device='cuda'), 'auto', 3),
+             (blk, torch.randn(fem.shape[1], 128, device='cuda'), 'tensor_cores', 2),
+             (blk, torch.randn(fem.shape[1], 128, device='cuda'), 'cuda_cores', 1)]
+    for boo, x, engine, want in cases:
+        n0 = L.spmm_product_launches()
+        S.boo_matmul(boo, x, engine=engine)
+        assert L.spmm_product_launches() - n0 == want, engine
+    torch.cuda.synchronize()
