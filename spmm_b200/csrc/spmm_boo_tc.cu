@@ -342,10 +342,11 @@ __device__ __forceinline__ void stage(const TcParams &p, WorkerSmem<NR, PW> &w, 
     }
 }
 
-// List entries [i0, i1) into ys for this thread's feature.  Entries of a
-// block arrive row by row: a running sum per row run, added to ys when the
-// row changes (no shared-memory dependency chain between consecutive
-// entries); 16 X loads in flight.
+// List entries [i0, i1) into ys for this thread's feature (i0 a multiple of
+// 4).  Entries of a block arrive row by row: a running sum per row run, added
+// to ys when the row changes (no shared-memory dependency chain between
+// consecutive entries); 16 X loads in flight, the entries held in registers
+// across the ys updates and their rows read four to a word.
 template <int NR, int PW>
 __device__ __forceinline__ void sum_range(const TcParams &p, WorkerSmem<NR, PW> &w, int i0, int i1, const float *xb,
                                           int wt) {
@@ -363,12 +364,18 @@ __device__ __forceinline__ void sum_range(const TcParams &p, WorkerSmem<NR, PW> 
     int i = i0;
     for (; i + U <= i1; i += U) {
         float x[U];
+        int2 en[U];
 #pragma unroll
-        for (int u = 0; u < U; ++u) x[u] = __ldg(xb + (int64_t)w.lent[i + u].x * p.K);
+        for (int u = 0; u < U; ++u) {
+            en[u] = w.lent[i + u];
+            x[u] = __ldg(xb + (int64_t)en[u].x * p.K);
+        }
 #pragma unroll
-        for (int u = 0; u < U; u += 4)
+        for (int u = 0; u < U; u += 4) {
+            const uint32_t r4 = *reinterpret_cast<const uint32_t *>(&w.lrow[i + u]);
 #pragma unroll
-            for (int q = 0; q < 4; ++q) add(w.lrow[i + u + q], __int_as_float(w.lent[i + u + q].y), x[u + q]);
+            for (int q = 0; q < 4; ++q) add((r4 >> (8 * q)) & 0xFFu, __int_as_float(en[u + q].y), x[u + q]);
+        }
     }
     for (; i < i1; ++i) {
         const int2 en = w.lent[i];
