@@ -484,14 +484,14 @@ def native_arm(args):
     alg = abytes + xbytes + ybytes
     peak, peak_kind = load_peaks()
     achieved = alg / (ms_step * 1e-3) / 1e9
-    engine = 'tc' if ws_bytes else 'cc'
-    if fmt == 'boo' and engine == 'cc' and 2 * A._sizes['rem_nnz'] >= A._sizes['total_nnz']:
-        engine = 'rem'                                  # remainder-major product
+    rem_major = fmt == 'boo' and 0 < 2 * A._sizes['rem_nnz'] and 2 * A._sizes['rem_nnz'] >= A._sizes['total_nnz']
+    engine = 'rem' if rem_major else ('tc' if ws_bytes else 'cc')
     tag = f'{args.config}:{fmt}:{engine}'
     traffic = load_traffic(tag)
     kernel_name = {'tc': 'boo_gather_kernel + boo_tc_kernel (one spmm_boo_matmul call)',
                    'cc': 'boo_spmm_kernel',
-                   'rem': 'rem_tile_kernel + rem_long_kernel + boo_spmm_kernel (one spmm_boo_matmul call)',
+                   'rem': 'rem_flat_plan_kernel + rem_flat_kernel + rem_flat_fix_kernel + boo_spmm_kernel '
+                          '(one spmm_boo_matmul call)',
                    }[engine] if fmt == 'boo' else 'pbr_spmm_kernel'
 
     # cuSPARSE reference point (benchmark only): torch's CSR x dense product on

@@ -123,9 +123,10 @@ typedef struct {
 typedef struct {
     int32_t version;        /* must be 1 */
     int32_t slab_features;  /* remainder-major BOO products: features per pass over A
-                             * (<= 0 = full width, the default and the faster on
-                             * B200; > 0 = the widest supported slab not above
-                             * it, 8 / 16 / 32 floats, 4 / 8 / 16 doubles) */
+                             * (0 = full width with X rows staged by asynchronous
+                             * copies, the default; < 0 = full width through registers;
+                             * > 0 = the widest supported slab not above it,
+                             * 8 / 16 / 32 floats, 4 / 8 / 16 doubles) */
     int32_t engine;         /* enum spmm_engine (BOO product only; PBR ignores it) */
     int32_t reserved;
     void *workspace;        /* optional device scratch of the tensor-core BOO product, */

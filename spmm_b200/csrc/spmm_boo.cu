@@ -15,6 +15,9 @@
 // Per output row the nonzeros are summed in the reference CPU path's order
 // (blocks in order, entries in order, remainder, tail; boo_matrix.cpp:
 // 336-396), with fused multiply-adds.
+#include <climits>
+
+#include "ptx.cuh"
 #include "spmm_common.cuh"
 
 namespace spmm {
@@ -47,6 +50,12 @@ struct BooParams {
     int rowmajor;
     int skip_rem;   // remainder-major: Y already holds the CSR remainder (load-balanced
                     // kernels ran first); add blocks and tail to it, skip other groups
+    // nnz-flat remainder: chunks of `chunk` entries, the row holding each
+    // chunk's first entry, two partial-sum rows per (batch, chunk)
+    int64_t rem_nnz, nch;
+    int32_t chunk;
+    int32_t *chunk_row;
+    S *part;
 };
 
 // first index in a[0..n) with a[i] >= key (a ascending)
@@ -558,6 +567,268 @@ __global__ void __launch_bounds__(32 * kRemWarps, slab_blocks<LPE>()) rem_slab_k
     }
 }
 
+// ---- nnz-flat remainder (default on the aligned path) ----
+//
+// The CSR remainder is cut into chunks of `chunk` consecutive entries,
+// whatever the rows (merge-path style), so every warp gets the same work
+// whatever the row lengths (power-law rows of 3 to 20k entries):
+//   * rem_flat_plan_kernel: the row holding each chunk's first entry, and
+//     zeros for the rows without entries;
+//   * rem_flat_kernel: warps take chunks round-robin and walk their entries
+//     with the X rows landing in shared memory through asynchronous copies
+//     (cp.async, 16 bytes per lane), so the X rows in flight are bounded by
+//     shared memory (kAsyncBuf batches of kAsyncBatch rows per warp) rather
+//     than by the register file: per batch the lanes read the (column, value)
+//     pairs one batch ahead and every lane copies its features of each X row
+//     slab as one commit group; the warp consumes the batches in order (each
+//     lane reads back only the bytes it copied itself) and refills the freed
+//     buffer.  A row lying inside the chunk is stored to Y; a row cut by the
+//     chunk's start goes to the chunk's partial row 0, a row cut only by its
+//     end to partial row 1;
+//   * rem_flat_fix_kernel: each row cut by chunk boundaries gets the sum of
+//     its partials in chunk order.
+// Sums run in entry order within a chunk; the result is deterministic.
+constexpr int kAsyncBatch = 4;   // X rows per batch (one commit group)
+constexpr int kAsyncBuf = 2;     // batches in flight per warp
+
+template <typename S, int VEC, int VPT>
+struct AsyncShape {
+    static constexpr int kSlab = 32 * VPT * VEC;                      // features per launch slice
+    static constexpr int kSlotBytes = kSlab * (int)sizeof(S);
+    static constexpr int kWarpBytes = kAsyncBuf * kAsyncBatch * kSlotBytes;
+    static constexpr int kWarps = (192 * 1024) / kWarpBytes < 24 ? (192 * 1024) / kWarpBytes : 24;
+    static constexpr int kThreads = 32 * kWarps;
+    // per warp, after every warp's slots: entry rows | entry values
+    static constexpr int kValsOff = kAsyncBuf * kAsyncBatch * 4;
+    static constexpr int kMetaBytes = (kValsOff + kAsyncBuf * kAsyncBatch * (int)sizeof(S) + 15) / 16 * 16;
+    static constexpr int kSmem = kWarps * (kWarpBytes + kMetaBytes) + 128;
+    static_assert(kWarps >= 4, "flat remainder: at least four warps per CTA");
+    static_assert(kWarpBytes % 128 == 0 && kValsOff % 8 == 0, "flat remainder: smem alignment");
+};
+
+// Warp per 32 rows: zeros for the empty rows (every batch), and chunk_row[c]
+// = r for every chunk c whose first entry c * chunk lies in row r.
+template <typename S, int VEC>
+__global__ void __launch_bounds__(256) rem_flat_plan_kernel(const BooParams<S> p) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nwarps = (int64_t)gridDim.x * 8;
+    const int64_t ntiles = (p.rows + 31) / 32;
+    for (int64_t t = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); t < ntiles; t += nwarps) {
+        const int64_t r = t * 32 + lane;
+        int32_t e0 = 0, e1 = 0;
+        if (r < p.rows) {
+            e0 = __ldg(p.rem_indptr + r);
+            e1 = __ldg(p.rem_indptr + r + 1);
+        }
+        if (e1 > e0)
+            for (int64_t c = (e0 + (int64_t)p.chunk - 1) / p.chunk; c * p.chunk < e1; ++c)
+                p.chunk_row[c] = (int32_t)r;
+        unsigned em = __ballot_sync(kFullMask, r < p.rows && e0 == e1);
+        while (em) {
+            const int l = __ffs(em) - 1;
+            em &= em - 1;
+            const int64_t row = t * 32 + l;
+            for (int64_t bt = 0; bt < p.batch; ++bt) {
+                S *yr = p.Y + (bt * p.rows + row) * p.K;
+                for (int64_t f = (int64_t)lane * VEC; f < p.K; f += 32 * VEC) {
+                    Frag<S, VEC> z;
+#pragma unroll
+                    for (int u = 0; u < VEC; ++u) z.v[u] = S(0);
+                    st_frag<S, VEC>(yr + f, z);
+                }
+            }
+        }
+    }
+}
+
+template <typename S, int VEC, int VPT>
+__global__ void __launch_bounds__(AsyncShape<S, VEC, VPT>::kThreads, 1) rem_flat_kernel(const BooParams<S> p) {
+    using Sh = AsyncShape<S, VEC, VPT>;
+    constexpr int STR = 32 * VEC;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *base = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 127) & ~(uintptr_t)127);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    S *slots = reinterpret_cast<S *>(base + warp * Sh::kWarpBytes);
+    uint8_t *meta = base + Sh::kWarps * Sh::kWarpBytes + warp * Sh::kMetaBytes;
+    int32_t *erow = reinterpret_cast<int32_t *>(meta);   // row per slot, -1: none
+    S *eval = reinterpret_cast<S *>(meta + Sh::kValsOff);
+
+    const int64_t f0 = (int64_t)blockIdx.y * Sh::kSlab + (int64_t)lane * VEC;
+    bool vm[VPT];
+#pragma unroll
+    for (int q = 0; q < VPT; ++q) vm[q] = f0 + (int64_t)q * STR < p.K;
+    const int64_t nwarps = (int64_t)gridDim.x * Sh::kWarps;
+    uint32_t nb = 0;   // batches this warp has issued (every chunk): buffer = nb % kAsyncBuf
+    for (int64_t bt = blockIdx.z; bt < p.batch; bt += gridDim.z) {
+        const S *xl = p.X + bt * p.cols * p.K + f0;
+        S *yb = p.Y + bt * p.rows * p.K + f0;
+        for (int64_t c = (int64_t)blockIdx.x * Sh::kWarps + warp; c < p.nch; c += nwarps) {
+            const int32_t E0 = (int32_t)(c * p.chunk);
+            const int32_t E1 = (int32_t)(p.rem_nnz - (int64_t)E0 < p.chunk ? p.rem_nnz : (int64_t)E0 + p.chunk);
+            const int32_t rs = p.chunk_row[c];
+            // window of 32 rows from wb: lane l holds row wb + l's entries [me0, me1)
+            int64_t wb = rs;
+            int32_t me0 = INT_MAX, me1 = INT_MAX;
+            auto load_window = [&]() {
+                me0 = me1 = INT_MAX;
+                if (wb + lane < p.rows) {
+                    me0 = __ldg(p.rem_indptr + wb + lane);
+                    me1 = __ldg(p.rem_indptr + wb + lane + 1);
+                }
+            };
+            load_window();
+            const bool rs_cut = __shfl_sync(kFullMask, me0, 0) < E0;   // row rs began in an earlier chunk
+            int32_t pos = E0;   // stream position of the prepared batch
+            // the prepared batch: pn entries, lane j < pn holds entry pos + j
+            int prow = -1, pn = 0;
+            int32_t pc = 0;
+            S pv = S(0);
+            auto prepare = [&]() {
+                prow = -1;
+                pn = 0;
+                pc = 0;
+                pv = S(0);
+                if (pos >= E1) return;
+                int32_t wend = __shfl_sync(kFullMask, me1, 31);
+                while (pos >= wend) {   // the window's rows all end at or before pos
+                    wb += 32;
+                    load_window();
+                    wend = __shfl_sync(kFullMask, me1, 31);
+                }
+                const int32_t lim = E1 < wend ? E1 : wend;
+                pn = lim - pos < kAsyncBatch ? lim - pos : kAsyncBatch;
+                int r = 0;
+#pragma unroll
+                for (int j = 0; j < kAsyncBatch; ++j) {
+                    const int rj = __popc(__ballot_sync(kFullMask, me1 <= pos + j));   // rows ending before
+                    if (lane == j) r = rj;
+                }
+                if (lane < pn) {
+                    prow = (int)(wb + r);
+                    pc = __ldg(p.rem_col + pos + lane);
+                    pv = __ldg(p.rem_val + pos + lane);
+                }
+            };
+            // Copies the prepared batch into buffer b and commits one group
+            // (empty once the chunk is done); false when it was empty.
+            auto issue = [&](uint32_t b) -> bool {
+                if (pn == 0) {
+                    cp_async_commit();
+                    return false;
+                }
+                __syncwarp();   // the previous readers of this buffer's metadata are done
+                if (lane < kAsyncBatch) {
+                    erow[b * kAsyncBatch + lane] = prow;
+                    eval[b * kAsyncBatch + lane] = pv;
+                }
+                S *dst = slots + (size_t)(b * kAsyncBatch) * Sh::kSlab + lane * VEC;
+#pragma unroll
+                for (int j = 0; j < kAsyncBatch; ++j) {
+                    const int32_t cj = __shfl_sync(kFullMask, pc, j);
+                    if (j < pn) {
+                        const S *src = xl + (int64_t)cj * p.K;
+#pragma unroll
+                        for (int qq = 0; qq < VPT; ++qq)
+                            if (vm[qq]) cp_async16(dst + j * Sh::kSlab + qq * STR, src + qq * STR);
+                    }
+                }
+                cp_async_commit();
+                pos += pn;
+                prepare();
+                return true;
+            };
+            prepare();
+            uint32_t issued = 0;   // non-empty batches of this chunk
+            bool more = true;
+            for (int i = 0; i < kAsyncBuf; ++i) {   // prologue: kAsyncBuf groups
+                if (more && issue((nb + issued) % kAsyncBuf)) ++issued;
+                else if (more) more = false;
+                else cp_async_commit();
+            }
+            Frag<S, VEC> acc[VPT];
+#pragma unroll
+            for (int q = 0; q < VPT; ++q)
+#pragma unroll
+                for (int u = 0; u < VEC; ++u) acc[q].v[u] = S(0);
+            int cur = -1;
+            // a finished row: to Y, or to a partial row when a chunk boundary cuts it
+            S *pb = p.part + ((bt * p.nch + c) * 2) * p.K + f0;
+            auto flush = [&](bool last_cut) {
+                S *dst = yb + (int64_t)cur * p.K;
+                if (cur == rs && rs_cut) dst = pb;
+                else if (last_cut) dst = pb + p.K;
+                rem_store_row<S, VEC, VPT>(dst, acc, vm);
+            };
+            for (uint32_t k = 0; k < issued; ++k) {
+                const uint32_t b = (nb + k) % kAsyncBuf;
+                cp_async_wait<kAsyncBuf - 1>();   // batch k's group (every later one may pend)
+                __syncwarp();
+                const S *slot = slots + (size_t)(b * kAsyncBatch) * Sh::kSlab + lane * VEC;
+#pragma unroll
+                for (int j = 0; j < kAsyncBatch; ++j) {
+                    const int r = erow[b * kAsyncBatch + j];
+                    if (r < 0) break;
+                    if (r != cur) {
+                        if (cur >= 0) flush(false);
+#pragma unroll
+                        for (int q = 0; q < VPT; ++q)
+#pragma unroll
+                            for (int u = 0; u < VEC; ++u) acc[q].v[u] = S(0);
+                        cur = r;
+                    }
+                    const S a = eval[b * kAsyncBatch + j];
+#pragma unroll
+                    for (int q = 0; q < VPT; ++q)
+                        if (vm[q]) {
+                            const Frag<S, VEC> x = lds_frag<S, VEC>(slot + j * Sh::kSlab + q * STR);
+#pragma unroll
+                            for (int u = 0; u < VEC; ++u) acc[q].v[u] = fma(a, x.v[u], acc[q].v[u]);
+                        }
+                }
+                // refill this buffer (one group, empty once the chunk is done)
+                if (more) {
+                    if (issue(b)) ++issued;
+                    else more = false;
+                } else {
+                    cp_async_commit();
+                }
+            }
+            if (cur >= 0) flush(__ldg(p.rem_indptr + cur + 1) > E1);
+            nb += issued;
+        }
+    }
+    cp_async_wait<0>();
+}
+
+// Warp per chunk c >= 1 whose first row r began in chunk c - 1: Y[r] = its
+// partial there (row 1: cut by that chunk's end) plus its partial rows 0 of
+// chunks c, c + 1, ... while r holds their first entry.
+template <typename S, int VEC>
+__global__ void __launch_bounds__(256) rem_flat_fix_kernel(const BooParams<S> p) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nwarps = (int64_t)gridDim.x * 8;
+    for (int64_t c = 1 + (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); c < p.nch; c += nwarps) {
+        const int32_t r = p.chunk_row[c];
+        const int64_t s0 = __ldg(p.rem_indptr + r), e0c = c * (int64_t)p.chunk;
+        if (s0 >= e0c || s0 < e0c - p.chunk) continue;   // not cut here, or cut first at an earlier boundary
+        int64_t c1 = c;
+        while (c1 + 1 < p.nch && p.chunk_row[c1 + 1] == r) ++c1;
+        for (int64_t bt = 0; bt < p.batch; ++bt) {
+            const S *pp = p.part + (bt * p.nch) * 2 * p.K;
+            S *yr = p.Y + (bt * p.rows + r) * p.K;
+            for (int64_t f = (int64_t)lane * VEC; f < p.K; f += 32 * VEC) {
+                Frag<S, VEC> acc = ldg_frag<S, VEC>(pp + ((c - 1) * 2 + 1) * p.K + f);
+                for (int64_t cc = c; cc <= c1; ++cc) {
+                    const Frag<S, VEC> t = ldg_frag<S, VEC>(pp + (cc * 2) * p.K + f);
+#pragma unroll
+                    for (int u = 0; u < VEC; ++u) acc.v[u] += t.v[u];
+                }
+                st_frag<S, VEC>(yr + f, acc);
+            }
+        }
+    }
+}
+
 template <typename S, int VEC, int VPT>
 __global__ void __launch_bounds__(32 * kLongWarps, 1) rem_long_kernel(const BooParams<S> p) {
     constexpr int SLAB = 32 * VPT * VEC;
@@ -619,7 +890,8 @@ __global__ void __launch_bounds__(32 * kLongWarps, 1) rem_long_kernel(const BooP
 // requests leave the kernel latency-bound.
 template <typename S, int VEC>
 int rem_slab_width(const BooParams<S> &p, int requested) {
-    if (p.K % VEC || requested <= 0) return 0;
+    if (requested < 0) return -1;   // full width through registers (rem_tile_kernel)
+    if (p.K % VEC || requested == 0) return 0;
     int w = 0;
     for (int lpe = 8; lpe >= 2; lpe >>= 1)
         if (!w && lpe * VEC <= requested) w = lpe * VEC;
@@ -638,10 +910,72 @@ int launch_rem_slab(const BooParams<S> &p, int sms, unsigned bz, cudaStream_t s)
     return SPMM_OK;
 }
 
-// Rows of at most kLongRow entries in slabs of `slab_w` features (0: full
-// width, 32 * VPT * VEC per slice), then the long rows at full width.
+// Chunk size of the nnz-flat remainder: about 8192 chunks, 256..2048 entries.
+inline int32_t rem_flat_chunk(int64_t rem_nnz) {
+    const int64_t c = ceil_div(rem_nnz, (int64_t)8192);
+    return (int32_t)(c < 256 ? 256 : c > 2048 ? 2048 : c);
+}
+
+// Scratch of the nnz-flat remainder: chunk rows, then two partial rows of K
+// per (batch, chunk).
+inline size_t rem_flat_workspace(int64_t rem_nnz, int64_t batch, int64_t K, size_t elem) {
+    if (rem_nnz <= 0) return 0;
+    const int64_t nch = ceil_div(rem_nnz, (int64_t)rem_flat_chunk(rem_nnz));
+    return (size_t)ceil_div(nch * 4, (int64_t)256) * 256 + (size_t)(batch * nch * 2 * K) * elem;
+}
+
+// The nnz-flat remainder (plan, chunks, fix-up) on scratch from `ws` or, when
+// that is absent or short, from the stream-ordered allocator.
 template <typename S, int VEC, int VPT>
-int launch_rem(const BooParams<S> &p, int slab_w, cudaStream_t s) {
+int launch_rem_flat(BooParams<S> p, int sms, unsigned bz, void *ws, size_t ws_bytes, cudaStream_t s) {
+    using Sh = AsyncShape<S, VEC, VPT>;
+    const int64_t slabs = ceil_div(p.K, (int64_t)Sh::kSlab);
+    if (slabs > 65535 || p.rem_nnz > 0x7fffffffLL) return SPMM_EUNSUPPORTED;
+    p.chunk = rem_flat_chunk(p.rem_nnz);
+    p.nch = ceil_div(p.rem_nnz, (int64_t)p.chunk);
+    const size_t need = rem_flat_workspace(p.rem_nnz, p.batch, p.K, sizeof(S));
+    void *own = nullptr;
+    if (!ws || ws_bytes < need) {
+        SPMM_CUDA_TRY(cudaMallocAsync(&own, need, s));
+        ws = own;
+    }
+    p.chunk_row = reinterpret_cast<int32_t *>(ws);
+    p.part = reinterpret_cast<S *>(reinterpret_cast<uint8_t *>(ws) + ceil_div(p.nch * 4, (int64_t)256) * 256);
+    auto kern = rem_flat_kernel<S, VEC, VPT>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Sh::kSmem);
+    const int64_t tiles = ceil_div(p.rows, (int64_t)32);
+    const int64_t gp = ceil_div(tiles, (int64_t)8) < (int64_t)sms * 8 ? ceil_div(tiles, (int64_t)8) : (int64_t)sms * 8;
+    if (e == cudaSuccess) {
+        rem_flat_plan_kernel<S, VEC><<<(unsigned)gp, 256, 0, s>>>(p);
+        e = cudaGetLastError();
+        if (e == cudaSuccess) note_product_launch();
+    }
+    if (e == cudaSuccess) {
+        const int64_t ctas = ceil_div(p.nch, (int64_t)Sh::kWarps);
+        const int64_t g = ctas < (int64_t)sms ? ctas : (int64_t)sms;
+        kern<<<dim3((unsigned)g, (unsigned)slabs, bz), Sh::kThreads, Sh::kSmem, s>>>(p);
+        e = cudaGetLastError();
+        if (e == cudaSuccess) note_product_launch();
+    }
+    if (e == cudaSuccess) {
+        const int64_t gf = ceil_div(p.nch, (int64_t)8) < (int64_t)sms * 8 ? ceil_div(p.nch, (int64_t)8) : (int64_t)sms * 8;
+        rem_flat_fix_kernel<S, VEC><<<(unsigned)(gf > 0 ? gf : 1), 256, 0, s>>>(p);
+        e = cudaGetLastError();
+        if (e == cudaSuccess) note_product_launch();
+    }
+    if (own) {
+        const cudaError_t f = cudaFreeAsync(own, s);
+        if (e == cudaSuccess) e = f;
+    }
+    return e == cudaSuccess ? SPMM_OK : SPMM_ECUDA;
+}
+
+// The CSR remainder of every row into Y: nnz-flat chunks (slab_w == 0, the
+// aligned default), else rows of at most kLongRow entries in slabs of slab_w
+// features (> 0) or at full width through registers (< 0; also the unaligned
+// path), then the long rows at full width.
+template <typename S, int VEC, int VPT>
+int launch_rem(const BooParams<S> &p, int slab_w, void *ws, size_t ws_bytes, cudaStream_t s) {
     constexpr int SLAB = 32 * VPT * VEC;
     const int64_t slabs = ceil_div(p.K, SLAB);
     if (slabs > 65535) return SPMM_EUNSUPPORTED;
@@ -649,9 +983,8 @@ int launch_rem(const BooParams<S> &p, int slab_w, cudaStream_t s) {
     SPMM_CUDA_TRY(cudaGetDevice(&dev));
     SPMM_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const unsigned bz = (unsigned)(p.batch < 65535 ? p.batch : 65535);
-    bool slabbed = false;
     if constexpr (VEC > 1) {
-        slabbed = true;
+        if (slab_w == 0) return launch_rem_flat<S, VEC, VPT>(p, sms, bz, ws, ws_bytes, s);
         if (slab_w == 8 * VEC) {
             SPMM_TRY(launch_rem_slab<S, VEC, 8>(p, sms, bz, s));
         } else if (slab_w == 4 * VEC) {
@@ -659,10 +992,12 @@ int launch_rem(const BooParams<S> &p, int slab_w, cudaStream_t s) {
         } else if (slab_w == 2 * VEC) {
             SPMM_TRY(launch_rem_slab<S, VEC, 2>(p, sms, bz, s));
         } else {
-            slabbed = false;
+            slab_w = -1;
         }
+    } else {
+        slab_w = -1;
     }
-    if (!slabbed) {
+    if (slab_w < 0) {
         const int64_t tile_ctas = ceil_div(ceil_div(p.rows, (int64_t)32), (int64_t)kRemWarps);
         const int64_t g1 = tile_ctas < (int64_t)sms * 8 ? tile_ctas : (int64_t)sms * 8;
         rem_tile_kernel<S, VEC, VPT><<<dim3((unsigned)g1, (unsigned)slabs, bz), 32 * kRemWarps, 0, s>>>(p);
@@ -676,26 +1011,28 @@ int launch_rem(const BooParams<S> &p, int slab_w, cudaStream_t s) {
 }
 
 template <typename S>
-int rem_dispatch(const BooParams<S> &p, bool aligned, int slab_req, cudaStream_t s);
+int rem_dispatch(const BooParams<S> &p, bool aligned, int slab_req, void *ws, size_t ws_bytes, cudaStream_t s);
 
 template <>
-int rem_dispatch<float>(const BooParams<float> &p, bool aligned, int slab_req, cudaStream_t s) {
+int rem_dispatch<float>(const BooParams<float> &p, bool aligned, int slab_req, void *ws, size_t ws_bytes,
+                        cudaStream_t s) {
     if (aligned && p.K % 4 == 0) {
         const int w = rem_slab_width<float, 4>(p, slab_req);
-        if (p.K <= 128) return launch_rem<float, 4, 1>(p, w, s);
-        return launch_rem<float, 4, 2>(p, w, s);
+        if (p.K <= 128) return launch_rem<float, 4, 1>(p, w, ws, ws_bytes, s);
+        return launch_rem<float, 4, 2>(p, w, ws, ws_bytes, s);
     }
-    return launch_rem<float, 1, 4>(p, 0, s);
+    return launch_rem<float, 1, 4>(p, -1, ws, ws_bytes, s);
 }
 
 template <>
-int rem_dispatch<double>(const BooParams<double> &p, bool aligned, int slab_req, cudaStream_t s) {
+int rem_dispatch<double>(const BooParams<double> &p, bool aligned, int slab_req, void *ws, size_t ws_bytes,
+                         cudaStream_t s) {
     if (aligned && p.K % 2 == 0) {
         const int w = rem_slab_width<double, 2>(p, slab_req);
-        if (p.K <= 64) return launch_rem<double, 2, 1>(p, w, s);
-        return launch_rem<double, 2, 2>(p, w, s);
+        if (p.K <= 64) return launch_rem<double, 2, 1>(p, w, ws, ws_bytes, s);
+        return launch_rem<double, 2, 2>(p, w, ws, ws_bytes, s);
     }
-    return launch_rem<double, 1, 4>(p, 0, s);
+    return launch_rem<double, 1, 4>(p, -1, ws, ws_bytes, s);
 }
 
 template <typename S>
@@ -779,12 +1116,18 @@ int boo_matmul_impl(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch
     p.X = (const S *)X;
     p.Y = (S *)Y;
     p.rowmajor = A->nz_order == SPMM_BOO_ROWMAJOR;
+    p.rem_nnz = A->rem_nnz;
+    p.nch = 0;
+    p.chunk = 0;
+    p.chunk_row = nullptr;
+    p.part = nullptr;
     const uintptr_t mis = ((uintptr_t)X | (uintptr_t)Y) & 15;
     // remainder-major matrices: the load-balanced remainder kernels write Y,
     // then the block kernel adds blocks and tail where a row group has any
     p.skip_rem = A->rem_nnz > 0 && 2 * A->rem_nnz >= A->total_nnz;
     if (p.skip_rem) {
-        const int rc = rem_dispatch<S>(p, mis == 0, cfg ? cfg->slab_features : 0, s);   // Y = remainder
+        const int rc = rem_dispatch<S>(p, mis == 0, cfg ? cfg->slab_features : 0, cfg ? cfg->workspace : nullptr,
+                                       cfg ? (size_t)cfg->workspace_bytes : 0, s);   // Y = remainder
         if (rc != SPMM_OK) return rc;
     }
     return boo_dispatch<S>(p, A->n_rg, mis == 0, s);      // (+)= blocks and tail
@@ -792,6 +1135,7 @@ int boo_matmul_impl(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch
 
 }  // namespace
 }  // namespace spmm
+
 
 using namespace spmm;
 
@@ -820,8 +1164,13 @@ extern "C" int spmm_boo_matmul(const spmm_boo_dev *A, const void *X, void *Y, in
 
 extern "C" size_t spmm_boo_matmul_workspace_size(const spmm_boo_dev *A, int64_t batch, int64_t K,
                                                  const spmm_launch_cfg *cfg) {
-    if (!A || batch <= 0 || K <= 0 || A->scalar_type != SPMM_F32) return 0;
+    if (!A || batch <= 0 || K <= 0) return 0;
+    if (A->scalar_type != SPMM_F32 && A->scalar_type != SPMM_F64) return 0;
     if (cfg && cfg->version != 1) return 0;
-    if (!tc_selected(A, cfg ? cfg->engine : SPMM_ENGINE_AUTO)) return 0;
-    return boo_tc_workspace(A, batch, K);
+    if (A->scalar_type == SPMM_F32 && tc_selected(A, cfg ? cfg->engine : SPMM_ENGINE_AUTO))
+        return boo_tc_workspace(A, batch, K);
+    // remainder-major: the nnz-flat remainder's scratch (default slab setting)
+    const bool rem_major = A->rem_nnz > 0 && 2 * A->rem_nnz >= A->total_nnz;
+    if (!rem_major || (cfg && cfg->slab_features != 0)) return 0;
+    return rem_flat_workspace(A->rem_nnz, batch, K, A->scalar_type == SPMM_F32 ? 4 : 8);
 }

@@ -29,6 +29,16 @@ __device__ __forceinline__ Frag<S, VEC> ldg_frag(const S *p) {
     return f;
 }
 
+// From shared memory, as one vector access.
+template <typename S, int VEC>
+__device__ __forceinline__ Frag<S, VEC> lds_frag(const S *p) {
+    using V = typename VecOf<S, VEC>::T;
+    const V t = *reinterpret_cast<const V *>(p);
+    Frag<S, VEC> f;
+    memcpy(&f, &t, sizeof(V));
+    return f;
+}
+
 template <typename S, int VEC>
 __device__ __forceinline__ void st_frag(S *p, const Frag<S, VEC> &f) {
     using V = typename VecOf<S, VEC>::T;

@@ -78,20 +78,44 @@ def test_remainder_major_deterministic(cuda):
 
 
 def test_product_launch_counter(cuda):
-    """spmm_product_launches counts the kernels each product launches: three
-    for a remainder-major BOO matrix, two for the tensor-core product (gather
-    pass + worker kernel), one for the CUDA-core block kernel."""
+    """spmm_product_launches counts the kernels each product launches: four
+    for a remainder-major BOO matrix (nnz-flat plan, chunks, fix-up, block
+    kernel; three on the register path: tiles, long rows, block kernel), two
+    for the tensor-core product (gather pass + worker kernel), one for the
+    CUDA-core block kernel."""
     from spmm_b200 import _lib, workloads
     L = _lib.lib()
     mat = _skewed(1200, 5000, 2, np.float32)
     rem = S.csr_to_boo(mat, cluster='identity', target_nr=32, target_nc=32, small_block_threshold=64).to('cuda')
     fem = workloads.fem3d(n=6)
     blk = S.csr_to_boo(fem, cluster='identity', target_nr=32, target_nc=32).to('cuda')
-    cases = [(rem, torch.randn(5000, 128, device='cuda'), 'auto', 3),
-             (blk, torch.randn(fem.shape[1], 128, device='cuda'), 'tensor_cores', 2),
-             (blk, torch.randn(fem.shape[1], 128, device='cuda'), 'cuda_cores', 1)]
-    for boo, x, engine, want in cases:
+    xr = torch.randn(5000, 128, device='cuda')
+    xb = torch.randn(fem.shape[1], 128, device='cuda')
+    cases = [(rem, xr, dict(), 4), (rem, xr, dict(slab_features=-1), 3),
+             (blk, xb, dict(engine='tensor_cores'), 2), (blk, xb, dict(engine='cuda_cores'), 1)]
+    for boo, x, kw, want in cases:
         n0 = L.spmm_product_launches()
-        S.boo_matmul(boo, x, engine=engine)
-        assert L.spmm_product_launches() - n0 == want, engine
+        S.boo_matmul(boo, x, **kw)
+        assert L.spmm_product_launches() - n0 == want, kw
     torch.cuda.synchronize()
+
+
+def test_remainder_flat_chunk_boundaries(cuda):
+    """nnz-flat chunks cut rows anywhere: rows spanning many chunks, rows
+    ending exactly on a chunk boundary, runs of empty rows inside a chunk and
+    a window of more than 32 rows inside one chunk."""
+    rng = np.random.default_rng(17)
+    lens = rng.integers(0, 4, 3000)
+    lens[100] = 9000                  # spans many chunks
+    lens[200:260] = 0                 # empty rows
+    lens[500] = 256 - int(lens[:500].sum()) % 256 + 256   # ends on a multiple of 256
+    indptr = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
+    cols = 12000
+    indices = np.concatenate([np.sort(rng.choice(cols, n, replace=False)) for n in lens]).astype(np.int64)
+    data = rng.standard_normal(indptr[-1]).astype(np.float32)
+    mat = sp.csr_matrix((data, indices, indptr), shape=(3000, cols))
+    boo = S.csr_to_boo(mat, cluster='identity', target_nr=32, target_nc=32, small_block_threshold=64)
+    assert 2 * boo.remainder_nnz() >= boo.total_nnz
+    for k in (4, 96, 260):
+        x = torch.from_numpy(rng.standard_normal((2, cols, k)).astype(np.float32))
+        _check(mat, boo, x, (0, -1))
