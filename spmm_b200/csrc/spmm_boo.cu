@@ -53,6 +53,7 @@ struct BooParams {
     // nnz-flat remainder: chunks of `chunk` entries, the row holding each
     // chunk's first entry, two partial-sum rows per (batch, chunk)
     int64_t rem_nnz, nch;
+    int64_t n_rg, rgs_per_cta;   // block kernel: CTA x takes row groups [x * rgs_per_cta, ...)
     int32_t chunk;
     int32_t *chunk_row;
     S *part;
@@ -144,21 +145,30 @@ boo_spmm_kernel(const BooParams<S> p) {
     const int tid = threadIdx.x;
     const int g = tid / LPR, l = tid % LPR;
     const int warp = tid >> 5, lane = tid & 31;
-    const int64_t rg = blockIdx.x;
     const int64_t f0 = (int64_t)blockIdx.y * SLAB + (int64_t)l * VEC;
     bool vm[VPT];
 #pragma unroll
     for (int v = 0; v < VPT; ++v) vm[v] = f0 + (int64_t)v * LPR * VEC < p.K;
 
-    const int32_t rbase = p.row_grp_ptr[rg];
-    const int32_t n_r = p.row_grp_ptr[rg + 1] - rbase;
+    // row groups [rg_begin, rg_end); blocks found by one search, then walked
+    const int64_t rg_begin = (int64_t)blockIdx.x * p.rgs_per_cta;
+    const int64_t rg_end = rg_begin + p.rgs_per_cta < p.n_rg ? rg_begin + p.rgs_per_cta : p.n_rg;
+    if (tid == 0) sm.blk_hi = lower_bound_i32(p.blk_row_grp, p.nb, rg_begin);
+    for (int64_t rg = rg_begin; rg < rg_end; ++rg) {
+    __syncthreads();   // the previous group's readers of sm are done
     if (tid == 0) {
-        sm.blk_lo = lower_bound_i32(p.blk_row_grp, p.nb, rg);
-        sm.blk_hi = lower_bound_i32(p.blk_row_grp, p.nb, rg + 1);
+        const int64_t lo = sm.blk_hi;
+        int64_t hi = lo;
+        if (lo < p.nb && p.blk_row_grp[lo] == rg)
+            hi = lo + 1 + lower_bound_i32(p.blk_row_grp + lo + 1, p.nb - lo - 1, rg + 1);
+        sm.blk_lo = lo;
+        sm.blk_hi = hi;
     }
     __syncthreads();
     const int64_t blk_lo = sm.blk_lo, blk_hi = sm.blk_hi;
-    if (p.skip_rem && blk_lo == blk_hi && p.tail_nnz == 0) return;   // nothing to add
+    if (p.skip_rem && blk_lo == blk_hi && p.tail_nnz == 0) continue;   // nothing to add
+    const int32_t rbase = p.row_grp_ptr[rg];
+    const int32_t n_r = p.row_grp_ptr[rg + 1] - rbase;
 
     for (int64_t bt = blockIdx.z; bt < p.batch; bt += gridDim.z) {
         const S *xl = p.X + bt * p.cols * p.K + f0;
@@ -308,14 +318,26 @@ boo_spmm_kernel(const BooParams<S> p) {
             }
         }
     }
+    }
 }
 
+// One CTA per row group; in add mode (skip_rem: most groups have nothing to
+// add) each CTA walks a run of groups, so the empty ones cost one load each.
 template <typename S, int VEC, int VPT, int LPR>
-int launch_boo_n(const BooParams<S> &p, int64_t n_rg, cudaStream_t s) {
+int launch_boo_n(BooParams<S> p, int64_t n_rg, cudaStream_t s) {
     constexpr int SLAB = LPR * VPT * VEC;
     const int64_t slabs = ceil_div(p.K, SLAB);
     if (slabs > 65535 || n_rg > 0x7fffffffLL) return SPMM_EUNSUPPORTED;
-    dim3 grid((unsigned)n_rg, (unsigned)slabs, (unsigned)(p.batch < 65535 ? p.batch : 65535));
+    p.n_rg = n_rg;
+    p.rgs_per_cta = 1;
+    if (p.skip_rem) {
+        int dev = 0, sms = 0;
+        SPMM_CUDA_TRY(cudaGetDevice(&dev));
+        SPMM_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        p.rgs_per_cta = ceil_div(n_rg, (int64_t)sms * 8);
+    }
+    const int64_t ctas = ceil_div(n_rg, p.rgs_per_cta);
+    dim3 grid((unsigned)ctas, (unsigned)slabs, (unsigned)(p.batch < 65535 ? p.batch : 65535));
     boo_spmm_kernel<S, VEC, VPT, LPR><<<grid, kBooThreads, 0, s>>>(p);
     SPMM_PRODUCT_LAUNCHED();
     return SPMM_OK;
@@ -1117,6 +1139,8 @@ int boo_matmul_impl(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch
     p.Y = (S *)Y;
     p.rowmajor = A->nz_order == SPMM_BOO_ROWMAJOR;
     p.rem_nnz = A->rem_nnz;
+    p.n_rg = A->n_rg;
+    p.rgs_per_cta = 1;
     p.nch = 0;
     p.chunk = 0;
     p.chunk_row = nullptr;
