@@ -119,3 +119,34 @@ def test_remainder_flat_chunk_boundaries(cuda):
     for k in (4, 96, 260):
         x = torch.from_numpy(rng.standard_normal((2, cols, k)).astype(np.float32))
         _check(mat, boo, x, (0, -1))
+
+
+def test_remainder_flat_abi_workspace_optional(cuda):
+    """Through the C ABI: the nnz-flat remainder's scratch from the caller or
+    from the stream-ordered allocator gives the same bits; the register path
+    (slab_features < 0) needs none."""
+    import ctypes as C
+    from spmm_b200 import _lib
+    from spmm_b200._device import stream_handle
+    mat = _skewed(1500, 4000, 5, np.float32)
+    boo = S.csr_to_boo(mat, cluster='identity', target_nr=32, target_nc=32, small_block_threshold=64).to('cuda')
+    st = boo._dev_struct(boo._gpu_meta)
+    x = torch.randn(2, 4000, 192, generator=torch.Generator().manual_seed(4)).cuda()
+    L = _lib.lib()
+    out = []
+    for with_ws in (False, True):
+        cfg = _lib.launch_cfg('auto')
+        ws_bytes = L.spmm_boo_matmul_workspace_size(C.byref(st), 2, 192, C.byref(cfg))
+        assert ws_bytes > 0
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device='cuda') if with_ws else None
+        if ws is not None:
+            cfg.workspace, cfg.workspace_bytes = ws.data_ptr(), ws_bytes
+        y = torch.empty(2, 1500, 192, device='cuda')
+        rc = L.spmm_boo_matmul(C.byref(st), C.c_void_p(x.data_ptr()), C.c_void_p(y.data_ptr()), 2, 192,
+                               C.byref(cfg), stream_handle(x.device))
+        assert rc == 0
+        torch.cuda.synchronize()
+        out.append(y)
+    assert torch.equal(out[0], out[1])
+    reg = _lib.launch_cfg('auto', slab_features=-1)
+    assert L.spmm_boo_matmul_workspace_size(C.byref(st), 2, 192, C.byref(reg)) == 0
