@@ -129,8 +129,8 @@ typedef struct {
                              * 8 / 16 / 32 floats, 4 / 8 / 16 doubles) */
     int32_t engine;         /* enum spmm_engine (BOO product only; PBR ignores it) */
     int32_t reserved;
-    void *workspace;        /* optional device scratch of the tensor-core BOO product, */
-    uint64_t workspace_bytes; /* spmm_boo_matmul_workspace_size() bytes, 16-byte aligned */
+    void *workspace;        /* optional device scratch of the BOO product (tensor-core */
+    uint64_t workspace_bytes; /* or nnz-flat remainder): spmm_boo_matmul_workspace_size() bytes */
 } spmm_launch_cfg;
 
 /* Which units multiply the BOO blocks.  AUTO takes the tensor cores when the
@@ -239,6 +239,26 @@ uint64_t spmm_product_launches(void);
  * block shape with block_rows * block_cols <= 64 and any K. */
 int spmm_pbr_matmul(const spmm_pbr_dev *A, const void *X, void *Y, int64_t batch, int64_t K,
                     const spmm_launch_cfg *cfg, spmm_stream_t stream);
+
+/* CSR from a BOO matrix on the GPU (replaces boo_to_csr, torch_fast_spdmm/
+ * boo_matrix/boo_matrix.cpp:277-333, bound at bindings/bindings.cpp): every
+ * stored entry -- blocks, CSR remainder, COO tail -- with each row ordered by
+ * (column, value) like the reference's per-row sort of (column, value) pairs.
+ * indptr (rows+1), indices and values (nnz_c + rem_nnz + tail_nnz) are
+ * caller-allocated; index_type (enum spmm_index_type) is the output index
+ * type.  Scratch: spmm_boo_to_csr_workspace_size() bytes. */
+size_t spmm_boo_to_csr_workspace_size(const spmm_boo_dev *A);
+int spmm_boo_to_csr(const spmm_boo_dev *A, void *indptr, void *indices, void *values, int index_type,
+                    void *workspace, size_t workspace_bytes, spmm_stream_t stream);
+
+/* CSR from a PBR matrix on the GPU (replaces pbr_to_csr, torch_fast_spdmm/
+ * pbr_matrix/pbr_matrix.cpp:279-331): block values in bit order, then the
+ * remainder, each row ordered by (column, value).  SPMM_EINVAL when a block
+ * bit lies past the last row (the reference's RuntimeError); synchronises the
+ * stream to check that.  Outputs and scratch as for spmm_boo_to_csr. */
+size_t spmm_pbr_to_csr_workspace_size(const spmm_pbr_dev *A);
+int spmm_pbr_to_csr(const spmm_pbr_dev *A, void *indptr, void *indices, void *values, int index_type,
+                    void *workspace, size_t workspace_bytes, spmm_stream_t stream);
 
 #ifdef __cplusplus
 }

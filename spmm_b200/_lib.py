@@ -33,7 +33,9 @@ EXPORTS = ('spmm_status_string', 'spmm_abi_version', 'spmm_boo_build_workspace_s
            'spmm_boo_build_analyze', 'spmm_boo_build_emit', 'spmm_boo_build_noalloc',
            'spmm_pbr_build_workspace_size',
            'spmm_pbr_build_analyze', 'spmm_pbr_build_emit', 'spmm_boo_matmul', 'spmm_pbr_matmul',
-           'spmm_tc_status', 'spmm_boo_matmul_workspace_size', 'spmm_product_launches')
+           'spmm_tc_status', 'spmm_boo_matmul_workspace_size', 'spmm_product_launches',
+           'spmm_boo_to_csr_workspace_size', 'spmm_boo_to_csr', 'spmm_pbr_to_csr_workspace_size',
+           'spmm_pbr_to_csr')
 
 
 class CsrDev(C.Structure):
@@ -124,6 +126,16 @@ def lib() -> C.CDLL:
         L.spmm_tc_status.restype = C.c_int
         L.spmm_product_launches.argtypes = []
         L.spmm_product_launches.restype = C.c_uint64
+        L.spmm_boo_to_csr_workspace_size.argtypes = [C.POINTER(BooDev)]
+        L.spmm_boo_to_csr_workspace_size.restype = C.c_size_t
+        L.spmm_pbr_to_csr_workspace_size.argtypes = [C.POINTER(PbrDev)]
+        L.spmm_pbr_to_csr_workspace_size.restype = C.c_size_t
+        L.spmm_boo_to_csr.argtypes = [C.POINTER(BooDev), C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                      C.c_void_p, C.c_size_t, C.c_void_p]
+        L.spmm_pbr_to_csr.argtypes = [C.POINTER(PbrDev), C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                      C.c_void_p, C.c_size_t, C.c_void_p]
+        L.spmm_boo_to_csr.restype = C.c_int
+        L.spmm_pbr_to_csr.restype = C.c_int
         for n in ('spmm_boo_build_analyze', 'spmm_boo_build_emit', 'spmm_pbr_build_analyze',
                   'spmm_pbr_build_emit', 'spmm_boo_matmul', 'spmm_pbr_matmul'):
             getattr(L, n).restype = C.c_int

@@ -10,7 +10,8 @@ Same names, arguments, returned classes and exceptions as the reference's
 * ``boo_matmul`` (boo.py:230-354) runs ``spmm_boo_matmul`` on X's device and
   stream.  A CPU ``x`` is copied to the current CUDA device, multiplied there
   and the result copied back: there is no CPU implementation.
-* ``boo_to_csr``, ``boo_info``, ``boo_arena_bytes`` are host utilities.
+* ``boo_to_csr`` runs on the GPU (``spmm_boo_to_csr``); ``boo_info`` and
+  ``boo_arena_bytes`` are host utilities.
 """
 
 from __future__ import annotations
@@ -387,31 +388,41 @@ def csr_to_boo(mat, cluster: str = 'hem', target_nr: int = 32, target_nc: int = 
                           _ORDER_CODE[nz_order])
 
 
+def _csr_from_device(rows, cols, n, index_dtype, scalar_dtype, device, run) -> sp.csr_matrix:
+    """Allocates the CSR outputs and scratch on `device`, lets `run` fill them
+    through the C ABI, and returns the host scipy matrix."""
+    itype = _lib.I64 if index_dtype == np.int64 else _lib.I32
+    tidx = torch.int64 if itype == _lib.I64 else torch.int32
+    tval = torch.float64 if scalar_dtype == np.float64 else torch.float32
+    with torch.cuda.device(device):
+        indptr = torch.empty(rows + 1, dtype=tidx, device=device)
+        indices = torch.empty(max(n, 1), dtype=tidx, device=device)
+        values = torch.empty(max(n, 1), dtype=tval, device=device)
+        run(indptr, indices, values, itype)
+        return sp.csr_matrix((values[:n].cpu().numpy(), indices[:n].cpu().numpy(), indptr.cpu().numpy()),
+                             shape=(rows, cols))
+
+
 def boo_to_csr(boo_mat) -> sp.csr_matrix:
     """Rows collected from blocks, remainder and tail, each row sorted by
-    (col, value) -- boo_matrix.cpp:277-333."""
+    (col, value) -- boo_matrix.cpp:277-333 -- on the GPU (spmm_boo_to_csr)."""
     index_dtype, scalar_dtype = _BOO_TYPE_MAP[type(boo_mat).__name__]
-    h = boo_mat._host_arrays()
-    rgp = h['row_grp_ptr'].astype(np.int64)
-    cgp = h['col_grp_ptr'].astype(np.int64)
-    bnz = h['blk_nz_ptr'].astype(np.int64)
-    nb = int(bnz.size - 1)
-    per = np.diff(bnz)
-    blk = np.repeat(np.arange(nb, dtype=np.int64), per)
-    shift = h['blk_shift'].astype(np.int64)[blk]
-    idx = h['nz_idx'].astype(np.int64)
-    lr, lc = idx >> shift, idx & ((np.int64(1) << shift) - 1)
-    gr = h['row_ids'].astype(np.int64)[rgp[h['blk_row_grp'].astype(np.int64)[blk]] + lr]
-    gc = h['col_ids'].astype(np.int64)[cgp[h['blk_col_grp'].astype(np.int64)[blk]] + lc]
-    rem_rows = np.repeat(np.arange(boo_mat.rows, dtype=np.int64), np.diff(h['rem_indptr'].astype(np.int64)))
-    rows = np.concatenate([gr, rem_rows, h['tail_row'].astype(np.int64)])
-    cols = np.concatenate([gc, h['rem_col_ind'].astype(np.int64), h['tail_col'].astype(np.int64)])
-    vals = np.concatenate([h['nz_val'], h['rem_vals'], h['tail_val']]).astype(scalar_dtype)
-    order = np.lexsort((vals, cols, rows))
-    counts = np.bincount(rows, minlength=boo_mat.rows)
-    indptr = np.concatenate([[0], np.cumsum(counts)]).astype(index_dtype)
-    return sp.csr_matrix((vals[order], cols[order].astype(index_dtype), indptr),
-                         shape=(boo_mat.rows, boo_mat.cols))
+    require_cuda('boo_to_csr')
+    meta = boo_mat._gpu_meta
+    device = meta.nz_val.device if meta is not None else default_device()
+    if meta is None:
+        meta = boo_mat._staged_on(device)
+    st = boo_mat._dev_struct(meta)
+    n = int(boo_mat._sizes['nnz_c'] + boo_mat._sizes['rem_nnz'] + boo_mat._sizes['tail_nnz'])
+    L = _lib.lib()
+
+    def run(indptr, indices, values, itype):
+        ws_bytes = L.spmm_boo_to_csr_workspace_size(C.byref(st))
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
+        _lib.check(L.spmm_boo_to_csr(C.byref(st), ptr(indptr), ptr(indices), ptr(values), itype, ptr(ws),
+                                     ws_bytes, stream_handle(device)), 'boo_to_csr')
+
+    return _csr_from_device(boo_mat.rows, boo_mat.cols, n, index_dtype, scalar_dtype, device, run)
 
 
 # ---------------------------------------------------------------------------

@@ -258,36 +258,29 @@ def csr_to_pbr(mat, block_rows: int = 8, block_cols: int = 8, min_nnz_per_block:
 
 def pbr_to_csr(pbr_mat) -> sp.csr_matrix:
     """Blocks (bit order) + remainder, rows sorted by (col, value)
-    (pbr_matrix.cpp:279-331)."""
+    (pbr_matrix.cpp:279-331), on the GPU (spmm_pbr_to_csr)."""
+    from .boo import _csr_from_device
     index_dtype, scalar_dtype = _PBR_TYPE_MAP[type(pbr_mat).__name__]
-    h = pbr_mat._host_arrays()
-    br, bc = pbr_mat.block_rows, pbr_mat.block_cols
-    codes = h['block_codes'].astype(np.uint64)
-    coords = h['block_coords'].astype(np.int64).reshape(-1, 2)
-    nb = codes.size
-    rows_l, cols_l = [], []
-    if nb:
-        bits = np.arange(br * bc, dtype=np.uint64)
-        mask = ((codes[:, None] >> bits[None, :]) & np.uint64(1)).astype(bool)
-        bidx, bit = np.nonzero(mask)              # block-major, bit order
-        gr = coords[bidx, 0] + bit // bc
-        gc = coords[bidx, 1] + bit % bc
-        if np.any(gr >= pbr_mat.rows):
+    require_cuda('pbr_to_csr')
+    meta = pbr_mat._gpu_meta
+    device = meta.codes.device if meta is not None else default_device()
+    if meta is None:
+        meta = pbr_mat._staged_on(device)
+    st = pbr_mat._dev_struct(meta)
+    n = int(pbr_mat._sizes['nnz_c'] + pbr_mat._sizes['rem_nnz'])
+    L = _lib.lib()
+
+    def run(indptr, indices, values, itype):
+        ws_bytes = L.spmm_pbr_to_csr_workspace_size(C.byref(st))
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
+        rc = L.spmm_pbr_to_csr(C.byref(st), ptr(indptr), ptr(indices), ptr(values), itype, ptr(ws), ws_bytes,
+                               stream_handle(device))
+        if rc == _lib.SPMM_EINVAL:
             raise RuntimeError('Block has a nonzero past the last matrix row. Check block size and '
                                'matrix dimensions for compatibility.')
-        rows_l.append(gr)
-        cols_l.append(gc)
-    rem_rows = np.repeat(np.arange(pbr_mat.rows, dtype=np.int64),
-                         np.diff(h['remainder_indptr'].astype(np.int64)))
-    rows_a = np.concatenate(rows_l + [rem_rows])
-    cols_a = np.concatenate(cols_l + [h['remainder_col_ind'].astype(np.int64)])
-    vals = np.concatenate([h['block_data'][:sum(x.size for x in rows_l)], h['remainder_data']])
-    vals = vals.astype(scalar_dtype)
-    order = np.lexsort((vals, cols_a, rows_a))
-    counts = np.bincount(rows_a, minlength=pbr_mat.rows)
-    indptr = np.concatenate([[0], np.cumsum(counts)]).astype(index_dtype)
-    return sp.csr_matrix((vals[order], cols_a[order].astype(index_dtype), indptr),
-                         shape=(pbr_mat.rows, pbr_mat.cols))
+        _lib.check(rc, 'pbr_to_csr')
+
+    return _csr_from_device(pbr_mat.rows, pbr_mat.cols, n, index_dtype, scalar_dtype, device, run)
 
 
 def _run_pbr(pbr_mat, meta, x: torch.Tensor) -> torch.Tensor:
