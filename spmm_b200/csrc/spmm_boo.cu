@@ -153,16 +153,19 @@ boo_spmm_kernel(const BooParams<S> p) {
     // row groups [rg_begin, rg_end); blocks found by one search, then walked
     const int64_t rg_begin = (int64_t)blockIdx.x * p.rgs_per_cta;
     const int64_t rg_end = rg_begin + p.rgs_per_cta < p.n_rg ? rg_begin + p.rgs_per_cta : p.n_rg;
-    if (tid == 0) sm.blk_hi = lower_bound_i32(p.blk_row_grp, p.nb, rg_begin);
+    if (warp == 0) {   // 32-way searches by warp 0
+        const int64_t lo0 = warp_lower_bound(p.blk_row_grp, p.nb, rg_begin, lane);
+        if (lane == 0) sm.blk_hi = lo0;
+    }
     for (int64_t rg = rg_begin; rg < rg_end; ++rg) {
     __syncthreads();   // the previous group's readers of sm are done
-    if (tid == 0) {
+    if (warp == 0) {
         const int64_t lo = sm.blk_hi;
-        int64_t hi = lo;
-        if (lo < p.nb && p.blk_row_grp[lo] == rg)
-            hi = lo + 1 + lower_bound_i32(p.blk_row_grp + lo + 1, p.nb - lo - 1, rg + 1);
-        sm.blk_lo = lo;
-        sm.blk_hi = hi;
+        const int64_t hi = group_end(p.blk_row_grp, p.nb, lo, rg, lane);
+        if (lane == 0) {
+            sm.blk_lo = lo;
+            sm.blk_hi = hi;
+        }
     }
     __syncthreads();
     const int64_t blk_lo = sm.blk_lo, blk_hi = sm.blk_hi;

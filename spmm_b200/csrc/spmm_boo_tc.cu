@@ -227,24 +227,6 @@ __device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__flo
 
 __device__ __forceinline__ bool finite(float x) { return fabsf(x) <= 3.402823466e38f; }
 
-// First index i in [0, n) with a[i] >= key (a ascending), by a 32-way search
-// of the whole warp.
-__device__ __forceinline__ int64_t warp_lower_bound(const int32_t *a, int64_t n, int64_t key, int lane) {
-    int64_t lo = 0, hi = n;
-    while (hi - lo > 32) {
-        const int64_t step = (hi - lo + 31) / 32;
-        const int64_t pi = lo + lane * step;
-        const bool pred = pi < hi && (int64_t)__ldg(a + pi) < key;
-        const int c = __popc(__ballot_sync(kFullMask, pred));
-        if (c == 0) return lo;
-        const int64_t nhi = lo + c * step;
-        lo = lo + (c - 1) * step + 1;
-        hi = nhi < hi ? nhi : hi;
-    }
-    const int64_t pi = lo + lane;
-    const bool pred = pi < hi && (int64_t)__ldg(a + pi) < key;
-    return lo + __popc(__ballot_sync(kFullMask, pred));
-}
 
 // ---- the worker ----------------------------------------------------------------
 
@@ -256,18 +238,6 @@ __device__ __forceinline__ bool drain_phase(uint64_t *bar, uint32_t parity) {
     while (!mbar_try_wait(bar, parity))
         if (clock64() - t0 > kWaitCycles) return false;
     return true;
-}
-
-// One past the last block of row group rg, scanning forward from b (the
-// first block with row group >= rg); row groups hold a handful of blocks.
-__device__ __forceinline__ int64_t group_end(const int32_t *blk_row_grp, int64_t nb, int64_t b, int64_t rg,
-                                             int lane) {
-    for (;; b += 32) {
-        const int64_t i = b + lane;
-        const bool in = i < nb && (int64_t)__ldg(blk_row_grp + i) <= rg;
-        const unsigned m = __ballot_sync(kFullMask, in);
-        if (m != kFullMask) return b + __popc(m);   // the group's blocks are a prefix
-    }
 }
 
 // CUDA-core part of a row group, summed into w.ys (thread f owns column f):
