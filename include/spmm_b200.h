@@ -260,6 +260,18 @@ size_t spmm_pbr_to_csr_workspace_size(const spmm_pbr_dev *A);
 int spmm_pbr_to_csr(const spmm_pbr_dev *A, void *indptr, void *indices, void *values, int index_type,
                     void *workspace, size_t workspace_bytes, spmm_stream_t stream);
 
+/* Multilevel heavy-edge matching labels on the GPU (replaces the host HEM of
+ * torch_fast_spdmm/torch_fast_spdmm/clustering.py:128-351, cluster='hem'):
+ * one label per row of the binary pattern (indptr int64 rows+1, indices int32,
+ * canonical: sorted, no duplicates), equal to the reference algorithm's
+ * labels before its cap enforcement.  Columns of degree > hub_degree are
+ * ignored, each row keeps its topk heaviest similarity edges (topk < 0: all),
+ * max_size / max_nnz < 0 mean no cap.  labels: rows int64 (device).  Scratch
+ * from the stream-ordered allocator; synchronises the stream. */
+int spmm_hem_labels(int64_t rows, int64_t cols, const int64_t *indptr, const int32_t *indices, int64_t target,
+                    int64_t max_size, int64_t max_nnz, int64_t hub_degree, int64_t topk, int32_t residual_rounds,
+                    int32_t feasible_first, int64_t *labels, spmm_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -35,7 +35,7 @@ EXPORTS = ('spmm_status_string', 'spmm_abi_version', 'spmm_boo_build_workspace_s
            'spmm_pbr_build_analyze', 'spmm_pbr_build_emit', 'spmm_boo_matmul', 'spmm_pbr_matmul',
            'spmm_tc_status', 'spmm_boo_matmul_workspace_size', 'spmm_product_launches',
            'spmm_boo_to_csr_workspace_size', 'spmm_boo_to_csr', 'spmm_pbr_to_csr_workspace_size',
-           'spmm_pbr_to_csr')
+           'spmm_pbr_to_csr', 'spmm_hem_labels')
 
 
 class CsrDev(C.Structure):
@@ -135,6 +135,10 @@ def lib() -> C.CDLL:
         L.spmm_pbr_to_csr.argtypes = [C.POINTER(PbrDev), C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
                                       C.c_void_p, C.c_size_t, C.c_void_p]
         L.spmm_boo_to_csr.restype = C.c_int
+        L.spmm_hem_labels.argtypes = [C.c_int64, C.c_int64, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64,
+                                      C.c_int64, C.c_int64, C.c_int64, C.c_int32, C.c_int32, C.c_void_p,
+                                      C.c_void_p]
+        L.spmm_hem_labels.restype = C.c_int
         L.spmm_pbr_to_csr.restype = C.c_int
         for n in ('spmm_boo_build_analyze', 'spmm_boo_build_emit', 'spmm_pbr_build_analyze',
                   'spmm_pbr_build_emit', 'spmm_boo_matmul', 'spmm_pbr_matmul'):

@@ -16,8 +16,9 @@ from typing import Optional, Tuple
 
 import numpy as np
 import scipy.sparse as sp
+import torch
 
-__all__ = ['cluster_axes', 'cluster_axis', 'CLUSTER_METHODS']
+__all__ = ['cluster_axes', 'cluster_axis', 'hem_labels_gpu', 'CLUSTER_METHODS']
 
 CLUSTER_METHODS = ('identity', 'random', 'degree', 'rcm', 'hem', 'graclus', 'metis')
 DEFAULT_HUB_DEGREE = 1024
@@ -82,6 +83,30 @@ def _enforce_caps(labels, row_nnz, max_size, max_nnz):
     return out
 
 
+def hem_labels_gpu(pat: sp.csr_matrix, target: int, max_size: Optional[int], max_nnz: Optional[int],
+                   hub_degree: int = DEFAULT_HUB_DEGREE, topk: Optional[int] = DEFAULT_TOPK,
+                   feasible_first: bool = False, residual_rounds: int = 3) -> np.ndarray:
+    """HEM labels of the rows of a canonical binary pattern on the current
+    CUDA device (spmm_hem_labels); the same labels as the host restatement
+    ``_hem.hem_labels`` (before cap enforcement)."""
+    from . import _lib
+    from ._device import default_device, ptr, stream_handle
+    n, m = pat.shape
+    if n == 0:
+        return np.zeros(0, dtype=np.int64)
+    dev = default_device()
+    with torch.cuda.device(dev):
+        indptr = torch.from_numpy(np.ascontiguousarray(pat.indptr, dtype=np.int64)).to(dev)
+        indices = torch.from_numpy(np.ascontiguousarray(pat.indices, dtype=np.int32)).to(dev)
+        labels = torch.empty(n, dtype=torch.int64, device=dev)
+        rc = _lib.lib().spmm_hem_labels(
+            n, m, ptr(indptr), ptr(indices), int(target), -1 if max_size is None else int(max_size),
+            -1 if max_nnz is None else int(max_nnz), int(hub_degree), -1 if topk is None else int(topk),
+            int(residual_rounds), 1 if feasible_first else 0, ptr(labels), stream_handle(dev))
+        _lib.check(rc, 'hem_labels')
+        return labels.cpu().numpy()
+
+
 def cluster_axis(mat, method: str = 'hem', target: int = 32, max_size: Optional[int] = None,
                  max_nnz: Optional[int] = None, seed: int = 0,
                  hub_degree: int = DEFAULT_HUB_DEGREE, topk: Optional[int] = DEFAULT_TOPK,
@@ -118,6 +143,8 @@ def cluster_axis(mat, method: str = 'hem', target: int = 32, max_size: Optional[
     elif method == 'metis':
         raise ImportError("cluster='metis' requires pymetis, which is not installed; "
                           'no HEM fallback is performed')
+    elif hem_hierarchy is None and exact_recompute and torch.cuda.is_available():
+        labels = hem_labels_gpu(pat, target, max_size, max_nnz, hub_degree, topk, feasible_first)
     else:
         from ._hem import hem_labels
         labels = hem_labels(pat, target, max_size, max_nnz, hub_degree, topk, exact_recompute,

@@ -1,0 +1,659 @@
+// hem.cu -- multilevel heavy-edge matching (HEM) labels on the GPU, the
+// reference's default BOO clustering (torch_fast_spdmm/torch_fast_spdmm/
+// clustering.py:128-351), with the same result as its host restatement.
+//
+// Per level, on the binary pattern P of the current (contracted) rows:
+//   * similarity graph (clustering.py:128-185): columns of degree above
+//     hub_degree are dropped; w(i, j) = shared columns of rows i != j.  Every
+//     (i, j) incidence is generated for a chunk of rows, radix-sorted and
+//     run-length counted; a second sort by (i, -w, j) keeps each row's topk
+//     heaviest (ties by column); the directed lists are united over both
+//     directions (w is symmetric, so max(G, G^T) is the union);
+//   * up to residual_rounds matching rounds (:188-268): each active vertex
+//     picks its best live edge by (w desc, pair hash desc, column asc);
+//     mutual picks whose merge respects the size / nnz caps are merged;
+//   * contraction (:271-351): new rows are the unions of the matched pairs'
+//     column sets (rows in index order of their smaller member); the loop
+//     ends when a level matches nothing.
+// Everything is integer arithmetic with the reference's tie-breaks, so the
+// labels are identical.  Scratch comes from the stream-ordered allocator.
+#include <algorithm>
+#include <utility>
+#include <vector>
+
+#include "common.cuh"
+
+namespace spmm {
+namespace {
+
+constexpr int kHemThreads = 256;
+constexpr int64_t kPairBudget = 1ll << 27;   // (i, j) incidences sorted per chunk
+
+template <typename T>
+struct DBuf {
+    T *p = nullptr;
+    cudaStream_t s = nullptr;
+    DBuf() = default;
+    DBuf(const DBuf &) = delete;
+    DBuf &operator=(const DBuf &) = delete;
+    int alloc(int64_t n, cudaStream_t st) {
+        release();
+        s = st;
+        return cudaMallocAsync(&p, (size_t)(n > 0 ? n : 1) * sizeof(T), st) == cudaSuccess ? SPMM_OK : SPMM_ECUDA;
+    }
+    void release() {
+        if (p) cudaFreeAsync(p, s);
+        p = nullptr;
+    }
+    ~DBuf() { release(); }
+};
+
+template <typename T>
+int to_host(T *dst, const T *src, int64_t n, cudaStream_t s) {
+    if (n <= 0) return SPMM_OK;
+    SPMM_CUDA_TRY(cudaMemcpyAsync(dst, src, (size_t)n * sizeof(T), cudaMemcpyDeviceToHost, s));
+    SPMM_CUDA_TRY(cudaStreamSynchronize(s));
+    return SPMM_OK;
+}
+
+inline unsigned warps_grid(int64_t rows) { return grid_for(rows * 32, kHemThreads); }
+
+// Symmetric 63-bit hash of the unordered pair {a, b} (a splitmix64 mix of the
+// ordered pair (min, max)); the same function as the host restatement.
+__device__ __forceinline__ uint64_t pair_hash(int64_t a, int64_t b) {
+    const uint64_t lo = (uint64_t)(a < b ? a : b), hi = (uint64_t)(a < b ? b : a);
+    uint64_t h = (lo * 0x9E3779B97F4A7C15ull) ^ (hi * 0xC2B2AE3D27D4EB4Full);
+    h ^= h >> 30;
+    h *= 0xBF58476D1CE4E5B9ull;
+    h ^= h >> 27;
+    h *= 0x94D049BB133111EBull;
+    h ^= h >> 31;
+    return h >> 1;
+}
+
+__global__ void col_deg_kernel(const int32_t *__restrict__ idx, int64_t nnz, uint32_t *__restrict__ deg) {
+    for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < nnz; k += (int64_t)gridDim.x * blockDim.x)
+        atomicAdd(deg + idx[k], 1u);
+}
+
+// Warp per row: kept entries (column degree <= hub) -- count (out == null) or
+// emit in order; also the row's incidence count (sum of kept column degrees).
+__global__ void prune_kernel(const int64_t *__restrict__ ptr, const int32_t *__restrict__ idx, int64_t n,
+                             const uint32_t *__restrict__ deg, uint32_t hub, int64_t *__restrict__ cnt,
+                             int64_t *__restrict__ pairs, const int64_t *__restrict__ optr,
+                             int32_t *__restrict__ out) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = (int64_t)gridDim.x * (blockDim.x / 32);
+    for (int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32; r < n; r += nw) {
+        const int64_t e0 = ptr[r], e1 = ptr[r + 1];
+        int64_t kept = 0, inc = 0;
+        int64_t o = out ? optr[r] : 0;
+        for (int64_t b = e0; b < e1; b += 32) {
+            const int64_t k = b + lane;
+            const int32_t c = k < e1 ? idx[k] : 0;
+            const uint32_t d = k < e1 ? deg[c] : 0u;
+            const bool keep = k < e1 && d <= hub;
+            const unsigned m = __ballot_sync(kFullMask, keep);
+            if (out && keep) out[o + __popc(m & lanemask_lt())] = c;
+            o += __popc(m);
+            kept += __popc(m);
+            uint64_t s = keep ? d : 0u;
+#pragma unroll
+            for (int w = 16; w > 0; w >>= 1) s += __shfl_xor_sync(kFullMask, s, w);
+            inc += (int64_t)s;
+        }
+        if (lane == 0 && !out) {
+            cnt[r] = kept;
+            pairs[r] = inc;
+        }
+    }
+}
+
+// Column-major copy of the pruned pattern: rows of each kept column.
+__global__ void transpose_kernel(const int64_t *__restrict__ ptr, const int32_t *__restrict__ idx, int64_t n,
+                                 const int64_t *__restrict__ tptr, uint32_t *__restrict__ tcur,
+                                 int32_t *__restrict__ trow) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = (int64_t)gridDim.x * (blockDim.x / 32);
+    for (int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32; r < n; r += nw)
+        for (int64_t k = ptr[r] + lane; k < ptr[r + 1]; k += 32) {
+            const int32_t c = idx[k];
+            trow[tptr[c] + atomicAdd(tcur + c, 1u)] = (int32_t)r;
+        }
+}
+
+// Warp per row i of [r0, r1): every incidence (i, j) through a kept column as
+// key (i - r0) << jb | j; j == i becomes the all-ones sentinel (sorts last).
+__global__ void gen_pairs_kernel(const int64_t *__restrict__ ptr, const int32_t *__restrict__ idx,
+                                 const int64_t *__restrict__ tptr, const int32_t *__restrict__ trow,
+                                 const int64_t *__restrict__ pstart, int64_t r0, int64_t r1, int jb,
+                                 uint64_t sentinel, uint64_t *__restrict__ keys) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = (int64_t)gridDim.x * (blockDim.x / 32);
+    for (int64_t i = r0 + ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32; i < r1; i += nw) {
+        int64_t o = pstart[i] - pstart[r0];
+        for (int64_t k = ptr[i]; k < ptr[i + 1]; ++k) {
+            const int32_t c = idx[k];
+            const int64_t t0 = tptr[c], t1 = tptr[c + 1];
+            for (int64_t t = t0 + lane; t < t1; t += 32) {
+                const int64_t j = trow[t];
+                keys[o + (t - t0)] = j == i ? sentinel : ((uint64_t)(i - r0) << jb) | (uint64_t)j;
+            }
+            o += t1 - t0;
+        }
+    }
+}
+
+// Run heads of the sorted keys (sentinels excluded): flag 1 at a new key.
+__global__ void head_flags_kernel(const uint64_t *__restrict__ keys, int64_t n, uint64_t sentinel,
+                                  int64_t *__restrict__ flag) {
+    for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < n; k += (int64_t)gridDim.x * blockDim.x)
+        flag[k] = keys[k] != sentinel && (k == 0 || keys[k] != keys[k - 1]) ? 1 : 0;
+}
+
+// Unique (i, j) with its count w, re-keyed (i << (wb + jb)) | (wmax - w) << jb | j
+// so one ascending sort orders each row by (w desc, j asc).
+__global__ void rle_kernel(const uint64_t *__restrict__ keys, int64_t n, uint64_t sentinel,
+                           const int64_t *__restrict__ pos, int jb, int wb, uint64_t *__restrict__ out) {
+    for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < n; k += (int64_t)gridDim.x * blockDim.x) {
+        const uint64_t key = keys[k];
+        if (key == sentinel || (k > 0 && key == keys[k - 1])) continue;
+        int64_t e = k + 1;
+        while (e < n && keys[e] == key) ++e;
+        const uint64_t w = (uint64_t)(e - k);
+        const uint64_t il = key >> jb, j = key & ((1ull << jb) - 1ull);
+        const uint64_t wmax = (1ull << wb) - 1ull;
+        out[pos[k]] = (il << (wb + jb)) | ((wmax - (w < wmax ? w : wmax)) << jb) | j;
+    }
+}
+
+// Sorted (row, -w, j) keys -> each row's first topk as directed edges (i, j, w).
+__global__ void topk_flags_kernel(const uint64_t *__restrict__ keys, int64_t n, int jb, int wb, int64_t topk,
+                                  int64_t *__restrict__ flag) {
+    const int sh = wb + jb;
+    for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < n; k += (int64_t)gridDim.x * blockDim.x) {
+        const uint64_t row = keys[k] >> sh;
+        bool keep = true;
+        if (topk >= 0) {
+            // the row's first topk entries: the entry topk places back is of another row
+            keep = k < topk || (keys[k - topk] >> sh) != row;
+        }
+        flag[k] = keep ? 1 : 0;
+    }
+}
+
+__global__ void topk_emit_kernel(const uint64_t *__restrict__ keys, int64_t n, const int64_t *__restrict__ flag,
+                                 const int64_t *__restrict__ pos, int64_t r0, int jb, int wb, int64_t ebase,
+                                 uint64_t *__restrict__ ekey, uint32_t *__restrict__ ew) {
+    const int sh = wb + jb;
+    const uint64_t wmax = (1ull << wb) - 1ull, jm = (1ull << jb) - 1ull;
+    for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < n; k += (int64_t)gridDim.x * blockDim.x) {
+        if (!flag[k]) continue;
+        const uint64_t key = keys[k];
+        const uint64_t i = (key >> sh) + (uint64_t)r0, j = key & jm;
+        const uint32_t w = (uint32_t)(wmax - ((key >> jb) & wmax));
+        const int64_t o = ebase + 2 * pos[k];
+        ekey[o] = (i << jb) | j;   // both directions; equal pairs collapse after the sort
+        ekey[o + 1] = (j << jb) | i;
+        ew[o] = w;
+        ew[o + 1] = w;
+    }
+}
+
+// Sorted directed edge keys -> symmetric graph CSR (duplicates dropped).
+__global__ void edge_heads_kernel(const uint64_t *__restrict__ key, int64_t n, int64_t *__restrict__ flag,
+                                  int jb, unsigned long long *__restrict__ rowcnt) {
+    for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < n; k += (int64_t)gridDim.x * blockDim.x) {
+        const bool head = k == 0 || key[k] != key[k - 1];
+        flag[k] = head ? 1 : 0;
+        if (head) atomicAdd(rowcnt + (key[k] >> jb), 1ull);
+    }
+}
+
+__global__ void edge_emit_kernel(const uint64_t *__restrict__ key, const uint32_t *__restrict__ w, int64_t n,
+                                 const int64_t *__restrict__ flag, const int64_t *__restrict__ pos, int jb,
+                                 int32_t *__restrict__ gcol, uint32_t *__restrict__ gw) {
+    for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < n; k += (int64_t)gridDim.x * blockDim.x) {
+        if (!flag[k]) continue;
+        gcol[pos[k]] = (int32_t)(key[k] & ((1ull << jb) - 1ull));
+        gw[pos[k]] = w[k];
+    }
+}
+
+struct Caps {
+    int64_t max_size, max_nnz;   // < 0: none
+    __device__ __forceinline__ bool ok(const int64_t *size, const int64_t *nnz, int64_t a, int64_t b) const {
+        return (max_size < 0 || size[a] + size[b] <= max_size) && (max_nnz < 0 || nnz[a] + nnz[b] <= max_nnz);
+    }
+};
+
+// Warp per vertex: its best live edge by (w desc, hash desc, column asc).
+__global__ void best_kernel(const unsigned long long *__restrict__ gptr, const int32_t *__restrict__ gcol,
+                            const uint32_t *__restrict__ gw, int64_t n, const uint8_t *__restrict__ active,
+                            const int64_t *__restrict__ size, const int64_t *__restrict__ nnz, Caps caps,
+                            int feasible_first, int64_t *__restrict__ best) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = (int64_t)gridDim.x * (blockDim.x / 32);
+    for (int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32; r < n; r += nw) {
+        uint32_t bw = 0;
+        uint64_t bh = 0;
+        int64_t bc = -1;
+        if (active[r]) {
+            for (int64_t e = (int64_t)gptr[r] + lane; e < (int64_t)gptr[r + 1]; e += 32) {
+                const int64_t c = gcol[e];
+                if (!active[c] || (feasible_first && !caps.ok(size, nnz, r, c))) continue;
+                const uint32_t w = gw[e];
+                const uint64_t h = pair_hash(r, c);
+                if (bc < 0 || w > bw || (w == bw && (h > bh || (h == bh && c < bc)))) {
+                    bw = w;
+                    bh = h;
+                    bc = c;
+                }
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const uint32_t ow = __shfl_xor_sync(kFullMask, bw, o);
+            const uint64_t oh = __shfl_xor_sync(kFullMask, bh, o);
+            const int64_t oc = __shfl_xor_sync(kFullMask, bc, o);
+            if (oc >= 0 && (bc < 0 || ow > bw || (ow == bw && (oh > bh || (oh == bh && oc < bc))))) {
+                bw = ow;
+                bh = oh;
+                bc = oc;
+            }
+        }
+        if (lane == 0) best[r] = bc;
+    }
+}
+
+// Mutual picks (r < best[r]) that respect the caps: matched, deactivated.
+__global__ void mutual_kernel(const int64_t *__restrict__ best, int64_t n, const int64_t *__restrict__ size,
+                              const int64_t *__restrict__ nnz, Caps caps, int64_t *__restrict__ mate,
+                              uint8_t *__restrict__ active, unsigned long long *__restrict__ matched) {
+    for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < n; r += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t b = best[r];
+        if (b > r && best[b] == r && caps.ok(size, nnz, r, b)) {
+            mate[r] = b;
+            mate[b] = r;
+            active[r] = 0;
+            active[b] = 0;
+            atomicAdd(matched, 1ull);
+        }
+    }
+}
+
+// 1 for vertices that stay a row of the next level (not the larger member of a pair).
+__global__ void root_flags_kernel(const int64_t *__restrict__ mate, int64_t n, int64_t *__restrict__ flag) {
+    for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < n; r += (int64_t)gridDim.x * blockDim.x)
+        flag[r] = (mate[r] >= 0 && mate[r] < r) ? 0 : 1;
+}
+
+// new_id of every vertex; sizes / nnz summed into the new rows; the new
+// pattern's row lengths (union of the pair's sorted columns).
+__global__ void contract_kernel(const int64_t *__restrict__ mate, int64_t n, const int64_t *__restrict__ rank,
+                                const int64_t *__restrict__ size, const int64_t *__restrict__ nnz,
+                                const int64_t *__restrict__ ptr, const int32_t *__restrict__ idx,
+                                int64_t *__restrict__ new_id, unsigned long long *__restrict__ nsize,
+                                unsigned long long *__restrict__ nnnz, int64_t *__restrict__ nlen) {
+    for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < n; r += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t m = mate[r];
+        const int64_t root = (m >= 0 && m < r) ? m : r;
+        const int64_t id = rank[root];
+        new_id[r] = id;
+        atomicAdd(nsize + id, (unsigned long long)size[r]);
+        atomicAdd(nnnz + id, (unsigned long long)nnz[r]);
+        if (root != r) continue;
+        int64_t len = ptr[r + 1] - ptr[r];
+        if (m > r) {   // |A u B| of two sorted lists
+            int64_t a = ptr[r], ae = ptr[r + 1], b = ptr[m], be = ptr[m + 1];
+            len = 0;
+            while (a < ae || b < be) {
+                const int32_t x = a < ae ? idx[a] : INT32_MAX, y = b < be ? idx[b] : INT32_MAX;
+                if (x <= y) ++a;
+                if (y <= x) ++b;
+                ++len;
+            }
+        }
+        nlen[id] = len;
+    }
+}
+
+__global__ void contract_emit_kernel(const int64_t *__restrict__ mate, int64_t n, const int64_t *__restrict__ rank,
+                                     const int64_t *__restrict__ ptr, const int32_t *__restrict__ idx,
+                                     const int64_t *__restrict__ nptr, int32_t *__restrict__ nidx) {
+    for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < n; r += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t m = mate[r];
+        if (m >= 0 && m < r) continue;
+        int64_t o = nptr[rank[r]];
+        int64_t a = ptr[r], ae = ptr[r + 1];
+        int64_t b = m > r ? ptr[m] : 0, be = m > r ? ptr[m + 1] : 0;
+        while (a < ae || b < be) {
+            const int32_t x = a < ae ? idx[a] : INT32_MAX, y = b < be ? idx[b] : INT32_MAX;
+            nidx[o++] = x <= y ? x : y;
+            if (x <= y) ++a;
+            if (y <= x) ++b;
+        }
+    }
+}
+
+__global__ void relabel_kernel(int64_t *__restrict__ labels, int64_t n, const int64_t *__restrict__ new_id) {
+    for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < n; v += (int64_t)gridDim.x * blockDim.x)
+        labels[v] = new_id[labels[v]];
+}
+
+template <typename T>
+__global__ void copy_cast_kernel(const unsigned long long *__restrict__ in, T *__restrict__ out, int64_t n) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        out[i] = (T)in[i];
+}
+
+__global__ void iota64_kernel(int64_t *__restrict__ out, int64_t n) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        out[i] = i;
+}
+
+__global__ void fill_kernel(int64_t *__restrict__ out, int64_t n, int64_t v) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        out[i] = v;
+}
+
+__global__ void widen_kernel(const uint32_t *__restrict__ in, int64_t *__restrict__ out, int64_t n) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        out[i] = in[i];
+}
+
+__global__ void diff_kernel(const int64_t *__restrict__ ptr, int64_t n, int64_t *__restrict__ out) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        out[i] = ptr[i + 1] - ptr[i];
+}
+
+// exclusive scan of n int64 counts into out[0..n], out[n] = total (copied to the host when asked)
+int scan_counts(const int64_t *in, int64_t *out, int64_t n, cudaStream_t s, int64_t *total_host) {
+    DBuf<int64_t> tmp;
+    SPMM_TRY(tmp.alloc(scan_temp_elems(n), s));
+    SPMM_TRY(exclusive_scan<int64_t>(in, out, n, tmp.p, out + n, s));
+    if (total_host) SPMM_TRY(to_host(total_host, out + n, 1, s));
+    return SPMM_OK;
+}
+
+// Stable radix sort of 64-bit keys by their low `bits` (a byte payload rides along).
+int sort_keys(DBuf<uint64_t> &k0, DBuf<uint64_t> &k1, int64_t n, int bits, cudaStream_t s) {
+    DBuf<uint8_t> v0, v1;
+    DBuf<uint32_t> tmp;
+    SPMM_TRY(v0.alloc(n, s));
+    SPMM_TRY(v1.alloc(n, s));
+    SPMM_TRY(tmp.alloc(radix_temp_elems(n), s));
+    bool first = true;
+    SPMM_TRY(radix_sort_pairs<uint64_t, uint8_t>(k0.p, v0.p, k1.p, v1.p, n, bits, tmp.p, &first, s));
+    if (!first) std::swap(k0.p, k1.p);
+    return SPMM_OK;
+}
+
+// One level's similarity graph as CSR over the n rows (gptr, gcol, gw).
+int similarity_graph(const int64_t *ptr, const int32_t *idx, int64_t n, int64_t m, int64_t nnz, uint32_t hub,
+                     int64_t topk, DBuf<unsigned long long> &gptr, DBuf<int32_t> &gcol, DBuf<uint32_t> &gw,
+                     int64_t *gnnz, cudaStream_t s) {
+    *gnnz = 0;
+    const int jb = bit_width_u64((uint64_t)(n > 1 ? n - 1 : 1));
+    DBuf<uint32_t> deg;
+    SPMM_TRY(deg.alloc(m, s));
+    SPMM_CUDA_TRY(cudaMemsetAsync(deg.p, 0, (size_t)m * 4, s));
+    if (nnz) {
+        col_deg_kernel<<<grid_for(nnz, kHemThreads), kHemThreads, 0, s>>>(idx, nnz, deg.p);
+        SPMM_LAUNCH_CHECK();
+    }
+    // pruned pattern (kept columns, in order) and each row's incidence count
+    DBuf<int64_t> pcnt, pinc, pptr, pstart;
+    SPMM_TRY(pcnt.alloc(n + 1, s));
+    SPMM_TRY(pinc.alloc(n + 1, s));
+    SPMM_TRY(pptr.alloc(n + 1, s));
+    SPMM_TRY(pstart.alloc(n + 1, s));
+    prune_kernel<<<warps_grid(n), kHemThreads, 0, s>>>(ptr, idx, n, deg.p, hub, pcnt.p, pinc.p, nullptr, nullptr);
+    SPMM_LAUNCH_CHECK();
+    int64_t pnnz = 0, npairs = 0;
+    SPMM_TRY(scan_counts(pcnt.p, pptr.p, n, s, &pnnz));
+    SPMM_TRY(scan_counts(pinc.p, pstart.p, n, s, &npairs));
+    if (pnnz == 0 || npairs == 0) return SPMM_OK;
+    DBuf<int32_t> pidx;
+    SPMM_TRY(pidx.alloc(pnnz, s));
+    prune_kernel<<<warps_grid(n), kHemThreads, 0, s>>>(ptr, idx, n, deg.p, hub, nullptr, nullptr, pptr.p, pidx.p);
+    SPMM_LAUNCH_CHECK();
+    // rows of each kept column
+    DBuf<int64_t> tdeg, tptr;
+    DBuf<int32_t> trow;
+    SPMM_TRY(tdeg.alloc(m + 1, s));
+    SPMM_TRY(tptr.alloc(m + 1, s));
+    SPMM_TRY(trow.alloc(pnnz, s));
+    {
+        DBuf<uint32_t> tcur;
+        SPMM_TRY(tcur.alloc(m, s));
+        SPMM_CUDA_TRY(cudaMemsetAsync(tcur.p, 0, (size_t)m * 4, s));
+        col_deg_kernel<<<grid_for(pnnz, kHemThreads), kHemThreads, 0, s>>>(pidx.p, pnnz, tcur.p);
+        SPMM_LAUNCH_CHECK();
+        widen_kernel<<<grid_for(m, kHemThreads), kHemThreads, 0, s>>>(tcur.p, tdeg.p, m);
+        SPMM_LAUNCH_CHECK();
+        SPMM_TRY(scan_counts(tdeg.p, tptr.p, m, s, nullptr));
+        SPMM_CUDA_TRY(cudaMemsetAsync(tcur.p, 0, (size_t)m * 4, s));
+        transpose_kernel<<<warps_grid(n), kHemThreads, 0, s>>>(pptr.p, pidx.p, n, tptr.p, tcur.p, trow.p);
+        SPMM_LAUNCH_CHECK();
+    }
+    // incidences per chunk of rows; row chunks from the host copy of the prefix
+    std::vector<int64_t> hstart((size_t)n + 1);
+    SPMM_TRY(to_host(hstart.data(), pstart.p, n + 1, s));
+    // heaviest possible w: the longest pruned row
+    int64_t wmax_len = 0;
+    {
+        std::vector<int64_t> hp((size_t)n + 1);
+        SPMM_TRY(to_host(hp.data(), pptr.p, n + 1, s));
+        for (int64_t r = 0; r < n; ++r) wmax_len = std::max(wmax_len, hp[r + 1] - hp[r]);
+    }
+    const int wb = bit_width_u64((uint64_t)wmax_len + 1);
+    // directed top-k edges of all chunks, both directions
+    const int64_t kcap = topk >= 0 ? topk : n;
+    std::vector<std::pair<int64_t, int64_t>> chunks;
+    for (int64_t r0 = 0; r0 < n;) {
+        int64_t r1 = r0 + 1;
+        while (r1 < n && hstart[r1 + 1] - hstart[r0] <= kPairBudget) ++r1;
+        chunks.push_back({r0, r1});
+        r0 = r1;
+    }
+    int64_t ecap = 0;
+    for (auto &c : chunks) {
+        const int64_t rows = c.second - c.first;
+        const int64_t pairs = hstart[c.second] - hstart[c.first];
+        ecap += 2 * std::min(pairs, rows * kcap);
+    }
+    DBuf<uint64_t> ek0, ek1;
+    DBuf<uint32_t> ew0;
+    SPMM_TRY(ek0.alloc(ecap, s));
+    SPMM_TRY(ew0.alloc(ecap, s));
+    int64_t ecount = 0;
+    for (auto &c : chunks) {
+        const int64_t r0 = c.first, r1 = c.second, rows = r1 - r0;
+        const int64_t P = hstart[r1] - hstart[r0];
+        if (P == 0) continue;
+        const int rb = bit_width_u64((uint64_t)rows);
+        if (rb + jb > 63 || rb + wb + jb > 64) return SPMM_EUNSUPPORTED;
+        const uint64_t sentinel = (rb + jb == 64) ? ~0ull : ((1ull << (rb + jb)) - 1ull);
+        DBuf<uint64_t> k0, k1;
+        SPMM_TRY(k0.alloc(P, s));
+        SPMM_TRY(k1.alloc(P, s));
+        gen_pairs_kernel<<<warps_grid(rows), kHemThreads, 0, s>>>(pptr.p, pidx.p, tptr.p, trow.p, pstart.p, r0, r1,
+                                                                  jb, sentinel, k0.p);
+        SPMM_LAUNCH_CHECK();
+        SPMM_TRY(sort_keys(k0, k1, P, rb + jb, s));
+        // unique pairs with their counts, keyed for the top-k order
+        DBuf<int64_t> flag, pos;
+        SPMM_TRY(flag.alloc(P + 1, s));
+        SPMM_TRY(pos.alloc(P + 1, s));
+        head_flags_kernel<<<grid_for(P, kHemThreads), kHemThreads, 0, s>>>(k0.p, P, sentinel, flag.p);
+        SPMM_LAUNCH_CHECK();
+        int64_t U = 0;
+        SPMM_TRY(scan_counts(flag.p, pos.p, P, s, &U));
+        if (U == 0) continue;
+        DBuf<uint64_t> u0, u1;
+        SPMM_TRY(u0.alloc(U, s));
+        SPMM_TRY(u1.alloc(U, s));
+        rle_kernel<<<grid_for(P, kHemThreads), kHemThreads, 0, s>>>(k0.p, P, sentinel, pos.p, jb, wb, u0.p);
+        SPMM_LAUNCH_CHECK();
+        k0.release();
+        k1.release();
+        SPMM_TRY(sort_keys(u0, u1, U, rb + wb + jb, s));
+        topk_flags_kernel<<<grid_for(U, kHemThreads), kHemThreads, 0, s>>>(u0.p, U, jb, wb, topk, flag.p);
+        SPMM_LAUNCH_CHECK();
+        int64_t kept = 0;
+        SPMM_TRY(scan_counts(flag.p, pos.p, U, s, &kept));
+        if (ecount + 2 * kept > ecap) return SPMM_EUNSUPPORTED;
+        topk_emit_kernel<<<grid_for(U, kHemThreads), kHemThreads, 0, s>>>(u0.p, U, flag.p, pos.p, r0, jb, wb,
+                                                                          ecount, ek0.p, ew0.p);
+        SPMM_LAUNCH_CHECK();
+        ecount += 2 * kept;
+    }
+    if (ecount == 0) return SPMM_OK;
+    // symmetric graph: sort (row, col) keys with their weights, drop repeats
+    DBuf<uint32_t> ew1;
+    DBuf<uint32_t> tmp;
+    SPMM_TRY(ek1.alloc(ecount, s));
+    SPMM_TRY(ew1.alloc(ecount, s));
+    SPMM_TRY(tmp.alloc(radix_temp_elems(ecount), s));
+    bool first = true;
+    SPMM_TRY(radix_sort_pairs<uint64_t, uint32_t>(ek0.p, ew0.p, ek1.p, ew1.p, ecount, 2 * jb, tmp.p, &first, s));
+    const uint64_t *ek = first ? ek0.p : ek1.p;
+    const uint32_t *ew = first ? ew0.p : ew1.p;
+    DBuf<int64_t> flag, pos;
+    SPMM_TRY(flag.alloc(ecount + 1, s));
+    SPMM_TRY(pos.alloc(ecount + 1, s));
+    DBuf<unsigned long long> rowcnt;
+    SPMM_TRY(rowcnt.alloc(n + 1, s));
+    SPMM_CUDA_TRY(cudaMemsetAsync(rowcnt.p, 0, (size_t)(n + 1) * 8, s));
+    edge_heads_kernel<<<grid_for(ecount, kHemThreads), kHemThreads, 0, s>>>(ek, ecount, flag.p, jb, rowcnt.p);
+    SPMM_LAUNCH_CHECK();
+    int64_t G = 0;
+    SPMM_TRY(scan_counts(flag.p, pos.p, ecount, s, &G));
+    SPMM_TRY(gptr.alloc(n + 1, s));
+    SPMM_TRY(gcol.alloc(G, s));
+    SPMM_TRY(gw.alloc(G, s));
+    {
+        DBuf<unsigned long long> tmp2;
+        SPMM_TRY(tmp2.alloc(scan_temp_elems(n + 1), s));
+        SPMM_TRY(exclusive_scan<unsigned long long>(rowcnt.p, gptr.p, n + 1, tmp2.p, nullptr, s));
+    }
+    edge_emit_kernel<<<grid_for(ecount, kHemThreads), kHemThreads, 0, s>>>(ek, ew, ecount, flag.p, pos.p, jb,
+                                                                           gcol.p, gw.p);
+    SPMM_LAUNCH_CHECK();
+    *gnnz = G;
+    return SPMM_OK;
+}
+
+}  // namespace
+}  // namespace spmm
+
+using namespace spmm;
+
+extern "C" int spmm_hem_labels(int64_t rows, int64_t cols, const int64_t *indptr, const int32_t *indices,
+                               int64_t target, int64_t max_size, int64_t max_nnz, int64_t hub_degree, int64_t topk,
+                               int32_t residual_rounds, int32_t feasible_first, int64_t *labels,
+                               spmm_stream_t stream) {
+    if (rows < 0 || cols < 0 || !labels || (rows > 0 && !indptr) || hub_degree < 0 || residual_rounds < 0)
+        return SPMM_EINVAL;
+    if (rows > 0x7fffffffLL || cols > 0x7fffffffLL) return SPMM_EUNSUPPORTED;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (rows == 0) return SPMM_OK;
+    iota64_kernel<<<grid_for(rows, kHemThreads), kHemThreads, 0, s>>>(labels, rows);
+    SPMM_LAUNCH_CHECK();
+    if (rows <= 1 || target <= 1) return SPMM_OK;
+    int64_t nnz0 = 0;
+    SPMM_TRY(to_host(&nnz0, indptr + rows, 1, s));
+    const Caps caps{max_size, max_nnz};
+    // level state: pattern (ptr, idx) of n rows, sizes and nnz of its rows
+    int64_t n = rows, nnz = nnz0;
+    DBuf<int64_t> lptr, size, rnnz;
+    DBuf<int32_t> lidx;
+    SPMM_TRY(lptr.alloc(n + 1, s));
+    SPMM_TRY(lidx.alloc(nnz, s));
+    SPMM_CUDA_TRY(cudaMemcpyAsync(lptr.p, indptr, (size_t)(n + 1) * 8, cudaMemcpyDeviceToDevice, s));
+    if (nnz) SPMM_CUDA_TRY(cudaMemcpyAsync(lidx.p, indices, (size_t)nnz * 4, cudaMemcpyDeviceToDevice, s));
+    SPMM_TRY(size.alloc(n, s));
+    SPMM_TRY(rnnz.alloc(n, s));
+    fill_kernel<<<grid_for(n, kHemThreads), kHemThreads, 0, s>>>(size.p, n, 1);
+    SPMM_LAUNCH_CHECK();
+    diff_kernel<<<grid_for(n, kHemThreads), kHemThreads, 0, s>>>(lptr.p, n, rnnz.p);
+    SPMM_LAUNCH_CHECK();
+    int lg = 0;
+    while ((1ll << lg) < target) ++lg;
+    const int max_levels = 8 * (lg > 1 ? lg : 1) + 16;
+    DBuf<unsigned long long> matched;
+    SPMM_TRY(matched.alloc(1, s));
+    for (int level = 0; level < max_levels && n > 1; ++level) {
+        DBuf<unsigned long long> gptr;
+        DBuf<int32_t> gcol;
+        DBuf<uint32_t> gw;
+        int64_t gnnz = 0;
+        SPMM_TRY(similarity_graph(lptr.p, lidx.p, n, cols, nnz, (uint32_t)std::min<int64_t>(hub_degree, 0xFFFFFFFFll),
+                                  topk, gptr, gcol, gw, &gnnz, s));
+        if (gnnz == 0) break;
+        DBuf<uint8_t> active;
+        DBuf<int64_t> best, mate;
+        SPMM_TRY(active.alloc(n, s));
+        SPMM_TRY(best.alloc(n, s));
+        SPMM_TRY(mate.alloc(n, s));
+        SPMM_CUDA_TRY(cudaMemsetAsync(active.p, 1, (size_t)n, s));
+        fill_kernel<<<grid_for(n, kHemThreads), kHemThreads, 0, s>>>(mate.p, n, -1);
+        SPMM_LAUNCH_CHECK();
+        unsigned long long total = 0;
+        for (int round = 0; round < residual_rounds; ++round) {
+            SPMM_CUDA_TRY(cudaMemsetAsync(matched.p, 0, 8, s));
+            best_kernel<<<warps_grid(n), kHemThreads, 0, s>>>(gptr.p, gcol.p, gw.p, n, active.p, size.p, rnnz.p,
+                                                               caps, feasible_first, best.p);
+            SPMM_LAUNCH_CHECK();
+            mutual_kernel<<<grid_for(n, kHemThreads), kHemThreads, 0, s>>>(best.p, n, size.p, rnnz.p, caps, mate.p,
+                                                                          active.p, matched.p);
+            SPMM_LAUNCH_CHECK();
+            unsigned long long got = 0;
+            SPMM_TRY(to_host(&got, matched.p, 1, s));
+            if (got == 0) break;
+            total += got;
+        }
+        if (total == 0) break;
+        // contraction
+        DBuf<int64_t> flag, rank, new_id, nlen, nptr;
+        SPMM_TRY(flag.alloc(n + 1, s));
+        SPMM_TRY(rank.alloc(n + 1, s));
+        root_flags_kernel<<<grid_for(n, kHemThreads), kHemThreads, 0, s>>>(mate.p, n, flag.p);
+        SPMM_LAUNCH_CHECK();
+        int64_t n_new = 0;
+        SPMM_TRY(scan_counts(flag.p, rank.p, n, s, &n_new));
+        DBuf<unsigned long long> nsize, nnnz;
+        SPMM_TRY(new_id.alloc(n, s));
+        SPMM_TRY(nlen.alloc(n_new + 1, s));
+        SPMM_TRY(nptr.alloc(n_new + 1, s));
+        SPMM_TRY(nsize.alloc(n_new, s));
+        SPMM_TRY(nnnz.alloc(n_new, s));
+        SPMM_CUDA_TRY(cudaMemsetAsync(nsize.p, 0, (size_t)n_new * 8, s));
+        SPMM_CUDA_TRY(cudaMemsetAsync(nnnz.p, 0, (size_t)n_new * 8, s));
+        contract_kernel<<<grid_for(n, kHemThreads), kHemThreads, 0, s>>>(mate.p, n, rank.p, size.p, rnnz.p, lptr.p,
+                                                                        lidx.p, new_id.p, nsize.p, nnnz.p, nlen.p);
+        SPMM_LAUNCH_CHECK();
+        int64_t nnz_new = 0;
+        SPMM_TRY(scan_counts(nlen.p, nptr.p, n_new, s, &nnz_new));
+        DBuf<int32_t> nidx;
+        SPMM_TRY(nidx.alloc(nnz_new, s));
+        contract_emit_kernel<<<grid_for(n, kHemThreads), kHemThreads, 0, s>>>(mate.p, n, rank.p, lptr.p, lidx.p,
+                                                                             nptr.p, nidx.p);
+        SPMM_LAUNCH_CHECK();
+        relabel_kernel<<<grid_for(rows, kHemThreads), kHemThreads, 0, s>>>(labels, rows, new_id.p);
+        SPMM_LAUNCH_CHECK();
+        SPMM_TRY(size.alloc(n_new, s));
+        SPMM_TRY(rnnz.alloc(n_new, s));
+        copy_cast_kernel<int64_t><<<grid_for(n_new, kHemThreads), kHemThreads, 0, s>>>(nsize.p, size.p, n_new);
+        SPMM_LAUNCH_CHECK();
+        copy_cast_kernel<int64_t><<<grid_for(n_new, kHemThreads), kHemThreads, 0, s>>>(nnnz.p, rnnz.p, n_new);
+        SPMM_LAUNCH_CHECK();
+        std::swap(lptr.p, nptr.p);
+        std::swap(lidx.p, nidx.p);
+        n = n_new;
+        nnz = nnz_new;
+    }
+    SPMM_CUDA_TRY(cudaStreamSynchronize(s));
+    return SPMM_OK;
+}
