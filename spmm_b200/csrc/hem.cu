@@ -367,6 +367,143 @@ __global__ void diff_kernel(const int64_t *__restrict__ ptr, int64_t n, int64_t 
         out[i] = ptr[i + 1] - ptr[i];
 }
 
+// ---- per-row counting by hashing (top-k >= 0) ----
+//
+// A CTA per row: the row's incidences are counted in an open-addressing
+// table (shared memory, or a global region for rows whose table would not
+// fit), then the row's topk entries by (w desc, j asc) are found by a radix
+// select on the key (wmax - w) << jb | j (unique per row) and emitted as both
+// directions of the directed edge.  No sort of the incidences is needed.
+constexpr int kHashThreads = 256;
+constexpr int kSmemSlots = 8192;    // small rows: 64 KB of (key, count) slots, 3 CTAs per SM
+constexpr int kMidSlots = 16384;    // mid rows: 128 KB, one CTA of 512 threads per SM
+
+__device__ __forceinline__ uint32_t slot_of(uint32_t j, int lg) {
+    return lg ? (j * 0x9E3779B1u) >> (32 - lg) : 0u;
+}
+
+// SLOTS: the shared-memory table of this launch's rows (tables of up to SLOTS
+// and more than SLOTS / 2 slots, the smallest class from 64); 0: rows whose
+// table exceeds kMidSlots, in global memory.
+template <int THREADS, int SLOTS>
+__global__ void __launch_bounds__(THREADS) hash_topk_kernel(
+    const int64_t *__restrict__ ptr, const int32_t *__restrict__ idx, const int64_t *__restrict__ tptr,
+    const int32_t *__restrict__ trow, const int64_t *__restrict__ pinc, const int64_t *__restrict__ goff,
+    int32_t *__restrict__ gkey, uint32_t *__restrict__ gcnt, int64_t n, int jb, int64_t topk,
+    unsigned long long *__restrict__ ecount, uint64_t *__restrict__ ekey, uint32_t *__restrict__ ew) {
+    extern __shared__ uint32_t hsm[];
+    int32_t *skey = reinterpret_cast<int32_t *>(hsm);
+    uint32_t *scnt = hsm + (SLOTS > 0 ? SLOTS : 1);
+    __shared__ uint32_t hist[256];
+    __shared__ unsigned long long red_u, red_w;
+    __shared__ unsigned long long sel_prefix;
+    __shared__ long long sel_k;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int64_t i = blockIdx.x; i < n; i += gridDim.x) {
+        const int64_t inc = pinc[i];
+        if (inc <= 1) continue;   // only itself (or nothing): no candidates
+        int lg = 6;
+        while ((1ll << lg) < 2 * inc) ++lg;
+        const int64_t S = 1ll << lg;
+        const int64_t lo_cap = SLOTS == kSmemSlots ? 0 : SLOTS == 0 ? kMidSlots : kSmemSlots;
+        const int64_t hi_cap = SLOTS == 0 ? INT64_MAX : SLOTS;
+        if (S <= lo_cap || S > hi_cap) continue;   // another launch's rows
+        int32_t *key = skey;
+        uint32_t *cnt = scnt;
+        if (SLOTS == 0) {
+            key = gkey + goff[i];
+            cnt = gcnt + goff[i];
+        }
+        __syncthreads();   // the previous row is done with the table
+        for (int64_t t = tid; t < S; t += THREADS) {
+            key[t] = -1;
+            cnt[t] = 0;
+        }
+        if (tid == 0) {
+            red_u = 0;
+            red_w = 0;
+        }
+        __syncthreads();
+        // insert: warps take the row's columns, lanes the column's rows
+        for (int64_t k = ptr[i] + warp; k < ptr[i + 1]; k += THREADS / 32) {
+            const int32_t c = idx[k];
+            for (int64_t t = tptr[c] + lane; t < tptr[c + 1]; t += 32) {
+                const int32_t j = trow[t];
+                if (j == i) continue;
+                uint32_t h = slot_of((uint32_t)j, lg);
+                for (;;) {
+                    const int32_t prev = atomicCAS(key + h, -1, j);
+                    if (prev == -1 || prev == j) {
+                        atomicAdd(cnt + h, 1u);
+                        break;
+                    }
+                    h = (h + 1) & (uint32_t)(S - 1);
+                }
+            }
+        }
+        __syncthreads();
+        // occupied slots and the heaviest weight
+        unsigned long long u = 0, wm = 0;
+        for (int64_t t = tid; t < S; t += THREADS)
+            if (key[t] >= 0) {
+                ++u;
+                wm = cnt[t] > wm ? cnt[t] : wm;
+            }
+        atomicAdd(&red_u, u);
+        atomicMax(&red_w, wm);
+        __syncthreads();
+        const unsigned long long U = red_u, W = red_w;
+        if (U == 0) continue;
+        const int bits = jb + (64 - __clzll((long long)W));   // key (W - w) << jb | j
+        // threshold: the topk-th smallest key (all kept when U <= topk)
+        unsigned long long kth = ~0ull;
+        if ((long long)U > topk) {
+            if (tid == 0) {
+                sel_prefix = 0;
+                sel_k = topk;
+            }
+            unsigned long long mask = 0;
+            for (int shift = ((bits + 7) / 8 - 1) * 8; shift >= 0; shift -= 8) {
+                for (int b = tid; b < 256; b += THREADS) hist[b] = 0;
+                __syncthreads();
+                const unsigned long long prefix = sel_prefix;
+                for (int64_t t = tid; t < S; t += THREADS) {
+                    if (key[t] < 0) continue;
+                    const unsigned long long K = ((W - cnt[t]) << jb) | (unsigned long long)key[t];
+                    if ((K & mask) == prefix) atomicAdd(&hist[(K >> shift) & 255], 1u);
+                }
+                __syncthreads();
+                if (tid == 0) {
+                    long long k = sel_k, cum = 0;
+                    int v = 0;
+                    for (; v < 255; ++v) {
+                        if (cum + hist[v] >= k) break;
+                        cum += hist[v];
+                    }
+                    sel_k = k - cum;
+                    sel_prefix = prefix | ((unsigned long long)v << shift);
+                }
+                mask |= 255ull << shift;
+                __syncthreads();
+            }
+            kth = sel_prefix;
+        }
+        // emit the kept entries, both directions
+        for (int64_t t = tid; t < S; t += THREADS) {
+            const int32_t j = key[t];
+            if (j < 0) continue;
+            const uint32_t w = cnt[t];
+            const unsigned long long K = ((W - w) << jb) | (unsigned long long)j;
+            if (K > kth) continue;
+            const unsigned long long o = atomicAdd(ecount, 2ull);
+            ekey[o] = ((uint64_t)i << jb) | (uint64_t)j;
+            ekey[o + 1] = ((uint64_t)j << jb) | (uint64_t)i;
+            ew[o] = w;
+            ew[o + 1] = w;
+        }
+    }
+}
+
 // exclusive scan of n int64 counts into out[0..n], out[n] = total (copied to the host when asked)
 int scan_counts(const int64_t *in, int64_t *out, int64_t n, cudaStream_t s, int64_t *total_host) {
     DBuf<int64_t> tmp;
@@ -440,6 +577,66 @@ int similarity_graph(const int64_t *ptr, const int32_t *idx, int64_t n, int64_t 
     // incidences per chunk of rows; row chunks from the host copy of the prefix
     std::vector<int64_t> hstart((size_t)n + 1);
     SPMM_TRY(to_host(hstart.data(), pstart.p, n + 1, s));
+    DBuf<uint64_t> ek0, ek1;
+    DBuf<uint32_t> ew0;
+    int64_t ecount = 0;
+    if (topk >= 0) {
+        // hashing path: global tables for the rows whose table exceeds shared memory
+        std::vector<int64_t> hoff((size_t)n + 1, 0);
+        int64_t gslots = 0;
+        for (int64_t r = 0; r < n; ++r) {
+            const int64_t inc = hstart[r + 1] - hstart[r];
+            hoff[r] = gslots;
+            if (inc > 1) {
+                int64_t S = 64;
+                while (S < 2 * inc) S <<= 1;
+                if (S > kMidSlots) gslots += S;
+            }
+        }
+        DBuf<int64_t> goff;
+        DBuf<int32_t> gkey;
+        DBuf<uint32_t> gcnt;
+        SPMM_TRY(goff.alloc(n + 1, s));
+        SPMM_CUDA_TRY(cudaMemcpyAsync(goff.p, hoff.data(), (size_t)(n + 1) * 8, cudaMemcpyHostToDevice, s));
+        SPMM_TRY(gkey.alloc(gslots, s));
+        SPMM_TRY(gcnt.alloc(gslots, s));
+        const int64_t ecap = 2 * n * (topk > 0 ? topk : 1);
+        SPMM_TRY(ek0.alloc(ecap, s));
+        SPMM_TRY(ew0.alloc(ecap, s));
+        DBuf<unsigned long long> ecnt;
+        SPMM_TRY(ecnt.alloc(1, s));
+        SPMM_CUDA_TRY(cudaMemsetAsync(ecnt.p, 0, 8, s));
+        if (topk > 0) {
+            const size_t smem = (size_t)kSmemSlots * 8;
+            auto small = hash_topk_kernel<kHashThreads, kSmemSlots>;
+            auto mid = hash_topk_kernel<512, kMidSlots>;
+            SPMM_CUDA_TRY(cudaFuncSetAttribute(small, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            SPMM_CUDA_TRY(cudaFuncSetAttribute(mid, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)((size_t)kMidSlots * 8)));
+            int dev = 0, sms = 0;
+            SPMM_CUDA_TRY(cudaGetDevice(&dev));
+            SPMM_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+            const int64_t grid = std::min<int64_t>(n, (int64_t)sms * 3);
+            small<<<(unsigned)grid, kHashThreads, smem, s>>>(pptr.p, pidx.p, tptr.p, trow.p, pinc.p, goff.p, gkey.p,
+                                                             gcnt.p, n, jb, topk, ecnt.p, ek0.p, ew0.p);
+            SPMM_LAUNCH_CHECK();
+            mid<<<(unsigned)std::min<int64_t>(n, sms), 512, (size_t)kMidSlots * 8, s>>>(
+                pptr.p, pidx.p, tptr.p, trow.p, pinc.p, goff.p, gkey.p, gcnt.p, n, jb, topk, ecnt.p, ek0.p, ew0.p);
+            SPMM_LAUNCH_CHECK();
+            if (gslots > 0) {   // rows with global tables: 1,024 threads each
+                hash_topk_kernel<1024, 0><<<(unsigned)std::min<int64_t>(n, sms * 2), 1024, 0, s>>>(
+                    pptr.p, pidx.p, tptr.p, trow.p, pinc.p, goff.p, gkey.p, gcnt.p, n, jb, topk, ecnt.p, ek0.p,
+                    ew0.p);
+                SPMM_LAUNCH_CHECK();
+            }
+        }
+        unsigned long long ec = 0;
+        SPMM_TRY(to_host(&ec, ecnt.p, 1, s));
+        ecount = (int64_t)ec;
+        pidx.release();
+        trow.release();
+    }
+    if (topk < 0) {
     // heaviest possible w: the longest pruned row
     int64_t wmax_len = 0;
     {
@@ -463,11 +660,8 @@ int similarity_graph(const int64_t *ptr, const int32_t *idx, int64_t n, int64_t 
         const int64_t pairs = hstart[c.second] - hstart[c.first];
         ecap += 2 * std::min(pairs, rows * kcap);
     }
-    DBuf<uint64_t> ek0, ek1;
-    DBuf<uint32_t> ew0;
     SPMM_TRY(ek0.alloc(ecap, s));
     SPMM_TRY(ew0.alloc(ecap, s));
-    int64_t ecount = 0;
     for (auto &c : chunks) {
         const int64_t r0 = c.first, r1 = c.second, rows = r1 - r0;
         const int64_t P = hstart[r1] - hstart[r0];
@@ -508,6 +702,7 @@ int similarity_graph(const int64_t *ptr, const int32_t *idx, int64_t n, int64_t 
                                                                           ecount, ek0.p, ew0.p);
         SPMM_LAUNCH_CHECK();
         ecount += 2 * kept;
+    }
     }
     if (ecount == 0) return SPMM_OK;
     // symmetric graph: sort (row, col) keys with their weights, drop repeats
