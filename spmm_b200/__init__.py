@@ -13,11 +13,13 @@ from .boo import (BOOInfo, BOOMatrixInt32Double, BOOMatrixInt32Float, BOOMatrixI
                   csr_to_boo)
 from .boo_plan import BOOExecutionPlan, prepare_boo_cuda
 from .clustering import CLUSTER_METHODS, cluster_axes, cluster_axis
+from .io import load_boo, load_pbr, save_boo, save_pbr
 from .pbr import (BlockFillStats, BlockStripeStats, DataOrder, PBRInfo, PBRMatrixInt32Double,
                   PBRMatrixInt32Float, PBRMatrixInt64Double, PBRMatrixInt64Float, csr_to_pbr,
                   pbr_analyze_csr, pbr_batched_matmul_chunkcols_cuda, pbr_batched_matmul_cpu,
                   pbr_batched_matmul_cuda, pbr_batched_matmul_nnzflat_cuda,
                   pbr_batched_matmul_variant_cuda, pbr_info, pbr_matmul, pbr_to_csr)
+from .timed import BOOTimedSpMM, DirectSpMM, PBRTimedSpMM
 
 __all__ = [
     'csr_to_boo', 'boo_to_csr', 'boo_info', 'boo_matmul', 'boo_arena_bytes', 'BOOInfo',
@@ -26,4 +28,5 @@ __all__ = [
     'BlockStripeStats', 'pbr_matmul', 'pbr_batched_matmul_cpu', 'pbr_batched_matmul_cuda',
     'pbr_batched_matmul_chunkcols_cuda', 'pbr_batched_matmul_nnzflat_cuda',
     'pbr_batched_matmul_variant_cuda', 'BOOExecutionPlan', 'prepare_boo_cuda',
+    'BOOTimedSpMM', 'PBRTimedSpMM', 'DirectSpMM', 'save_boo', 'load_boo', 'save_pbr', 'load_pbr',
 ]
