@@ -60,6 +60,8 @@ def parse():
     ap.add_argument('--no-cusparse', action='store_true', help='skip the cuSPARSE reference timing')
     ap.add_argument('--engine', choices=('auto', 'cuda_cores', 'tensor_cores'), default='auto',
                     help="units that multiply the BOO blocks (spmm_launch_cfg.engine)")
+    ap.add_argument('--grouping', choices=('identity', 'hem'), default='identity',
+                    help="BOO row / column grouping (cluster='hem' runs the GPU HEM labels; build time only)")
     ap.add_argument('--slab-features', type=int, default=0,
                     help='features per pass of the remainder kernels (spmm_launch_cfg.slab_features; '
                          '0 = auto, <0 = full width)')
@@ -395,7 +397,7 @@ def native_arm(args):
     elif fmt == 'boo':
         A = None
         if rank == 0:
-            A = S.csr_to_boo(mat, cluster='identity', target_nr=cfg['target'], target_nc=cfg['target'])
+            A = S.csr_to_boo(mat, cluster=args.grouping, target_nr=cfg['target'], target_nc=cfg['target'])
             A.to(dev)
         if world > 1:
             A = D.broadcast_boo(A, dev)                  # built once, replicated over NCCL
@@ -556,7 +558,7 @@ def native_arm(args):
         'data': 'synthetic (seeded generator of the config)',
         'config': {'workload': args.config + (f' {args.gen_kw}' if args.gen_kw else ''),
                    'format': fmt,
-                   'grouping': 'identity' if fmt == 'boo' else '8x8 bitset blocks',
+                   'grouping': args.grouping if fmt == 'boo' else '8x8 bitset blocks',
                    'target': cfg['target'] if fmt == 'boo' else None,
                    'rows': int(mat_full.shape[0] if split == 'rows' else mat.shape[0]),
                    'nnz': int(mat_full.nnz if split == 'rows' else mat.nnz),

@@ -85,8 +85,13 @@ __global__ void label_max_kernel(const int32_t *__restrict__ labels, int64_t n,
         if (l < 0 || (int64_t)l >= n) bad = true;
         else if ((unsigned long long)l + 1 > m) m = (unsigned long long)l + 1;
     }
-    if (bad) atomicOr(err, 1u);
-    if (m) atomicMax(maxp, m);
+    // one atomic per warp (labels < 2^31, so the maximum fits 32 bits)
+    const unsigned wm = __reduce_max_sync(kFullMask, (unsigned)m);
+    const bool wbad = __any_sync(kFullMask, bad);
+    if ((threadIdx.x & 31) == 0) {
+        if (wbad) atomicOr(err, 1u);
+        if (wm) atomicMax(maxp, (unsigned long long)wm);
+    }
 }
 
 // ---- groups ---------------------------------------------------------------
