@@ -33,6 +33,7 @@ import json
 import os
 import statistics
 import subprocess
+import tempfile
 import sys
 import time
 
@@ -96,7 +97,7 @@ class ClockSampler:
     def __init__(self, gpu_id: str):
         self.proc = None
         self.gpu_id = gpu_id
-        self.path = os.path.join(ROOT, 'gpurun_out', f'clocks_{os.getpid()}.csv')
+        self.path = os.path.join(tempfile.gettempdir(), f'spmm_b200_clocks_{os.getpid()}.csv')
 
     def start(self):
         try:

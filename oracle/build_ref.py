@@ -28,7 +28,9 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REF_OUT = os.path.join(HERE, '_ref')
-DEFAULT_REFERENCE = os.environ.get('SPMM_REFERENCE_ROOT', '/root/reference')
+# the reference checkout next to this repository, unless SPMM_REFERENCE_ROOT names one
+DEFAULT_REFERENCE = os.environ.get('SPMM_REFERENCE_ROOT',
+                                   os.path.abspath(os.path.join(HERE, '..', '..', 'reference')))
 MODULE = 'torch_fast_spdmm_core'
 
 
