@@ -133,7 +133,7 @@ __device__ __forceinline__ void accumulate(Frag<S, VEC> (&acc)[VPT], const int32
 }
 
 template <typename S, int VEC, int VPT, int LPR>
-__global__ void __launch_bounds__(kBooThreads)
+__global__ void __launch_bounds__(kBooThreads, VPT == 1 ? 4 : 1)
 boo_spmm_kernel(const BooParams<S> p) {
     constexpr int NG = kBooThreads / LPR;        // lane groups per CTA
     constexpr int RPG = kRowsChunk / NG;          // rows per lane group per chunk
