@@ -133,7 +133,9 @@ class BOOTimedSpMM(_Timed):
                      max_nr=max_nr, max_nc=max_nc, max_nnz_blk=max_nnz_blk)
         for k, v in sizes.items():
             setattr(st, k, int(v))
-        st.nz_order = 0
+        # row_seg=True promises row-major blocks (as the reference requires);
+        # otherwise the order-agnostic column-major treatment is used
+        st.nz_order = 0 if row_seg else 1
         st.scalar_type = _lib.F32
         for name, t in arrays.items():
             setattr(st, name, ptr(t))
