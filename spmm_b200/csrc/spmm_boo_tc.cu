@@ -721,17 +721,23 @@ __global__ void __launch_bounds__(256) boo_gather_kernel(const TcParams p) {
     }
     __syncthreads();
     float4 *out = const_cast<float4 *>(p.Xt) + (bt * p.n_cg + g) * QW * p.K;
+    // item = (quad q, 4 features from f): four 16-byte loads (one per column
+    // of the quad), a 4 x 4 transpose in registers, four 16-byte stores
+    const int64_t f4 = p.K / 4;
+    for (int64_t it = threadIdx.x; it < QW * f4; it += blockDim.x) {
+        const int q = (int)(it / f4);
+        const int64_t f = (it % f4) * 4;
+        float4 v[4];
 #pragma unroll
-    for (int q = threadIdx.x >> 7; q < QW; q += 2) {
-        const float *r0 = xr[4 * q], *r1 = xr[4 * q + 1], *r2 = xr[4 * q + 2], *r3 = xr[4 * q + 3];
-        for (int64_t f = threadIdx.x & 127; f < p.K; f += 128) {
-            float4 v;
-            v.x = r0 ? __ldg(r0 + f) : 0.f;
-            v.y = r1 ? __ldg(r1 + f) : 0.f;
-            v.z = r2 ? __ldg(r2 + f) : 0.f;
-            v.w = r3 ? __ldg(r3 + f) : 0.f;
-            out[q * p.K + f] = v;
+        for (int c = 0; c < 4; ++c) {
+            const float *r = xr[4 * q + c];
+            v[c] = r ? __ldg(reinterpret_cast<const float4 *>(r + f)) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
+        float4 *o = out + q * p.K + f;
+        o[0] = make_float4(v[0].x, v[1].x, v[2].x, v[3].x);
+        o[1] = make_float4(v[0].y, v[1].y, v[2].y, v[3].y);
+        o[2] = make_float4(v[0].z, v[1].z, v[2].z, v[3].z);
+        o[3] = make_float4(v[0].w, v[1].w, v[2].w, v[3].w);
     }
 }
 
