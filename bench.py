@@ -527,12 +527,22 @@ def native_arm(args):
 
     # e2e: the public API with host operands (pinned H2D of X, D2H of Y per step)
     x_host = x.cpu().pin_memory()
-    for _ in range(2):
-        (S.boo_matmul(A, x_host, engine=args.engine, slab_features=args.slab_features) if fmt == 'boo' else S.pbr_matmul(A, x_host))
+
+    def e2e_step():
+        return (S.boo_matmul(A, x_host, engine=args.engine, slab_features=args.slab_features) if fmt == 'boo'
+                else S.pbr_matmul(A, x_host))
+
+    # warm-up in the timed loop's own pattern (the previous result stays alive
+    # while the next is made), so both pinned result buffers of the steady
+    # state exist before timing: a first page-locking of 400 MB inside the
+    # timed steps would be charged to the product
+    yh = None
+    for _ in range(3):
+        yh = e2e_step()
     torch.cuda.synchronize(dev)
     e0 = time.perf_counter()
     for _ in range(args.e2e_steps):
-        yh = S.boo_matmul(A, x_host, engine=args.engine, slab_features=args.slab_features) if fmt == 'boo' else S.pbr_matmul(A, x_host)
+        yh = e2e_step()
     torch.cuda.synchronize(dev)
     e_s = (time.perf_counter() - e0) / args.e2e_steps
     if world > 1:

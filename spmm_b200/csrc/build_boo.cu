@@ -182,10 +182,19 @@ __global__ void block_select_kernel(const uint64_t *__restrict__ keys,
             if (count > mn) mn = count;
         }
     }
-    if (over) atomicOr(&cnt->err_u16, 1u);
-    if (mr) atomicMax(&cnt->max_nr, mr);
-    if (mc) atomicMax(&cnt->max_nc, mc);
-    if (mn) atomicMax(&cnt->max_nnz_blk, mn);
+    // one atomic per warp and counter (every value fits 32 bits): per-thread
+    // atomics on these three words serialised the kernel at one candidate per
+    // L2 atomic slot
+    const unsigned wr = __reduce_max_sync(kFullMask, (unsigned)mr);
+    const unsigned wc = __reduce_max_sync(kFullMask, (unsigned)mc);
+    const unsigned wn = __reduce_max_sync(kFullMask, (unsigned)mn);
+    const bool wover = __any_sync(kFullMask, over);
+    if ((threadIdx.x & 31) == 0) {
+        if (wover) atomicOr(&cnt->err_u16, 1u);
+        if (wr) atomicMax(&cnt->max_nr, (unsigned long long)wr);
+        if (wc) atomicMax(&cnt->max_nc, (unsigned long long)wc);
+        if (wn) atomicMax(&cnt->max_nnz_blk, (unsigned long long)wn);
+    }
 }
 
 // ---- emit -------------------------------------------------------------------
