@@ -67,6 +67,7 @@ constexpr int kFeat = 128;           // features per task: MMA M, tensor-memory 
 // nonzeros before two MMAs per 8 used columns beat per-nonzero FMAs.
 constexpr int kDenseNnz = 48;
 constexpr int kSegs = 32;            // blocks or rows listed per pass
+constexpr int kWin = 3;              // windows of 32 candidate segments loaded at once
 constexpr int kListCap = 512;        // staged (row, column, value) entries per pass
 constexpr int kNzPre = 4;            // nonzeros per thread fetched ahead
 constexpr long long kWaitCycles = 1ll << 32;  // ~2 s at 2 GHz
@@ -103,6 +104,8 @@ struct alignas(1024) WorkerSmem {
     int32_t sbase[kSegs];           //   first entry,
     int32_t scb[kSegs];             //   block: col_ids base of its group; row segment: -1
     uint32_t saux[kSegs];           //   block: index shift; row segment: local row
+    int32_t scnt[kSegs];            //   entry count (while the table is filled)
+    int32_t snext;                  // first segment not yet listed
     int32_t dk0[kSegs], dk1[kSegs], dcg[kSegs];  // the row group's tensor-core blocks
     uint32_t dshift[kSegs];
     uint64_t mma_bar;               // completes once per MMA commit
@@ -246,42 +249,104 @@ __device__ __forceinline__ bool drain_phase(uint64_t *bar, uint32_t parity) {
 // (seg_table), their entries staged as (local row, column, value) by the
 // warpgroup (stage), and each thread sums them for its feature (sum_range).
 
-// Segment table for segments [s0, s0 + kSegs) of the row group (warp 0).
+// Segment table (warp 0): the next kSegs NON-EMPTY segments from segment
+// `pos` on, in segment order, and in w.snext the segment to resume from.
+// Candidates are loaded kWin x 32 at a time in two rounds of independent
+// loads (more windows spill registers at four workers per SM), so rows
+// without remainder entries and tensor-core blocks cost no pass of their own
+// and a row group's segment list costs one load chain, not one per 32
+// (64-row groups with a remainder: three passes became one).
 template <int NR, int PW>
 __device__ __forceinline__ void seg_table(const TcParams &p, WorkerSmem<NR, PW> &w, int64_t bs, int nblk, int nseg,
-                                          int32_t rbase, int s0, int wt) {
+                                          int32_t rbase, int pos, int wt) {
     if (wt >= 32) return;
-    const int sidx = s0 + wt;
-    int cnt = 0, base = 0, cb = -1;
-    uint32_t aux = 0;
-    if (sidx < nblk) {
-        const int64_t b = bs + sidx;
-        const int32_t k0 = __ldg(p.blk_nz_ptr + b), k1 = __ldg(p.blk_nz_ptr + b + 1);
-        if (k1 - k0 < p.dense_nnz) {
-            cnt = k1 - k0;
-            base = k0;
-            cb = __ldg(p.col_grp_ptr + __ldg(p.blk_col_grp + b));
-            aux = __ldg(p.blk_shift + b);
+    const unsigned lt = lanemask_lt();
+    int filled = 0;
+    while (filled < kSegs && pos < nseg) {
+        // candidate s = pos + 32 u + lane: block s (s < nblk; empty when it goes
+        // through the tensor cores) or the CSR remainder of local row s - nblk.
+        // Two rounds of independent loads for all windows.
+        int32_t t0[kWin], t1[kWin], t2[kWin];
+#pragma unroll
+        for (int u = 0; u < kWin; ++u) {
+            const int sc = pos + 32 * u + wt;
+            t0[u] = t1[u] = t2[u] = 0;
+            if (sc < nblk) {
+                const int64_t b = bs + sc;
+                t0[u] = __ldg(p.blk_nz_ptr + b);
+                t1[u] = __ldg(p.blk_nz_ptr + b + 1);
+                t2[u] = __ldg(p.blk_col_grp + b);
+            } else if (sc < nseg) {
+                t2[u] = __ldg(p.row_ids + rbase + (sc - nblk));
+            }
         }
-    } else if (sidx < nseg) {
-        const int r = sidx - nblk;
-        const int32_t row = __ldg(p.row_ids + rbase + r);
-        base = __ldg(p.rem_indptr + row);
-        cnt = __ldg(p.rem_indptr + row + 1) - base;
-        aux = (uint32_t)r;
+        int cnt[kWin], base[kWin], cb[kWin];
+        uint32_t aux[kWin];
+#pragma unroll
+        for (int u = 0; u < kWin; ++u) {
+            const int sc = pos + 32 * u + wt;
+            cnt[u] = 0;
+            base[u] = 0;
+            cb[u] = -1;
+            aux[u] = 0;
+            if (sc < nblk) {
+                if (t1[u] - t0[u] < p.dense_nnz) {
+                    cnt[u] = t1[u] - t0[u];
+                    base[u] = t0[u];
+                    cb[u] = __ldg(p.col_grp_ptr + t2[u]);
+                    aux[u] = __ldg(p.blk_shift + bs + sc);
+                }
+            } else if (sc < nseg) {
+                base[u] = __ldg(p.rem_indptr + t2[u]);
+                cnt[u] = __ldg(p.rem_indptr + t2[u] + 1) - base[u];
+                aux[u] = (uint32_t)(sc - nblk);
+            }
+        }
+        int next = pos;   // first candidate not consumed
+#pragma unroll
+        for (int u = 0; u < kWin; ++u) {
+            if (filled < kSegs) {
+                const unsigned ne = __ballot_sync(kFullMask, cnt[u] > 0);
+                const int room = kSegs - filled;
+                const int rank = __popc(ne & lt);
+                if (cnt[u] > 0 && rank < room) {
+                    const int slot = filled + rank;
+                    w.scnt[slot] = cnt[u];
+                    w.sbase[slot] = base[u];
+                    w.scb[slot] = cb[u];
+                    w.saux[slot] = aux[u];
+                }
+                if (__popc(ne) > room) {   // full: resume at the first candidate not taken
+                    const unsigned first_left = __ballot_sync(kFullMask, cnt[u] > 0 && rank == room);
+                    next = pos + 32 * u + (__ffs(first_left) - 1);
+                    filled = kSegs;
+                } else {                   // the whole window of 32 is consumed
+                    filled += __popc(ne);
+                    next = pos + 32 * (u + 1);
+                }
+            }
+        }
+        pos = next;
     }
-    int incl = cnt;
+    __syncwarp();
+    int incl = wt < filled ? w.scnt[wt] : 0;
+    if (wt >= filled) {   // unused slots: empty segments
+        w.sbase[wt] = 0;
+        w.scb[wt] = -1;
+        w.saux[wt] = 0;
+    }
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
         const int n = __shfl_up_sync(kFullMask, incl, o);
         if (wt >= o) incl += n;
     }
     w.soff[wt + 1] = incl;
-    if (wt == 0) w.soff[0] = 0;
-    w.sbase[wt] = base;
-    w.scb[wt] = cb;
-    w.saux[wt] = aux;
+    if (wt == 0) {
+        w.soff[0] = 0;
+        w.snext = pos < nseg ? pos : nseg;
+    }
 }
+
 
 // Entries [g0, g0 + ne) of the current segment table into the list.
 template <int NR, int PW>
@@ -361,10 +426,11 @@ __device__ __forceinline__ void cuda_part(const TcParams &p, WorkerSmem<NR, PW> 
                                           int32_t rbase, int32_t nr, const float *xb, int wt, uint32_t bar) {
     const int nblk = (int)(be - bs);
     const int nseg = nblk + (p.rem_nnz ? (nr < NR ? nr : NR) : 0);
-    for (int s0 = 0; s0 < nseg; s0 += kSegs) {
-        seg_table<NR, PW>(p, w, bs, nblk, nseg, rbase, s0, wt);
+    for (int pos = 0; pos < nseg;) {
+        seg_table<NR, PW>(p, w, bs, nblk, nseg, rbase, pos, wt);
         named_bar_sync(bar, 128);
         const int total = w.soff[kSegs];
+        pos = w.snext;
         for (int g0 = 0; g0 < total; g0 += kListCap) {
             const int ne = total - g0 < kListCap ? total - g0 : kListCap;
             stage<NR, PW>(p, w, g0, ne, wt);
