@@ -20,9 +20,10 @@ Multi-GPU (torchrun, one process per GPU), two partitionings:
 The time is the max over ranks of the device-measured duration.
 
 ``--impl reference`` times the reference's own CPU implementation
-(boo_batched_matmul_cpu of the reference core built into oracle/_ref, else the
-C restatement in oracle/) on this host's cores, rows split across worker
-processes, on the same workload.
+(boo_batched_matmul_cpu / pbr_batched_matmul_cpu of the reference core built
+into oracle/_ref, else the C restatement in oracle/) on this host's cores,
+rows split across worker processes, on the same workload and format as the
+native arm (--config, --gen-kw, --format).
 """
 
 from __future__ import annotations
@@ -215,28 +216,36 @@ def cpu_baseline(mat, cfg, x_np, fmt='boo', budget_s=12.0):
 _W = {}
 
 
-def _worker_init(shm_name, shape, dtype, indptr, indices, data, cols, target):
+def _worker_init(shm_name, shape, dtype, indptr, indices, data, cols, target, fmt):
     from multiprocessing import shared_memory
     shm = shared_memory.SharedMemory(name=shm_name)
     _W['shm'] = shm
     _W['x'] = np.ndarray(shape, dtype=dtype, buffer=shm.buf)
+    _W['fmt'] = fmt
     import scipy.sparse as sp
     sub = sp.csr_matrix((data, indices, indptr), shape=(len(indptr) - 1, cols))
     core = _reference_core()
-    _W['obj'], _W['kind'] = _build_ref_boo(core, sub, cols, target)
+    _W['obj'], _W['kind'] = (_build_ref_boo(core, sub, cols, target) if fmt == 'boo'
+                             else _build_ref_pbr(core, sub, cols))
     if _W['kind'] == 'reference':
         import torch
         torch.set_num_threads(1)
         _W['xt'] = torch.from_numpy(_W['x'])
 
 
+def _worker_ready():
+    return True
+
+
 def _worker_step(_):
     t0 = time.perf_counter()
+    boo = _W['fmt'] == 'boo'
     if _W['kind'] == 'reference':
-        _reference_core().boo_batched_matmul_cpu(_W['obj'], _W['xt'])
+        core = _reference_core()
+        (core.boo_batched_matmul_cpu if boo else core.pbr_batched_matmul_cpu)(_W['obj'], _W['xt'])
     else:
         from oracle import oracle as O
-        O.boo_matmul(_W['obj'], _W['x'])
+        (O.boo_matmul if boo else O.pbr_matmul)(_W['obj'], _W['x'])
     return time.perf_counter() - t0
 
 
@@ -246,7 +255,8 @@ def reference_arm(args):
     rank = int(os.environ.get('RANK', '0'))
     if rank != 0:
         return 0
-    mat, cfg = make_matrix(args.config)
+    mat, cfg = make_matrix(args.config, args.gen_kw)   # the native arm's matrix
+    fmt = args.format or cfg['fmt']                   # and format
     K = cfg['K']
     from spmm_b200 import workloads as W
     x = W.dense_x(mat.shape[1], K, seed=0).numpy()
@@ -259,13 +269,14 @@ def reference_arm(args):
     est_rate = 2.0e9                    # flop/s per core of the serial reference loop
     rows = min(mat.shape[0], int(mat.shape[0] * min(1.0, 0.5 * P * est_rate /
                                                     (2.0 * mat.nnz * K))))
-    rows = max(rows - rows % cfg['target'], cfg['target'])
+    unit = cfg['target'] if fmt == 'boo' else 8       # whole row groups / PBR stripes
+    rows = min(mat.shape[0], max(rows - rows % unit, unit))
     sub = mat[:rows]
     shm = shared_memory.SharedMemory(create=True, size=x.nbytes)
     try:
         xs = np.ndarray(x.shape, dtype=x.dtype, buffer=shm.buf)
         xs[:] = x
-        bounds = np.linspace(0, rows // cfg['target'], P + 1).astype(int) * cfg['target']
+        bounds = np.minimum(np.linspace(0, -(-rows // unit), P + 1).astype(int) * unit, rows)
         ctx = mp.get_context('spawn')
         pools = []
         for i in range(P):
@@ -274,8 +285,11 @@ def reference_arm(args):
                 continue
             pools.append(ctx.Pool(1, initializer=_worker_init,
                                   initargs=(shm.name, x.shape, x.dtype, part.indptr, part.indices,
-                                            part.data, mat.shape[1], cfg['target'])))
+                                            part.data, mat.shape[1], cfg['target'], fmt)))
         kind = 'reference' if _reference_core() is not None else 'port'
+        # every worker has finished its initializer (process start, format
+        # build) before the first step, warm-up or not
+        [r.get() for r in [p.apply_async(_worker_ready) for p in pools]]
 
         def step():
             t0 = time.perf_counter()
@@ -300,7 +314,7 @@ def reference_arm(args):
             'n_gpus': args.gpus, 'steps': args.steps, 'warmup': args.warmup,
             'ms_per_step': round(1e3 * t, 3), 'higher_is_better': True, 'scaling': 'weak',
             'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic (seeded generator)',
-            'config': {'workload': args.config, 'format': 'boo', 'rows': int(mat.shape[0]),
+            'config': {'workload': args.config, 'format': fmt, 'rows': int(mat.shape[0]),
                        'nnz': int(mat.nnz), 'K': K},
             'cpu_baseline': {'value': round(value, 4), 'unit': 'GFLOP/s', 'cores': len(pools),
                              'kind': kind, 'sample': sample},
