@@ -454,7 +454,38 @@ def native_arm(args):
         if rc:
             raise _lib.SpmmError(rc, 'bench')
 
+    abytes, xbytes, ybytes = (format_bytes_boo if fmt == 'boo' else format_bytes_pbr)(A, K)
+    alg = abytes + xbytes + ybytes
+    # a workload that fits in L2 (C1) is timed step by step with L2 flushed
+    # (a write of twice its size, untimed) before every step; larger ones are
+    # timed as one run of steps
+    l2 = int(getattr(torch.cuda.get_device_properties(dev), 'L2_cache_size', 0) or (126 << 20))
+    flush_buf = torch.empty(2 * l2, dtype=torch.uint8, device=dev) if alg < 2 * l2 else None
+
+    def timed_steps(n, fn_step):
+        """ms of n steps of fn_step on `stream`, measured with CUDA events."""
+        if flush_buf is None:
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for _ in range(n):
+                fn_step()
+            b.record(stream)
+            torch.cuda.synchronize(dev)
+            return a.elapsed_time(b)
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(n)]
+        for a, b in evs:
+            flush_buf.zero_()
+            a.record(stream)
+            fn_step()
+            b.record(stream)
+        torch.cuda.synchronize(dev)
+        return sum(a.elapsed_time(b) for a, b in evs)
+
     for _ in range(max(args.warmup, 3)):
+        if flush_buf is not None:
+            flush_buf.zero_()
         launch()
     torch.cuda.synchronize(dev)
 
@@ -471,16 +502,9 @@ def native_arm(args):
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
-    ev0 = torch.cuda.Event(enable_timing=True)
-    ev1 = torch.cuda.Event(enable_timing=True)
     n_launch0 = L.spmm_product_launches()
-    ev0.record(stream)
-    for _ in range(args.steps):
-        launch()
-    ev1.record(stream)
+    ms = timed_steps(args.steps, launch)
     gpu_launches = int(L.spmm_product_launches() - n_launch0)   # counted by the library
-    torch.cuda.synchronize(dev)
-    ms = ev0.elapsed_time(ev1)
     if world > 1:
         t = torch.tensor([ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -497,8 +521,6 @@ def native_arm(args):
     else:
         value = world * flops_rank / (ms_step * 1e-3) / 1e9
 
-    abytes, xbytes, ybytes = (format_bytes_boo if fmt == 'boo' else format_bytes_pbr)(A, K)
-    alg = abytes + xbytes + ybytes
     peak, peak_kind = load_peaks()
     achieved = alg / (ms_step * 1e-3) / 1e9
     rem_major = fmt == 'boo' and 0 < 2 * A._sizes['rem_nnz'] and 2 * A._sizes['rem_nnz'] >= A._sizes['total_nnz']
@@ -523,15 +545,9 @@ def native_arm(args):
             for _ in range(3):
                 yc = torch.sparse.mm(At, x)
             torch.cuda.synchronize(dev)
-            c0 = torch.cuda.Event(enable_timing=True)
-            c1 = torch.cuda.Event(enable_timing=True)
             nrep = max(5, min(args.steps, 50))
-            c0.record(stream)
-            for _ in range(nrep):
-                yc = torch.sparse.mm(At, x)
-            c1.record(stream)
-            torch.cuda.synchronize(dev)
-            cms = c0.elapsed_time(c1) / nrep
+            cms = timed_steps(nrep, lambda: torch.sparse.mm(At, x)) / nrep   # same L2 rule
+            yc = None
             cusparse = {'ms_per_step': round(cms, 4), 'value': round(flops_rank / (cms * 1e-3) / 1e9, 3),
                         'unit': 'GFLOP/s', 'what': 'torch.sparse.mm (cusparseSpMM) on the same CSR, X',
                         'speedup_of_this': round(cms / ms_step, 3)}
@@ -592,7 +608,10 @@ def native_arm(args):
                    'parallelism': (f'row-split x{world} (nnz-balanced row groups, X broadcast once)'
                                    if split == 'rows' else f'feature-split x{world}'),
                    'x_broadcast_ms': None if x_bcast_ms is None else round(x_bcast_ms, 3),
-                   'l2': 'inputs larger than L2 (A+X+Y = %.2f GB), no flush' % (alg / 1e9),
+                   'l2': ('inputs larger than L2 (A+X+Y = %.2f GB), no flush' % (alg / 1e9)
+                          if flush_buf is None else
+                          'L2 flushed before every step (%d MB write, untimed; per-step CUDA events), '
+                          'A+X+Y = %.3f GB' % ((2 * l2) >> 20, alg / 1e9)),
                    'build_s': round(build_s, 3)},
         'roofline': {'bound': 'hbm', 'achieved': round(achieved, 1), 'peak': peak,
                      'unit': 'GB/s', 'frac': round(achieved / peak, 4), 'traffic': traffic,
