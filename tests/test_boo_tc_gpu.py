@@ -201,3 +201,41 @@ def test_tc_abi_workspace_optional(cuda):
     assert torch.equal(out[0], out[1])
     cc = _lib.launch_cfg('cuda_cores')
     assert L.spmm_boo_matmul_workspace_size(C.byref(st), 1, 256, C.byref(cc)) == 0
+
+
+@pytest.mark.parametrize('g,n_sparse,rem_rows', [
+    (32, 31, 'none'), (32, 32, 'none'), (32, 33, 'none'), (32, 20, 'all'), (32, 40, 'even'),
+    (64, 1, 'all'), (64, 97, 'even'), (64, 130, 'all'),
+])
+def test_tc_cuda_core_segment_lists(cuda, g, n_sparse, rem_rows):
+    """Row groups whose CUDA-core part spans many segments -- sparse blocks and
+    rows with remainder entries, empty rows in between -- so the segment list
+    fills in the middle of a window of candidates and resumes there, and
+    lists several times per row group."""
+    rng = np.random.default_rng(g * 1000 + n_sparse)
+    n_groups = 3
+    rows, ncg = g * n_groups, 1 + n_sparse + g
+    cols = g * ncg
+    r, c = [], []
+    for grp in range(n_groups):
+        r0 = grp * g
+        r += list(r0 + rng.integers(0, g, 3 * g))                 # one tensor-core block (col group 0)
+        c += list(rng.integers(0, g, 3 * g))
+        for s in range(1, 1 + n_sparse):                          # kept blocks of 6-12 nonzeros
+            k = int(rng.integers(6, 13))
+            r += list(r0 + rng.integers(0, g, k))
+            c += list(s * g + rng.integers(0, g, k))
+        for q in range(g):                                        # one entry in a block of its own:
+            if rem_rows == 'all' or (rem_rows == 'even' and q % 2 == 0):   # spilled to the remainder
+                r.append(r0 + q)
+                c.append((1 + n_sparse + q) * g + int(rng.integers(0, g)))
+    vals = rng.standard_normal(len(r)).astype(np.float32)
+    mat = sp.csr_matrix((vals, (np.array(r), np.array(c))), shape=(rows, cols), dtype=np.float32)
+    mat.sum_duplicates()
+    mat.sort_indices()
+    boo = S.csr_to_boo(mat, row_labels=np.arange(rows) // g, col_labels=np.arange(cols) // g)
+    assert boo.num_blocks() == n_groups * (1 + n_sparse)
+    assert boo.remainder_nnz() == n_groups * {'none': 0, 'all': g, 'even': g // 2}[rem_rows]
+    x = torch.from_numpy(rng.standard_normal((cols, 128)).astype(np.float32))
+    _check(mat, boo, x, 'tensor_cores')
+    _check(mat, boo, x, 'cuda_cores')
