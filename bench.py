@@ -4,7 +4,10 @@ Default workload (N=1 line): BASELINE config 2 -- 3-D FEM hex mesh, 64^3 nodes x
 3 DOF (786,432 rows, 61,731,000 nonzeros), BOO with identity grouping at
 target 32x32, X [786432, 128] fp32 ~ N(0,1); synthetic, seeded.  One step = one
 Y = A*X over the whole matrix with A, X and Y resident in HBM (1.18 GB, far
-larger than the 126 MB L2, so no flush is needed between steps).
+larger than the 126 MB L2, so no flush is needed between steps).  A workload
+smaller than twice the L2 (C1) is timed step by step instead, with the L2
+flushed (an untimed write of twice its size) before every step; the
+cuSPARSE reference point follows the same rule.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
                   [--config c2_fem3d] [--format boo|pbr]
