@@ -194,10 +194,12 @@ def cpu_baseline(mat, cfg, x_np, fmt='boo', budget_s=12.0):
     frac = 16
     rows = max(1, mat.shape[0] // frac)
     sub = _sample(mat, rows)
+    tb = time.perf_counter()
     if fmt == 'boo':
         obj, kind = _build_ref_boo(core, sub, mat.shape[1], cfg['target'])
     else:
         obj, kind = _build_ref_pbr(core, sub, mat.shape[1])
+    build_s = time.perf_counter() - tb
     times = []
     t_end = time.perf_counter() + budget_s
     _ref_matmul(obj, kind, x_np, fmt)           # warm-up
@@ -209,7 +211,25 @@ def cpu_baseline(mat, cfg, x_np, fmt='boo', budget_s=12.0):
     return {'value': round(2.0 * sub.nnz * K / t / 1e9, 4), 'unit': 'GFLOP/s', 'cores': 1,
             'kind': kind,
             'sample': f'rows [0, {rows}) of the workload ({sub.nnz} nnz), K={K}, '
-                      f'median of {len(times)} calls, 1 thread'}
+                      f'median of {len(times)} calls, 1 thread',
+            'build_s': build_s, 'build_nnz': int(sub.nnz)}
+
+
+def build_line(gpu_build_s, nnz, cpu):
+    """Format build throughput: the GPU build of the whole matrix from a host
+    CSR (host labels, copy to the device, GPU builder) against the reference's
+    CPU builder on the CPU-baseline sample, in nonzeros per second."""
+    line = {'gpu_s': round(gpu_build_s, 4),
+            'gpu_nnz_per_s': round(nnz / gpu_build_s) if gpu_build_s > 0 else None,
+            'what': 'csr_to_boo / csr_to_pbr from a host CSR (whole matrix) vs the reference CPU '
+                    'builder (1 thread, CPU-baseline sample)'}
+    if cpu and cpu.get('build_s'):
+        line['cpu_reference_s'] = round(cpu['build_s'], 4)
+        line['cpu_sample_nnz'] = cpu['build_nnz']
+        line['cpu_nnz_per_s'] = round(cpu['build_nnz'] / cpu['build_s'])
+        if line['gpu_nnz_per_s']:
+            line['gpu_over_cpu'] = round(line['gpu_nnz_per_s'] / line['cpu_nnz_per_s'], 2)
+    return line
 
 
 # ---------------------------------------------------------------------------
@@ -590,6 +610,9 @@ def native_arm(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(mat, cfg, x.cpu().numpy(), fmt)
+    build = build_line(build_s, int(mat.nnz), cpu) if world == 1 else None
+    if cpu is not None:
+        cpu = {k: v for k, v in cpu.items() if not k.startswith('build')}
 
     if world > 1:
         dist.destroy_process_group()
@@ -622,7 +645,7 @@ def native_arm(args):
                      'kernel': kernel_name},
         'cusparse': cusparse,
         'e2e': e2e, 'gpu_launches': gpu_launches,
-        'clocks': clocks, 'cpu_baseline': cpu,
+        'clocks': clocks, 'cpu_baseline': cpu, 'build': build,
     }
     print(json.dumps(line), flush=True)
     return 0

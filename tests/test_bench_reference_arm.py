@@ -43,3 +43,19 @@ def test_reference_arm_other_ranks_exit_quietly():
                         '--config', 'c1_laplacian2d', '--gen-kw', '{"n": 16}', '--steps', '1'],
                        capture_output=True, text=True, timeout=300, cwd=ROOT, env=env)
     assert r.returncode == 0 and not [ln for ln in r.stdout.splitlines() if ln.startswith('{')]
+
+
+@pytest.mark.parametrize('fmt', ['boo', 'pbr'])
+def test_cpu_baseline_and_build_line(fmt):
+    import bench
+    from spmm_b200 import workloads as W
+    mat = W.laplacian2d(n=64)
+    x = W.dense_x(mat.shape[1], 32, seed=0).numpy()
+    cpu = bench.cpu_baseline(mat, W.CONFIGS['c1_laplacian2d'], x, fmt, budget_s=0.5)
+    assert cpu['value'] > 0 and cpu['cores'] == 1 and cpu['kind'] in ('reference', 'port')
+    assert cpu['build_nnz'] == mat[:mat.shape[0] // 16].nnz and cpu['build_s'] > 0
+    line = bench.build_line(0.25, mat.nnz, cpu)
+    assert line['gpu_nnz_per_s'] == round(mat.nnz / 0.25)
+    assert line['cpu_nnz_per_s'] == round(cpu['build_nnz'] / cpu['build_s'])
+    assert line['gpu_over_cpu'] == round(line['gpu_nnz_per_s'] / line['cpu_nnz_per_s'], 2)
+    assert 'cpu_reference_s' not in bench.build_line(0.25, mat.nnz, None)
