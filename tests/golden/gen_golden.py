@@ -150,6 +150,23 @@ def main():
                        p + 'data': a.data.astype(np.float32), p + 'row_labels': r_l, p + 'col_labels': c_l})
             manifest['clustering'].append(dict(case=k, n=n, **kw))
             k += 1
+    # HEM on structured graphs (grids, meshes, skewed and uniform degrees,
+    # dense blocks): many equal similarity weights, so the tie-break order is
+    # what decides the labels.  Inputs from this package's seeded generators.
+    from spmm_b200 import workloads as W
+    structured = (('laplacian2d', W.laplacian2d(12)), ('fem3d', W.fem3d(3)),
+                  ('powerlaw', W.powerlaw(400)), ('uniform', W.uniform(300, k=6)),
+                  ('blockdiag', W.blockdiag(8, 16)))
+    for gname, a in structured:
+        for tgt, ff in ((8, True), (16, False)):
+            kw = dict(method='hem', target_nr=tgt, target_nc=tgt, max_nr=tgt, max_nc=tgt,
+                      max_block_nnz=None, seed=0, feasible_first=ff)
+            r_l, c_l = clus.cluster_axes(a, **kw)
+            p = f'c{k}/'
+            cl.update({p + 'indptr': a.indptr.astype(np.int32), p + 'indices': a.indices.astype(np.int32),
+                       p + 'data': a.data.astype(np.float32), p + 'row_labels': r_l, p + 'col_labels': c_l})
+            manifest['clustering'].append(dict(case=k, n=int(a.shape[0]), graph=gname, **kw))
+            k += 1
 
     np.savez_compressed(os.path.join(HERE, 'boo_golden.npz'), **boo)
     np.savez_compressed(os.path.join(HERE, 'pbr_golden.npz'), **pbr)
