@@ -8,14 +8,30 @@
  *
  * Conventions
  *   - Ownership: the caller owns every buffer (inputs, outputs, workspace).
- *     The library allocates no device memory and keeps no state between calls.
+ *     Device memory the library allocates itself, all of it named here:
+ *       * spmm_hem_labels / spmm_hem_hierarchy take their per-level scratch
+ *         from the stream-ordered allocator (cudaMallocAsync / cudaFreeAsync)
+ *         and release it before returning;
+ *       * spmm_boo_build_noalloc uses a fixed 32 MiB array compiled into the
+ *         library (one per device that loads it, held until exit);
+ *     the builders, products and conversions allocate nothing: their scratch
+ *     is the caller's workspace (*_workspace_size()), and a product given too
+ *     little returns SPMM_EWORKSPACE.
  *   - Errors: every entry point returns an int status (SPMM_OK == 0).  No C++
  *     exception crosses the ABI.  spmm_status_string() gives the text.
+ *     Device-side outcomes of an asynchronous product (a bounded wait that
+ *     expired: SPMM_ETIMEOUT) land in the call's status word
+ *     (spmm_launch_cfg::status); a call given none reports into one
+ *     process-wide word shared by all such calls, read by spmm_tc_status().
  *   - Streams: work is enqueued on `stream` (cudaStream_t; NULL = legacy
  *     default stream) in order with the caller's other work on that stream.
- *     Only the *_analyze builder phases block the host (they must return sizes).
- *   - Threading: no globals; concurrent calls on different streams with
- *     different buffers are safe.
+ *     The *_analyze builder phases, spmm_boo_build_noalloc, spmm_pbr_to_csr
+ *     and the HEM labellers block the host (they return sizes or check data).
+ *   - Threading: re-entrant; concurrent calls on different streams with
+ *     different buffers (workspaces and status words included) are safe.
+ *     Process-wide state: the fallback status word above, the noalloc
+ *     scratch (overlapping noalloc calls race on it) and the product-launch
+ *     counter (spmm_product_launches(), a measurement aid).
  *   - Devices: work runs on the CUDA device current on the calling thread; all
  *     pointers must belong to that device.
  *   - Dense operands: X is [batch][cols][K] and Y is [batch][rows][K], both
@@ -43,7 +59,9 @@ enum spmm_status {
     SPMM_EWORKSPACE = 6,      /* workspace smaller than *_workspace_size() asked for */
     SPMM_EUNSUPPORTED = 7,    /* size or type outside what this build handles */
     SPMM_EALIGN = 8,          /* a pointer lacks the alignment its dtype requires */
-    SPMM_ESCRATCH = 9         /* problem larger than spmm_boo_build_noalloc's fixed scratch */
+    SPMM_ESCRATCH = 9,        /* problem larger than spmm_boo_build_noalloc's fixed scratch */
+    SPMM_ETIMEOUT = 10,       /* a bounded device wait expired (in a status word; Y incomplete) */
+    SPMM_ENCCL = 11           /* a collective failed (the multi-GPU helpers above this ABI) */
 };
 
 enum spmm_index_type { SPMM_INDEX_I32 = 0, SPMM_INDEX_I64 = 1 };
@@ -117,20 +135,23 @@ typedef struct {
     void *rem_vals;                /* rem_nnz */
 } spmm_pbr_dev;
 
-/* Optional per-call tuning; NULL selects the defaults.  No process-wide state:
- * the reference's global setters (torch_fast_spdmm/kernels/boo_kernel.cu:
- * 58-99) have no counterpart here. */
+/* Optional per-call settings; NULL selects the defaults.  No process-wide
+ * tuning state: the reference's global setters (torch_fast_spdmm/kernels/
+ * boo_kernel.cu:58-99) have no counterpart here. */
 typedef struct {
-    int32_t version;        /* must be 1 */
-    int32_t slab_features;  /* remainder-major BOO products: features per pass over A
-                             * (0 = full width with X rows staged by asynchronous
-                             * copies, the default; < 0 = full width through registers;
-                             * > 0 = the widest supported slab not above it,
-                             * 8 / 16 / 32 floats, 4 / 8 / 16 doubles) */
+    int32_t version;        /* 1, or 2 (adds `status`) */
+    int32_t slab_features;  /* remainder-major BOO products: 0 = the nnz-flat remainder with
+                             * X rows staged by asynchronous copies (default); < 0 = rows
+                             * through registers (no workspace); > 0 is taken as 0 */
     int32_t engine;         /* enum spmm_engine (BOO product only; PBR ignores it) */
-    int32_t reserved;
-    void *workspace;        /* optional device scratch of the BOO product (tensor-core */
-    uint64_t workspace_bytes; /* or nnz-flat remainder): spmm_boo_matmul_workspace_size() bytes */
+    int32_t wait_us;        /* bounded device waits of the tensor-core product: 0 = about
+                             * 2 s (default); > 0 = give up after about this many
+                             * microseconds (tests of the timeout path) */
+    void *workspace;        /* device scratch of the BOO product, 16-byte aligned: at least */
+    uint64_t workspace_bytes; /* spmm_boo_matmul_workspace_size() bytes when that is > 0 */
+    int32_t *status;        /* version 2, optional: a device int32 the call sets to 0
+                             * (stream-ordered) and a kernel sets to SPMM_ETIMEOUT when one
+                             * of its bounded waits expired; read it after the stream */
 } spmm_launch_cfg;
 
 /* Which units multiply the BOO blocks.  AUTO takes the tensor cores when the
@@ -183,8 +204,8 @@ int spmm_boo_build_emit(const spmm_csr_dev *A, const int32_t *row_labels,
  *     rem_indptr rows+1, row_ids rows, col_grp_ptr cols+1, col_ids cols,
  *     blk_nz_ptr nnz+1, every other array nnz entries.  On return the size
  *     fields of *out hold the real sizes.
- *   - The first call on a device (with it current) looks up the array's device
- *     address; make that first call before any stream capture.
+ *   - Each call looks up the array's device address on the current device
+ *     (cudaGetSymbolAddress; no allocation).
  *   - Blocks the host until the sizes are known, like the analyze phase.
  *   - All calls share the array: calls whose GPU work overlaps race and must
  *     be serialised by the caller. */
@@ -209,23 +230,28 @@ int spmm_pbr_build_emit(const spmm_csr_dev *A, int64_t block_rows, int64_t block
 
 /* Y = A*X for a BOO matrix (replaces boo_spmm_cuda_impl / boo_run_into,
  * torch_fast_spdmm/bindings/bindings_boo.cu:34-313, bound as
- * boo_spmm_cuda_{f32,f64} at bindings_boo.cu:408-476).  One launch: blocks,
- * CSR remainder and COO tail of each row group are summed by the CTA that owns
- * the group and every Y element is written once (no memset, no atomics). */
+ * boo_spmm_cuda_{f32,f64} at bindings_boo.cu:408-476).  Blocks, CSR
+ * remainder and COO tail of a row group are summed by the CTA (or tensor-core
+ * worker) that owns the group and every Y element is written once, with no
+ * memset and no atomics: one launch on CUDA cores, two on the tensor cores
+ * (X gathered by column group, then the product), four for remainder-major
+ * matrices (the nnz-flat remainder's plan, chunks and fix-up, then blocks and
+ * tail added by the block kernel). */
 int spmm_boo_matmul(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch, int64_t K,
                     const spmm_launch_cfg *cfg, spmm_stream_t stream);
 
-/* Bytes of device scratch the BOO product takes through cfg->workspace (the X
- * panels gathered by column group for the tensor cores); 0 when the
- * CUDA-core product runs.  Without a workspace the product allocates the same
- * amount stream-ordered (cudaMallocAsync) for the call. */
+/* Bytes of device scratch the BOO product needs in cfg->workspace for these
+ * operands and settings: the X panels gathered by column group (tensor-core
+ * product) or the chunk table and partial rows of the nnz-flat remainder
+ * (remainder-major matrices); 0 when none is needed.  spmm_boo_matmul
+ * returns SPMM_EWORKSPACE when it is needed and missing. */
 size_t spmm_boo_matmul_workspace_size(const spmm_boo_dev *A, int64_t batch, int64_t K,
                                       const spmm_launch_cfg *cfg);
 
-/* Status word of the tensor-core kernels (no reference counterpart): 0, or the
- * code of the first bounded wait that expired on the device (the launch then
- * stopped early and Y is incomplete).  Synchronises the device; `clear`
- * resets the word.  Returns -1 when the CUDA runtime fails. */
+/* The process-wide status word of products called without one
+ * (spmm_launch_cfg::status == NULL; no reference counterpart): 0, or
+ * SPMM_ETIMEOUT once a bounded wait of such a call expired.  Synchronises the
+ * device; `clear` resets the word.  Returns -1 when the CUDA runtime fails. */
 int spmm_tc_status(int clear);
 
 /* Product kernels (BOO and PBR SpMM, the tensor-core gather pass included)
@@ -271,6 +297,18 @@ int spmm_pbr_to_csr(const spmm_pbr_dev *A, void *indptr, void *indices, void *va
 int spmm_hem_labels(int64_t rows, int64_t cols, const int64_t *indptr, const int32_t *indices, int64_t target,
                     int64_t max_size, int64_t max_nnz, int64_t hub_degree, int64_t topk, int32_t residual_rounds,
                     int32_t feasible_first, int64_t *labels, spmm_stream_t stream);
+
+/* The same labels, plus the matching hierarchy (replaces the `hierarchy`
+ * record of the reference's _hem_labels, clustering.py:271-282, behind
+ * cluster_axis(..., hem_hierarchy=[])): levels (device, level_slots x rows
+ * int64, level_slots >= spmm_hem_level_slots(target)) receives the identity
+ * labels, then the labels after each level that matched, finest to coarsest;
+ * *n_levels (host) the number of arrays written.  levels may be NULL. */
+int64_t spmm_hem_level_slots(int64_t target);
+int spmm_hem_hierarchy(int64_t rows, int64_t cols, const int64_t *indptr, const int32_t *indices, int64_t target,
+                       int64_t max_size, int64_t max_nnz, int64_t hub_degree, int64_t topk, int32_t residual_rounds,
+                       int32_t feasible_first, int64_t *labels, int64_t *levels, int64_t level_slots,
+                       int64_t *n_levels, spmm_stream_t stream);
 
 #ifdef __cplusplus
 }

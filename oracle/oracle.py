@@ -19,7 +19,8 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, 'liboracle.so')
-SOURCES = [os.path.join(HERE, n) for n in ('spmm_oracle.c', 'spmm_oracle.h', 'spmm_oracle_body.h')]
+SOURCES = [os.path.join(HERE, n) for n in ('spmm_oracle.c', 'spmm_oracle.h', 'spmm_oracle_body.h',
+                                            'hem_oracle.c')]
 
 POLICY_CODE = {'keep': 0, 'merge': 1, 'remainder': 2, 'tail_batch': 3}
 ORDER_CODE = {'rowmajor': 0, 'colmajor': 1}
@@ -48,7 +49,7 @@ def build_lib(force: bool = False) -> str:
     if force or stale:
         tmp = LIB_PATH + f'.{os.getpid()}.tmp'
         subprocess.check_call(['gcc', '-O2', '-std=c11', '-fPIC', '-shared', '-o', tmp,
-                               os.path.join(HERE, 'spmm_oracle.c')])
+                               os.path.join(HERE, 'spmm_oracle.c'), os.path.join(HERE, 'hem_oracle.c')])
         os.replace(tmp, LIB_PATH)
     return LIB_PATH
 
@@ -79,6 +80,10 @@ def lib():
             getattr(_LIB, f'oracle_csr_to_boo_{sfx}').restype = C.c_int
             getattr(_LIB, f'oracle_csr_to_pbr_{sfx}').restype = C.c_int
             getattr(_LIB, f'oracle_pbr_to_csr_{sfx}').restype = C.c_int
+        _LIB.oracle_hem_labels.restype = C.c_int
+        _LIB.oracle_hem_level_slots.restype = C.c_int64
+        _LIB.oracle_hem_level_slots.argtypes = [C.c_int64]
+        _LIB.oracle_enforce_caps.restype = C.c_int
     return _LIB
 
 
@@ -321,3 +326,63 @@ def pbr_canonical(p: dict) -> dict:
         lens = np.diff(offsets)[order]
         out['block_offsets'] = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
     return out
+
+
+# ----------------------------------------------------------------------------
+# clustering (hem_oracle.c)
+# ----------------------------------------------------------------------------
+
+def binary_pattern(mat):
+    """Canonical binary CSR pattern of `mat` (rows sorted, duplicates merged)."""
+    import scipy.sparse as sp
+    a = sp.csr_matrix(mat, copy=True)
+    a.sum_duplicates()
+    a.sort_indices()
+    a.data = np.ones(a.nnz, dtype=np.int8)
+    return a
+
+
+def hem_labels(pat, target, max_size=None, max_nnz=None, hub_degree=1024, topk=32,
+               residual_rounds=3, feasible_first=False, hierarchy: bool = False):
+    """HEM labels of the rows of a canonical binary pattern, before cap
+    enforcement (clustering.py:128-351).  With ``hierarchy``, returns
+    (labels, [identity, labels after level 1, ...])."""
+    n, m = pat.shape
+    indptr = np.ascontiguousarray(pat.indptr, dtype=np.int64)
+    indices = np.ascontiguousarray(pat.indices, dtype=np.int64)
+    labels = np.empty(n, dtype=np.int64)
+    slots = int(lib().oracle_hem_level_slots(int(target)))
+    hier = np.empty((slots, max(n, 1)), dtype=np.int64) if hierarchy else None
+    nlev = C.c_int64(0)
+    neg = lambda v: -1 if v is None else int(v)  # noqa: E731
+    rc = lib().oracle_hem_labels(
+        C.c_int64(n), C.c_int64(m), _p(indptr), _p(indices), C.c_int64(int(target)), C.c_int64(neg(max_size)),
+        C.c_int64(neg(max_nnz)), C.c_int64(int(hub_degree)), C.c_int64(neg(topk)), C.c_int32(residual_rounds),
+        C.c_int32(1 if feasible_first else 0), _p(labels), _p(hier) if hier is not None else None,
+        C.byref(nlev))
+    if rc:
+        raise OracleError(7)
+    if hierarchy:
+        return labels, [hier[k, :n].copy() for k in range(nlev.value)]
+    return labels
+
+
+def enforce_caps(labels, row_nnz, max_size=None, max_nnz=None):
+    """Cap enforcement + consecutive relabelling (clustering.py:83-121)."""
+    lab = np.ascontiguousarray(labels, dtype=np.int64).copy()
+    nz = np.ascontiguousarray(row_nnz, dtype=np.int64)
+    if lab.size and lib().oracle_enforce_caps(C.c_int64(lab.size), _p(lab), _p(nz),
+                                              C.c_int64(-1 if max_size is None else int(max_size)),
+                                              C.c_int64(-1 if max_nnz is None else int(max_nnz))):
+        raise OracleError(7)
+    return lab
+
+
+def hem_cluster(mat, target, max_size=None, max_nnz=None, hub_degree=1024, topk=32, feasible_first=False):
+    """int32 HEM group label per row of `mat`: the reference's
+    cluster_axis(method='hem') (clustering.py:454-509)."""
+    pat = binary_pattern(mat)
+    if pat.shape[0] == 0:
+        return np.zeros(0, dtype=np.int32)
+    lab = hem_labels(pat, target, max_size, max_nnz, hub_degree, topk, feasible_first=feasible_first)
+    return enforce_caps(lab, np.diff(pat.indptr), max_size, max_nnz).astype(np.int32)

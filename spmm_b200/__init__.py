@@ -10,7 +10,7 @@ are built on the GPU; every product runs on the GPU; there is no CPU fallback.
 from .boo import (BOOInfo, BOOMatrixInt32Double, BOOMatrixInt32Float, BOOMatrixInt64Double,
                   BOOMatrixInt64Float, BooNzOrder, BooSmallBlockPolicy, NZ_ORDERS,
                   SMALL_BLOCK_POLICIES, boo_arena_bytes, boo_info, boo_matmul, boo_to_csr,
-                  csr_to_boo)
+                  check_product, csr_to_boo, product_status)
 from .boo_plan import BOOExecutionPlan, prepare_boo_cuda
 from .clustering import CLUSTER_METHODS, cluster_axes, cluster_axis
 from .io import load_boo, load_pbr, save_boo, save_pbr
@@ -23,6 +23,7 @@ from .timed import BOOTimedSpMM, DirectSpMM, PBRTimedSpMM
 
 __all__ = [
     'csr_to_boo', 'boo_to_csr', 'boo_info', 'boo_matmul', 'boo_arena_bytes', 'BOOInfo',
+    'product_status', 'check_product',
     'SMALL_BLOCK_POLICIES', 'NZ_ORDERS', 'cluster_axes', 'cluster_axis', 'CLUSTER_METHODS',
     'csr_to_pbr', 'pbr_to_csr', 'pbr_analyze_csr', 'pbr_info', 'PBRInfo', 'BlockFillStats',
     'BlockStripeStats', 'pbr_matmul', 'pbr_batched_matmul_cpu', 'pbr_batched_matmul_cuda',

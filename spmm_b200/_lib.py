@@ -28,6 +28,8 @@ I32, I64 = 0, 1
 F32, F64 = 0, 1
 
 SPMM_ESCRATCH = 9
+SPMM_ETIMEOUT = 10
+SPMM_ENCCL = 11
 
 EXPORTS = ('spmm_status_string', 'spmm_abi_version', 'spmm_boo_build_workspace_size',
            'spmm_boo_build_analyze', 'spmm_boo_build_emit', 'spmm_boo_build_noalloc',
@@ -35,7 +37,7 @@ EXPORTS = ('spmm_status_string', 'spmm_abi_version', 'spmm_boo_build_workspace_s
            'spmm_pbr_build_analyze', 'spmm_pbr_build_emit', 'spmm_boo_matmul', 'spmm_pbr_matmul',
            'spmm_tc_status', 'spmm_boo_matmul_workspace_size', 'spmm_product_launches',
            'spmm_boo_to_csr_workspace_size', 'spmm_boo_to_csr', 'spmm_pbr_to_csr_workspace_size',
-           'spmm_pbr_to_csr', 'spmm_hem_labels')
+           'spmm_pbr_to_csr', 'spmm_hem_labels', 'spmm_hem_level_slots', 'spmm_hem_hierarchy')
 
 
 class CsrDev(C.Structure):
@@ -69,17 +71,21 @@ class PbrDev(C.Structure):
 
 class LaunchCfg(C.Structure):
     _fields_ = [('version', C.c_int32), ('slab_features', C.c_int32), ('engine', C.c_int32),
-                ('reserved', C.c_int32), ('workspace', C.c_void_p), ('workspace_bytes', C.c_uint64)]
+                ('wait_us', C.c_int32), ('workspace', C.c_void_p), ('workspace_bytes', C.c_uint64),
+                ('status', C.c_void_p)]
 
 
 ENGINES = {'auto': 0, 'cuda_cores': 1, 'tensor_cores': 2}
 
 
 def launch_cfg(engine: str = 'auto', workspace: int = 0, workspace_bytes: int = 0,
-               slab_features: int = 0) -> 'LaunchCfg':
+               slab_features: int = 0, status: int = 0, wait_us: int = 0) -> 'LaunchCfg':
+    """spmm_launch_cfg (version 2): engine, remainder slab setting, workspace
+    and the call's device status word (0 / None: none)."""
     if engine not in ENGINES:
         raise ValueError(f"engine must be one of {sorted(ENGINES)}, got {engine!r}")
-    return LaunchCfg(1, int(slab_features), ENGINES[engine], 0, workspace or None, workspace_bytes)
+    return LaunchCfg(2, int(slab_features), ENGINES[engine], int(wait_us), workspace or None, workspace_bytes,
+                     status or None)
 
 
 class SpmmError(RuntimeError):
@@ -139,6 +145,12 @@ def lib() -> C.CDLL:
                                       C.c_int64, C.c_int64, C.c_int64, C.c_int32, C.c_int32, C.c_void_p,
                                       C.c_void_p]
         L.spmm_hem_labels.restype = C.c_int
+        L.spmm_hem_level_slots.argtypes = [C.c_int64]
+        L.spmm_hem_level_slots.restype = C.c_int64
+        L.spmm_hem_hierarchy.argtypes = [C.c_int64, C.c_int64, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64,
+                                         C.c_int64, C.c_int64, C.c_int64, C.c_int32, C.c_int32, C.c_void_p,
+                                         C.c_void_p, C.c_int64, C.POINTER(C.c_int64), C.c_void_p]
+        L.spmm_hem_hierarchy.restype = C.c_int
         L.spmm_pbr_to_csr.restype = C.c_int
         for n in ('spmm_boo_build_analyze', 'spmm_boo_build_emit', 'spmm_pbr_build_analyze',
                   'spmm_pbr_build_emit', 'spmm_boo_matmul', 'spmm_pbr_matmul'):

@@ -429,9 +429,12 @@ def boo_to_csr(boo_mat) -> sp.csr_matrix:
 # SpMM
 # ---------------------------------------------------------------------------
 
-def _run_boo(boo_mat, meta, x: torch.Tensor, engine: str = 'auto', slab_features: int = 0) -> torch.Tensor:
-    cfg = _lib.launch_cfg(engine, slab_features=slab_features)
+def _run_boo(boo_mat, meta, x: torch.Tensor, engine: str = 'auto', slab_features: int = 0,
+             wait_us: int = 0) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """(Y, the call's device status word).  One scratch buffer per call from
+    torch's caching allocator: the product's workspace, then the status word."""
     device = x.device
+    status = None
     with torch.cuda.device(device):
         x3 = x if x.dim() == 3 else x.unsqueeze(0)
         x3 = x3.contiguous()
@@ -440,13 +443,36 @@ def _run_boo(boo_mat, meta, x: torch.Tensor, engine: str = 'auto', slab_features
         if y.numel():
             st = boo_mat._dev_struct(meta)
             L = _lib.lib()
+            cfg = _lib.launch_cfg(engine, slab_features=slab_features, wait_us=wait_us)
             ws_bytes = L.spmm_boo_matmul_workspace_size(C.byref(st), batch, K, C.byref(cfg))
-            ws = torch.empty(ws_bytes, dtype=torch.uint8, device=device) if ws_bytes else None
-            if ws is not None:
-                cfg.workspace, cfg.workspace_bytes = ws.data_ptr(), ws_bytes
+            off = (ws_bytes + 255) // 256 * 256
+            buf = torch.empty(off + 256, dtype=torch.uint8, device=device)
+            status = buf[off:off + 4].view(torch.int32)
+            cfg.status = status.data_ptr()
+            if ws_bytes:
+                cfg.workspace, cfg.workspace_bytes = buf.data_ptr(), ws_bytes
             rc = L.spmm_boo_matmul(C.byref(st), ptr(x3), ptr(y), batch, K, C.byref(cfg),
                                    stream_handle(device))
             _lib.check(rc, 'boo_matmul')
+    return y, status
+
+
+def product_status(y: torch.Tensor) -> int:
+    """Device-side outcome of the product that returned `y` (not in the
+    reference): SPMM_OK (0), or SPMM_ETIMEOUT when one of its bounded waits
+    expired and `y` is incomplete.  Synchronises `y`'s device."""
+    status = getattr(y, '_spmm_status', None)
+    if status is None:
+        return 0
+    return int(status.item())
+
+
+def check_product(y: torch.Tensor) -> torch.Tensor:
+    """Raises SpmmError(SPMM_ETIMEOUT) when the product that returned `y` did
+    not complete; returns `y`.  Synchronises `y`'s device."""
+    rc = product_status(y)
+    if rc:
+        raise _lib.SpmmError(rc, 'boo_matmul')
     return y
 
 
@@ -463,16 +489,20 @@ def boo_matmul(boo_mat, x: torch.Tensor, threads: int = 256, p: int = 64,
                launch_mode: str = 'legacy', execution_plan=None,
                features_per_thread: int = 1,
                nnzflat_impl: Optional[str] = None, *, engine: str = 'auto',
-               slab_features: int = 0) -> torch.Tensor:
+               slab_features: int = 0, wait_us: int = 0) -> torch.Tensor:
     """Y = A @ X (boo.py:230-354).
 
     ``engine`` (not in the reference) picks the units that multiply the
     blocks: 'auto' (tensor cores for float32 with K a multiple of 128 and
     blocks up to 64 x 64, else CUDA cores), 'cuda_cores', or 'tensor_cores'
     (an error where not applicable).  ``slab_features`` (not in the
-    reference) sets the features per pass of the remainder kernels of a
-    remainder-major matrix: 0 or less is full width (the default, faster on
-    B200), a positive value the widest supported slab not above it.
+    reference) selects the remainder kernels of a remainder-major matrix: 0
+    (default) the nnz-flat chunks, a negative value the register path (no
+    workspace).  ``wait_us`` (not in the reference) bounds the tensor-core
+    product's device waits (0: about 2 s); a product whose wait expired
+    leaves Y incomplete and reports SPMM_ETIMEOUT through
+    ``product_status(y)`` / ``check_product(y)`` (GPU ``x``; a CPU ``x``
+    raises ``SpmmError`` directly).
 
     The launch knobs of the reference's sm_86 kernels (``threads``, ``p``,
     ``csr_mode``, ``features_per_thread``, ``nnzflat_impl``, ``launch_mode``)
@@ -499,7 +529,10 @@ def boo_matmul(boo_mat, x: torch.Tensor, threads: int = 256, p: int = 64,
         require_cuda('boo_matmul')
         device = default_device()
         meta = boo_mat._staged_on(device)
-        y = _to_host(_run_boo(boo_mat, meta, x.to(device, non_blocking=True), engine, slab_features), x)
+        yd, status = _run_boo(boo_mat, meta, x.to(device, non_blocking=True), engine, slab_features)
+        y = _to_host(yd, x)                      # synchronises: the status word is final
+        if status is not None and int(status.item()):
+            raise _lib.SpmmError(int(status.item()), 'boo_matmul')
         return y.squeeze(0) if x.dim() == 2 else y
 
     meta = boo_mat._gpu_meta
@@ -538,8 +571,10 @@ def boo_matmul(boo_mat, x: torch.Tensor, threads: int = 256, p: int = 64,
             raise ValueError('Execution plan does not match this matrix and its current CUDA staging')
         if launch_mode != 'auto' or not row_seg or p != plan.p:
             raise ValueError('Execution plans require launch_mode="auto", row_seg=True and the prepared p')
-    y = _run_boo(boo_mat, meta, x, engine, slab_features)
-    return y.squeeze(0) if x.dim() == 2 else y
+    y, status = _run_boo(boo_mat, meta, x, engine, slab_features, wait_us)
+    y = y.squeeze(0) if x.dim() == 2 else y
+    y._spmm_status = status      # read by product_status / check_product
+    return y
 
 
 # ---------------------------------------------------------------------------

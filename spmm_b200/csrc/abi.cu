@@ -19,11 +19,14 @@ extern "C" const char *spmm_status_string(int status) {
         case SPMM_EALIGN: return "misaligned pointer";
         case SPMM_ESCRATCH:
             return "spmm_boo_build_noalloc: problem exceeds the 32 MiB static scratch";
+        case SPMM_ETIMEOUT:
+            return "a bounded device wait expired: the product stopped early and Y is incomplete";
+        case SPMM_ENCCL: return "a collective (NCCL / process group) failed or timed out";
         default: return "unknown status";
     }
 }
 
-extern "C" int spmm_abi_version(void) { return 1; }
+extern "C" int spmm_abi_version(void) { return 2; }
 
 namespace spmm {
 static std::atomic<uint64_t> g_product_launches{0};

@@ -16,43 +16,30 @@
 //    rejected with SPMM_ESCRATCH before any device work -- about half a
 //    million nonzeros for a square matrix.
 //  * Host code cannot pass the array's name to a kernel: in host code the
-//    name is a host-side shadow, not a device address.  So on the first call
-//    on each device (with that device current) the entry point looks the
-//    device address up with cudaGetSymbolAddress and caches it; that first
-//    call should come before any stream capture.
+//    name is a host-side shadow, not a device address.  So every call looks
+//    the device address up on the current device with cudaGetSymbolAddress
+//    (it allocates nothing) and hands that to the builder; nothing is cached,
+//    so a call after a device reset or on another device needs no set-up.
 //  * All calls share the array and it keeps the previous call's contents; the
 //    builder initialises everything it reads.  Calls whose GPU work overlaps
 //    (different streams or threads, same device) race on the array and must
 //    be serialised by the caller.
-#include <mutex>
-
 #include "common.cuh"
 
 namespace {
 
 constexpr size_t kNoallocScratchBytes = size_t(32) << 20;
-constexpr int kMaxDevices = 128;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocScratchBytes];
 
-std::mutex g_scratch_mu;
-void *g_scratch_addr[kMaxDevices];   // device address of g_noalloc_scratch, per device
-
-// Device address of the scratch array on the current device (set up once).
+// Device address of the scratch array on the current device.
 int scratch_address(void **addr) {
-    int dev = -1;
-    if (cudaGetDevice(&dev) != cudaSuccess) return SPMM_ECUDA;
-    if (dev < 0 || dev >= kMaxDevices) return SPMM_EUNSUPPORTED;
-    std::lock_guard<std::mutex> lock(g_scratch_mu);
-    if (g_scratch_addr[dev] == nullptr) {
-        void *p = nullptr;
-        if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) {
-            (void)cudaGetLastError();
-            return SPMM_ECUDA;
-        }
-        g_scratch_addr[dev] = p;
+    void *p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) {
+        (void)cudaGetLastError();
+        return SPMM_ECUDA;
     }
-    *addr = g_scratch_addr[dev];
+    *addr = p;
     return SPMM_OK;
 }
 

@@ -745,18 +745,40 @@ int similarity_graph(const int64_t *ptr, const int32_t *idx, int64_t n, int64_t 
 
 using namespace spmm;
 
-extern "C" int spmm_hem_labels(int64_t rows, int64_t cols, const int64_t *indptr, const int32_t *indices,
-                               int64_t target, int64_t max_size, int64_t max_nnz, int64_t hub_degree, int64_t topk,
-                               int32_t residual_rounds, int32_t feasible_first, int64_t *labels,
-                               spmm_stream_t stream) {
+// Levels the matching loop may run for `target` (the reference's cap,
+// clustering.py:291-296): 8 * max(1, ceil(log2(target))) + 16.
+static int hem_max_levels(int64_t target) {
+    int lg = 0;
+    while ((1ll << lg) < target) ++lg;
+    return 8 * (lg > 1 ? lg : 1) + 16;
+}
+
+extern "C" int64_t spmm_hem_level_slots(int64_t target) { return (int64_t)hem_max_levels(target) + 1; }
+
+extern "C" int spmm_hem_hierarchy(int64_t rows, int64_t cols, const int64_t *indptr, const int32_t *indices,
+                                  int64_t target, int64_t max_size, int64_t max_nnz, int64_t hub_degree, int64_t topk,
+                                  int32_t residual_rounds, int32_t feasible_first, int64_t *labels, int64_t *levels,
+                                  int64_t level_slots, int64_t *n_levels, spmm_stream_t stream) {
     if (rows < 0 || cols < 0 || !labels || (rows > 0 && !indptr) || hub_degree < 0 || residual_rounds < 0)
         return SPMM_EINVAL;
+    if (levels && (!n_levels || level_slots < spmm_hem_level_slots(target))) return SPMM_EINVAL;
     if (rows > 0x7fffffffLL || cols > 0x7fffffffLL) return SPMM_EUNSUPPORTED;
     cudaStream_t s = (cudaStream_t)stream;
+    int64_t recorded = 0;
+    if (n_levels) *n_levels = 0;
     if (rows == 0) return SPMM_OK;
     iota64_kernel<<<grid_for(rows, kHemThreads), kHemThreads, 0, s>>>(labels, rows);
     SPMM_LAUNCH_CHECK();
-    if (rows <= 1 || target <= 1) return SPMM_OK;
+    // levels[k][rows]: identity, then the labels after each level that matched
+    auto record = [&]() -> int {
+        if (!levels) return SPMM_OK;
+        SPMM_CUDA_TRY(cudaMemcpyAsync(levels + recorded * rows, labels, (size_t)rows * 8, cudaMemcpyDeviceToDevice, s));
+        *n_levels = ++recorded;
+        return SPMM_OK;
+    };
+    SPMM_TRY(record());
+    if (rows <= 1 || target <= 1) return levels ? (cudaStreamSynchronize(s) == cudaSuccess ? SPMM_OK : SPMM_ECUDA)
+                                                : SPMM_OK;
     int64_t nnz0 = 0;
     SPMM_TRY(to_host(&nnz0, indptr + rows, 1, s));
     const Caps caps{max_size, max_nnz};
@@ -774,9 +796,7 @@ extern "C" int spmm_hem_labels(int64_t rows, int64_t cols, const int64_t *indptr
     SPMM_LAUNCH_CHECK();
     diff_kernel<<<grid_for(n, kHemThreads), kHemThreads, 0, s>>>(lptr.p, n, rnnz.p);
     SPMM_LAUNCH_CHECK();
-    int lg = 0;
-    while ((1ll << lg) < target) ++lg;
-    const int max_levels = 8 * (lg > 1 ? lg : 1) + 16;
+    const int max_levels = hem_max_levels(target);
     DBuf<unsigned long long> matched;
     SPMM_TRY(matched.alloc(1, s));
     for (int level = 0; level < max_levels && n > 1; ++level) {
@@ -838,6 +858,7 @@ extern "C" int spmm_hem_labels(int64_t rows, int64_t cols, const int64_t *indptr
         SPMM_LAUNCH_CHECK();
         relabel_kernel<<<grid_for(rows, kHemThreads), kHemThreads, 0, s>>>(labels, rows, new_id.p);
         SPMM_LAUNCH_CHECK();
+        SPMM_TRY(record());
         SPMM_TRY(size.alloc(n_new, s));
         SPMM_TRY(rnnz.alloc(n_new, s));
         copy_cast_kernel<int64_t><<<grid_for(n_new, kHemThreads), kHemThreads, 0, s>>>(nsize.p, size.p, n_new);
@@ -851,4 +872,12 @@ extern "C" int spmm_hem_labels(int64_t rows, int64_t cols, const int64_t *indptr
     }
     SPMM_CUDA_TRY(cudaStreamSynchronize(s));
     return SPMM_OK;
+}
+
+extern "C" int spmm_hem_labels(int64_t rows, int64_t cols, const int64_t *indptr, const int32_t *indices,
+                               int64_t target, int64_t max_size, int64_t max_nnz, int64_t hub_degree, int64_t topk,
+                               int32_t residual_rounds, int32_t feasible_first, int64_t *labels,
+                               spmm_stream_t stream) {
+    return spmm_hem_hierarchy(rows, cols, indptr, indices, target, max_size, max_nnz, hub_degree, topk,
+                              residual_rounds, feasible_first, labels, nullptr, 0, nullptr, stream);
 }

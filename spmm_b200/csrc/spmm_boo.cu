@@ -23,7 +23,7 @@
 namespace spmm {
 
 int boo_matmul_tc(const spmm_boo_dev *A, const float *X, float *Y, int64_t batch, int64_t K, void *ws,
-                  size_t ws_bytes, cudaStream_t s);
+                  size_t ws_bytes, int32_t *status, int32_t wait_us, cudaStream_t s);
 size_t boo_tc_workspace(const spmm_boo_dev *A, int64_t batch, int64_t K);
 
 namespace {
@@ -353,21 +353,13 @@ int launch_boo_n(BooParams<S> p, int64_t n_rg, cudaStream_t s) {
 // boo_kernel.cu:905-937, runs one thread block per row) rows are skewed: up to
 // tens of thousands of entries next to a median of ~20.  Three launches on the
 // stream, each Y element written once and then updated once at most:
-//   * the rows of at most kLongRow entries, by one of two kernels:
-//     - rem_tile_kernel (the default): warp tiles of 32
+//   * the rows of at most kLongRow entries (rem_tile_kernel): warp tiles of 32
 //       consecutive rows dealt round-robin to all warps; the tile's row
 //       pointers in one coalesced load; per row the (column, value) pairs are
 //       fetched 32 at a time by the lanes (the next row's first chunk while the
 //       current row's X rows are in flight) and broadcast by shuffles, 8 / VPT
 //       X rows in flight per warp;
-//     - rem_slab_kernel (spmm_launch_cfg::slab_features > 0): the same warp tiles, but each
-//       launch slice covers a narrow slab of W features, so the slab of every
-//       X row fits in L2 and the reuse of popular columns hits there (A is read
-//       once per slab).  A group of LPE lanes covers one row's slab; the
-//       warp's 32 / LPE groups take the tile's rows greedily, a group that
-//       finishes a row claiming the next one, so rows of any length share the
-//       warp without padding;
-//     both store Y for every such row (zeros for empty rows);
+//     it stores Y for every such row (zeros for empty rows);
 //   * rem_long_kernel: a CTA per tile of 512 rows takes every longer row of
 //     its tile; its 16 warps each sum a contiguous sixteenth of the row and the
 //     CTA adds the partials in warp order and stores Y;
@@ -377,9 +369,6 @@ int launch_boo_n(BooParams<S> p, int64_t n_rg, cudaStream_t s) {
 constexpr int kLongRow = 1024;
 constexpr int kRemWarps = 8;    // warps per CTA of the tile kernel
 constexpr int kLongWarps = 16;  // warps sharing one long row, 16 / VPT X rows in flight each
-// resident CTAs per SM of the slab kernel (register budget: LPE X slabs in flight)
-template <int LPE>
-constexpr int slab_blocks() { return LPE >= 8 ? 2 : 4; }
 
 // acc += sum over entries [e0, e1) of val * X[col]; (c, v) = this lane's
 // entry e0 + lane (already loaded by the caller).
@@ -493,104 +482,6 @@ __global__ void __launch_bounds__(32 * kRemWarps, 2) rem_tile_kernel(const BooPa
     }
 }
 
-// Rows of at most kLongRow entries over slab blockIdx.y of W = LPE * VEC
-// features.  Each step a group's lanes hold LPE (column, value) pairs of its
-// row (the next step's pairs are fetched while this step's X slabs are in
-// flight), broadcast them within the group and each fetch LPE X slabs.
-template <typename S, int VEC, int LPE>
-__global__ void __launch_bounds__(32 * kRemWarps, slab_blocks<LPE>()) rem_slab_kernel(const BooParams<S> p) {
-    constexpr int W = LPE * VEC;
-    constexpr int G = 32 / LPE;   // rows in flight per warp
-    __shared__ int32_t sptr[kRemWarps][33];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int lig = lane % LPE, gl = lane - lig;   // lane in group, group's first lane
-    const unsigned before = (1u << gl) - 1u;       // lanes of the groups before this one
-    const int64_t f0 = (int64_t)blockIdx.y * W + (int64_t)lig * VEC;
-    const bool fm = f0 < p.K;
-    int32_t *sp = sptr[warp];
-    const int64_t nwarps = (int64_t)gridDim.x * kRemWarps;
-    const int64_t ntiles = (p.rows + 31) / 32;
-    for (int64_t bt = blockIdx.z; bt < p.batch; bt += gridDim.z) {
-        const S *xl = p.X + bt * p.cols * p.K + f0;
-        S *yb = p.Y + bt * p.rows * p.K + f0;
-        for (int64_t t = (int64_t)blockIdx.x * kRemWarps + warp; t < ntiles; t += nwarps) {
-            const int64_t r0 = t * 32;
-            const int nrow = p.rows - r0 < 32 ? (int)(p.rows - r0) : 32;
-            __syncwarp();
-            if (lane < nrow) sp[lane] = __ldg(p.rem_indptr + r0 + lane);
-            if (lane == 0) sp[nrow] = __ldg(p.rem_indptr + r0 + nrow);
-            __syncwarp();
-            int row = 0, next = G;
-            int64_t e = 0, eend = 0;
-            bool keep = false;   // false: empty slot, or a long row (rem_long_kernel stores it)
-            auto open = [&](int r) {
-                row = r;
-                e = eend = 0;
-                keep = false;
-                if (r < nrow) {
-                    e = sp[r];
-                    eend = sp[r + 1];
-                    keep = eend - e <= kLongRow;
-                    if (!keep) e = eend;
-                }
-            };
-            open(gl / LPE);
-            int32_t c = 0;
-            S v = S(0);
-            if (e + lig < eend) {
-                c = __ldg(p.rem_col + e + lig);
-                v = __ldg(p.rem_val + e + lig);
-            }
-            Frag<S, VEC> acc;
-#pragma unroll
-            for (int q = 0; q < VEC; ++q) acc.v[q] = S(0);
-            while (__any_sync(kFullMask, row < nrow)) {
-                int32_t cn = 0;
-                S vn = S(0);
-                if (e + LPE + lig < eend) {
-                    cn = __ldg(p.rem_col + e + LPE + lig);
-                    vn = __ldg(p.rem_val + e + LPE + lig);
-                }
-                Frag<S, VEC> x[LPE];
-                S a[LPE];
-#pragma unroll
-                for (int u = 0; u < LPE; ++u) {
-                    const int32_t cu = __shfl_sync(kFullMask, c, gl + u);
-                    a[u] = __shfl_sync(kFullMask, v, gl + u);
-                    if (fm && e + u < eend) {
-                        x[u] = ldg_frag<S, VEC>(xl + (int64_t)cu * p.K);
-                    } else {
-#pragma unroll
-                        for (int q = 0; q < VEC; ++q) x[u].v[q] = S(0);
-                    }
-                }
-#pragma unroll
-                for (int u = 0; u < LPE; ++u)
-#pragma unroll
-                    for (int q = 0; q < VEC; ++q) acc.v[q] = fma(a[u], x[u].v[q], acc.v[q]);
-                e += LPE;
-                const bool fin = row < nrow && e >= eend;
-                if (fin && keep && fm) st_frag<S, VEC>(yb + (r0 + row) * p.K, acc);
-                const unsigned fb = __ballot_sync(kFullMask, fin && lig == 0);
-                if (fin) {
-#pragma unroll
-                    for (int q = 0; q < VEC; ++q) acc.v[q] = S(0);
-                    open(next + __popc(fb & before));
-                    c = 0;
-                    v = S(0);
-                    if (e + lig < eend) {
-                        c = __ldg(p.rem_col + e + lig);
-                        v = __ldg(p.rem_val + e + lig);
-                    }
-                } else {
-                    c = cn;
-                    v = vn;
-                }
-                next += __popc(fb);
-            }
-        }
-    }
-}
 
 // ---- nnz-flat remainder (default on the aligned path) ----
 //
@@ -905,36 +796,6 @@ __global__ void __launch_bounds__(32 * kLongWarps, 1) rem_long_kernel(const BooP
     }
 }
 
-// Slab width of the remainder pass: 0 for full-width tiles, else W features
-// per launch slice (W = LPE * VEC, LPE in {2, 4, 8}), the widest not above
-// spmm_launch_cfg::slab_features.  Full width unless asked: on B200 the narrow
-// slabs lose for every remainder-major shape measured (power-law 2M x 2M,
-// K = 256: 12.1 ms full width, 22-24 ms at W = 16 / 32, 52 ms at W = 8) --
-// a slab of a row-major X fills half an L2 line, so the X slabs do not stay
-// resident (L2 hit rate 37% against 20%), and the K / W times more memory
-// requests leave the kernel latency-bound.
-template <typename S, int VEC>
-int rem_slab_width(const BooParams<S> &p, int requested) {
-    if (requested < 0) return -1;   // full width through registers (rem_tile_kernel)
-    if (p.K % VEC || requested == 0) return 0;
-    int w = 0;
-    for (int lpe = 8; lpe >= 2; lpe >>= 1)
-        if (!w && lpe * VEC <= requested) w = lpe * VEC;
-    return w < p.K ? w : 0;
-}
-
-template <typename S, int VEC, int LPE>
-int launch_rem_slab(const BooParams<S> &p, int sms, unsigned bz, cudaStream_t s) {
-    const int64_t slabs = ceil_div(p.K, (int64_t)(LPE * VEC));
-    if (slabs > 65535) return SPMM_EUNSUPPORTED;
-    const int64_t tile_ctas = ceil_div(ceil_div(p.rows, (int64_t)32), (int64_t)kRemWarps);
-    const int64_t cap = (int64_t)sms * slab_blocks<LPE>() * 2;
-    const int64_t g1 = tile_ctas < cap ? tile_ctas : cap;
-    rem_slab_kernel<S, VEC, LPE><<<dim3((unsigned)g1, (unsigned)slabs, bz), 32 * kRemWarps, 0, s>>>(p);
-    SPMM_PRODUCT_LAUNCHED();
-    return SPMM_OK;
-}
-
 // Chunk size of the nnz-flat remainder: about 8192 chunks, 256..2048 entries.
 inline int32_t rem_flat_chunk(int64_t rem_nnz) {
     const int64_t c = ceil_div(rem_nnz, (int64_t)8192);
@@ -949,21 +810,15 @@ inline size_t rem_flat_workspace(int64_t rem_nnz, int64_t batch, int64_t K, size
     return (size_t)ceil_div(nch * 4, (int64_t)256) * 256 + (size_t)(batch * nch * 2 * K) * elem;
 }
 
-// The nnz-flat remainder (plan, chunks, fix-up) on scratch from `ws` or, when
-// that is absent or short, from the stream-ordered allocator.
+// The nnz-flat remainder (plan, chunks, fix-up) on the caller's scratch `ws`
+// (rem_flat_workspace() bytes, checked by the caller).
 template <typename S, int VEC, int VPT>
-int launch_rem_flat(BooParams<S> p, int sms, unsigned bz, void *ws, size_t ws_bytes, cudaStream_t s) {
+int launch_rem_flat(BooParams<S> p, int sms, unsigned bz, void *ws, cudaStream_t s) {
     using Sh = AsyncShape<S, VEC, VPT>;
     const int64_t slabs = ceil_div(p.K, (int64_t)Sh::kSlab);
     if (slabs > 65535 || p.rem_nnz > 0x7fffffffLL) return SPMM_EUNSUPPORTED;
     p.chunk = rem_flat_chunk(p.rem_nnz);
     p.nch = ceil_div(p.rem_nnz, (int64_t)p.chunk);
-    const size_t need = rem_flat_workspace(p.rem_nnz, p.batch, p.K, sizeof(S));
-    void *own = nullptr;
-    if (!ws || ws_bytes < need) {
-        SPMM_CUDA_TRY(cudaMallocAsync(&own, need, s));
-        ws = own;
-    }
     p.chunk_row = reinterpret_cast<int32_t *>(ws);
     p.part = reinterpret_cast<S *>(reinterpret_cast<uint8_t *>(ws) + ceil_div(p.nch * 4, (int64_t)256) * 256);
     auto kern = rem_flat_kernel<S, VEC, VPT>;
@@ -988,19 +843,14 @@ int launch_rem_flat(BooParams<S> p, int sms, unsigned bz, void *ws, size_t ws_by
         e = cudaGetLastError();
         if (e == cudaSuccess) note_product_launch();
     }
-    if (own) {
-        const cudaError_t f = cudaFreeAsync(own, s);
-        if (e == cudaSuccess) e = f;
-    }
     return e == cudaSuccess ? SPMM_OK : SPMM_ECUDA;
 }
 
-// The CSR remainder of every row into Y: nnz-flat chunks (slab_w == 0, the
-// aligned default), else rows of at most kLongRow entries in slabs of slab_w
-// features (> 0) or at full width through registers (< 0; also the unaligned
-// path), then the long rows at full width.
+// The CSR remainder of every row into Y: nnz-flat chunks (`flat`: aligned X
+// and Y, the default), else rows of at most kLongRow entries at full width
+// through registers, then the long rows.
 template <typename S, int VEC, int VPT>
-int launch_rem(const BooParams<S> &p, int slab_w, void *ws, size_t ws_bytes, cudaStream_t s) {
+int launch_rem(const BooParams<S> &p, bool flat, void *ws, cudaStream_t s) {
     constexpr int SLAB = 32 * VPT * VEC;
     const int64_t slabs = ceil_div(p.K, SLAB);
     if (slabs > 65535) return SPMM_EUNSUPPORTED;
@@ -1009,25 +859,12 @@ int launch_rem(const BooParams<S> &p, int slab_w, void *ws, size_t ws_bytes, cud
     SPMM_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const unsigned bz = (unsigned)(p.batch < 65535 ? p.batch : 65535);
     if constexpr (VEC > 1) {
-        if (slab_w == 0) return launch_rem_flat<S, VEC, VPT>(p, sms, bz, ws, ws_bytes, s);
-        if (slab_w == 8 * VEC) {
-            SPMM_TRY(launch_rem_slab<S, VEC, 8>(p, sms, bz, s));
-        } else if (slab_w == 4 * VEC) {
-            SPMM_TRY(launch_rem_slab<S, VEC, 4>(p, sms, bz, s));
-        } else if (slab_w == 2 * VEC) {
-            SPMM_TRY(launch_rem_slab<S, VEC, 2>(p, sms, bz, s));
-        } else {
-            slab_w = -1;
-        }
-    } else {
-        slab_w = -1;
+        if (flat) return launch_rem_flat<S, VEC, VPT>(p, sms, bz, ws, s);
     }
-    if (slab_w < 0) {
-        const int64_t tile_ctas = ceil_div(ceil_div(p.rows, (int64_t)32), (int64_t)kRemWarps);
-        const int64_t g1 = tile_ctas < (int64_t)sms * 8 ? tile_ctas : (int64_t)sms * 8;
-        rem_tile_kernel<S, VEC, VPT><<<dim3((unsigned)g1, (unsigned)slabs, bz), 32 * kRemWarps, 0, s>>>(p);
-        SPMM_PRODUCT_LAUNCHED();
-    }
+    const int64_t tile_ctas = ceil_div(ceil_div(p.rows, (int64_t)32), (int64_t)kRemWarps);
+    const int64_t g1 = tile_ctas < (int64_t)sms * 8 ? tile_ctas : (int64_t)sms * 8;
+    rem_tile_kernel<S, VEC, VPT><<<dim3((unsigned)g1, (unsigned)slabs, bz), 32 * kRemWarps, 0, s>>>(p);
+    SPMM_PRODUCT_LAUNCHED();
     const int64_t g2 = ceil_div(p.rows, (int64_t)(32 * kLongWarps));
     if (g2 > 0x7fffffffLL) return SPMM_EUNSUPPORTED;
     rem_long_kernel<S, VEC, VPT><<<dim3((unsigned)g2, (unsigned)slabs, bz), 32 * kLongWarps, 0, s>>>(p);
@@ -1035,29 +872,25 @@ int launch_rem(const BooParams<S> &p, int slab_w, void *ws, size_t ws_bytes, cud
     return SPMM_OK;
 }
 
+// Vector width of the remainder pass: 16-byte X / Y accesses when both are
+// 16-byte aligned and K is a multiple of the vector; 1 otherwise.
 template <typename S>
-int rem_dispatch(const BooParams<S> &p, bool aligned, int slab_req, void *ws, size_t ws_bytes, cudaStream_t s);
+constexpr int rem_vec() { return 16 / (int)sizeof(S); }
 
-template <>
-int rem_dispatch<float>(const BooParams<float> &p, bool aligned, int slab_req, void *ws, size_t ws_bytes,
-                        cudaStream_t s) {
-    if (aligned && p.K % 4 == 0) {
-        const int w = rem_slab_width<float, 4>(p, slab_req);
-        if (p.K <= 128) return launch_rem<float, 4, 1>(p, w, ws, ws_bytes, s);
-        return launch_rem<float, 4, 2>(p, w, ws, ws_bytes, s);
-    }
-    return launch_rem<float, 1, 4>(p, -1, ws, ws_bytes, s);
+template <typename S>
+bool rem_flat_applies(const BooParams<S> &p, bool aligned, int slab_req) {
+    return aligned && p.K % rem_vec<S>() == 0 && slab_req >= 0;
 }
 
-template <>
-int rem_dispatch<double>(const BooParams<double> &p, bool aligned, int slab_req, void *ws, size_t ws_bytes,
-                         cudaStream_t s) {
-    if (aligned && p.K % 2 == 0) {
-        const int w = rem_slab_width<double, 2>(p, slab_req);
-        if (p.K <= 64) return launch_rem<double, 2, 1>(p, w, ws, ws_bytes, s);
-        return launch_rem<double, 2, 2>(p, w, ws, ws_bytes, s);
+template <typename S>
+int rem_dispatch(const BooParams<S> &p, bool aligned, int slab_req, void *ws, cudaStream_t s) {
+    constexpr int V = rem_vec<S>();
+    const bool flat = rem_flat_applies(p, aligned, slab_req);
+    if (aligned && p.K % V == 0) {
+        if (p.K <= 32 * V) return launch_rem<S, V, 1>(p, flat, ws, s);
+        return launch_rem<S, V, 2>(p, flat, ws, s);
     }
-    return launch_rem<double, 1, 4>(p, -1, ws, ws_bytes, s);
+    return launch_rem<S, 1, 4>(p, false, ws, s);
 }
 
 template <typename S>
@@ -1106,10 +939,13 @@ bool tc_selected(const spmm_boo_dev *A, int engine) {
 template <typename S>
 int boo_matmul_impl(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch, int64_t K, int engine,
                     const spmm_launch_cfg *cfg, cudaStream_t s) {
+    void *ws = cfg ? cfg->workspace : nullptr;
+    const size_t ws_bytes = cfg && ws ? (size_t)cfg->workspace_bytes : 0;
     if constexpr (sizeof(S) == 4) {
         if (tc_selected(A, engine)) {
-            const int rc = boo_matmul_tc(A, (const float *)X, (float *)Y, batch, K, cfg ? cfg->workspace : nullptr,
-                                         cfg ? (size_t)cfg->workspace_bytes : 0, s);
+            int32_t *status = cfg && cfg->version >= 2 ? cfg->status : nullptr;
+            const int rc = boo_matmul_tc(A, (const float *)X, (float *)Y, batch, K, ws, ws_bytes, status,
+                                         cfg ? cfg->wait_us : 0, s);
             if (rc != SPMM_EUNSUPPORTED || engine == SPMM_ENGINE_TENSOR_CORES) return rc;
         }
     } else {
@@ -1148,16 +984,19 @@ int boo_matmul_impl(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch
     p.chunk = 0;
     p.chunk_row = nullptr;
     p.part = nullptr;
-    const uintptr_t mis = ((uintptr_t)X | (uintptr_t)Y) & 15;
+    const bool aligned = (((uintptr_t)X | (uintptr_t)Y) & 15) == 0;
     // remainder-major matrices: the load-balanced remainder kernels write Y,
     // then the block kernel adds blocks and tail where a row group has any
     p.skip_rem = A->rem_nnz > 0 && 2 * A->rem_nnz >= A->total_nnz;
     if (p.skip_rem) {
-        const int rc = rem_dispatch<S>(p, mis == 0, cfg ? cfg->slab_features : 0, cfg ? cfg->workspace : nullptr,
-                                       cfg ? (size_t)cfg->workspace_bytes : 0, s);   // Y = remainder
+        const int slab_req = cfg ? cfg->slab_features : 0;
+        if (rem_flat_applies(p, aligned, slab_req) &&
+            (!ws || ws_bytes < rem_flat_workspace(A->rem_nnz, batch, K, sizeof(S))))
+            return SPMM_EWORKSPACE;
+        const int rc = rem_dispatch<S>(p, aligned, slab_req, ws, s);   // Y = remainder
         if (rc != SPMM_OK) return rc;
     }
-    return boo_dispatch<S>(p, A->n_rg, mis == 0, s);      // (+)= blocks and tail
+    return boo_dispatch<S>(p, A->n_rg, aligned, s);      // (+)= blocks and tail
 }
 
 }  // namespace
@@ -1169,14 +1008,18 @@ using namespace spmm;
 extern "C" int spmm_boo_matmul(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch, int64_t K,
                                const spmm_launch_cfg *cfg, spmm_stream_t stream) {
     if (!A || batch < 0 || K < 0) return SPMM_EINVAL;
-    if (cfg && cfg->version != 1) return SPMM_EINVAL;
+    if (cfg && cfg->version != 1 && cfg->version != 2) return SPMM_EINVAL;
     const int engine = cfg ? cfg->engine : SPMM_ENGINE_AUTO;
     if (engine < SPMM_ENGINE_AUTO || engine > SPMM_ENGINE_TENSOR_CORES) return SPMM_EINVAL;
+    if (cfg && cfg->wait_us < 0) return SPMM_EINVAL;
     if (A->scalar_type != SPMM_F32 && A->scalar_type != SPMM_F64) return SPMM_EINVAL;
     if (A->nz_order != SPMM_BOO_ROWMAJOR && A->nz_order != SPMM_BOO_COLMAJOR) return SPMM_EINVAL;
     if (A->rows < 0 || A->cols < 0 || A->n_rg < 0 || A->nb < 0 || A->tail_nnz < 0) return SPMM_EINVAL;
     if (A->rows > 0x7fffffffLL || A->cols > 0x7fffffffLL) return SPMM_EUNSUPPORTED;
     if (A->max_nr > 65536 || A->max_nc > 65536) return SPMM_EUNSUPPORTED;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (cfg && cfg->version >= 2 && cfg->status)   // this call's status word starts at 0
+        SPMM_CUDA_TRY(cudaMemsetAsync(cfg->status, 0, sizeof(int32_t), s));
     if (batch == 0 || K == 0 || A->rows == 0) return SPMM_OK;
     if (!Y || (A->cols && !X)) return SPMM_EINVAL;
     if (!A->row_grp_ptr || !A->row_ids || !A->rem_indptr) return SPMM_EINVAL;
@@ -1184,7 +1027,6 @@ extern "C" int spmm_boo_matmul(const spmm_boo_dev *A, const void *X, void *Y, in
                   !A->nz_idx || !A->nz_val || !A->col_grp_ptr || !A->col_ids))
         return SPMM_EINVAL;
     if (A->n_rg == 0) return SPMM_EINVAL;  // rows > 0 need at least one group
-    cudaStream_t s = (cudaStream_t)stream;
     if (A->scalar_type == SPMM_F32) return boo_matmul_impl<float>(A, X, Y, batch, K, engine, cfg, s);
     return boo_matmul_impl<double>(A, X, Y, batch, K, engine, cfg, s);
 }
@@ -1193,11 +1035,14 @@ extern "C" size_t spmm_boo_matmul_workspace_size(const spmm_boo_dev *A, int64_t 
                                                  const spmm_launch_cfg *cfg) {
     if (!A || batch <= 0 || K <= 0) return 0;
     if (A->scalar_type != SPMM_F32 && A->scalar_type != SPMM_F64) return 0;
-    if (cfg && cfg->version != 1) return 0;
-    if (A->scalar_type == SPMM_F32 && tc_selected(A, cfg ? cfg->engine : SPMM_ENGINE_AUTO))
-        return boo_tc_workspace(A, batch, K);
-    // remainder-major: the nnz-flat remainder's scratch (default slab setting)
+    if (cfg && cfg->version != 1 && cfg->version != 2) return 0;
+    if (A->scalar_type == SPMM_F32 && tc_selected(A, cfg ? cfg->engine : SPMM_ENGINE_AUTO)) {
+        const size_t w = boo_tc_workspace(A, batch, K);
+        if (w || (cfg && cfg->engine == SPMM_ENGINE_TENSOR_CORES)) return w;
+    }
+    // remainder-major: the nnz-flat remainder's scratch (16-byte aligned X and Y)
     const bool rem_major = A->rem_nnz > 0 && 2 * A->rem_nnz >= A->total_nnz;
-    if (!rem_major || (cfg && cfg->slab_features != 0)) return 0;
-    return rem_flat_workspace(A->rem_nnz, batch, K, A->scalar_type == SPMM_F32 ? 4 : 8);
+    const size_t elem = A->scalar_type == SPMM_F32 ? 4 : 8;
+    if (!rem_major || (cfg && cfg->slab_features < 0) || K % (int64_t)(16 / elem)) return 0;
+    return rem_flat_workspace(A->rem_nnz, batch, K, elem);
 }

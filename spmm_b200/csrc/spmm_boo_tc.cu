@@ -56,7 +56,9 @@
 
 namespace spmm {
 
-__device__ int g_tc_status;  // 0, or the first abort code of a tensor-core launch
+// Status word of launches given none by the caller (spmm_launch_cfg::status):
+// 0, or SPMM_ETIMEOUT once a bounded wait of such a launch expired.
+__device__ int g_tc_status;
 
 namespace {
 
@@ -70,7 +72,7 @@ constexpr int kSegs = 32;            // blocks or rows listed per pass
 constexpr int kWin = 3;              // windows of 32 candidate segments loaded at once
 constexpr int kListCap = 512;        // staged (row, column, value) entries per pass
 constexpr int kNzPre = 4;            // nonzeros per thread fetched ahead
-constexpr long long kWaitCycles = 1ll << 32;  // ~2 s at 2 GHz
+constexpr long long kWaitCycles = 1ll << 32;  // ~2 s at 2 GHz (default bound of a wait)
 
 struct TcParams {
     int64_t rows, cols, K, nb, n_rg, rem_nnz, tail_nnz;
@@ -90,6 +92,8 @@ struct TcParams {
     float *Y;
     const float4 *Xt;  // X gathered by column group: [batch][n_cg][PW/4][K] float4
     int64_t n_cg;
+    int *status;          // this launch's status word (the caller's, or g_tc_status)
+    long long wait_cycles;  // bound of the abortable waits, in SM clock cycles
 };
 
 // One worker's shared memory.
@@ -134,9 +138,9 @@ struct TcShape {
 
 // ---- bounded waits ------------------------------------------------------
 
-__device__ __forceinline__ void raise_abort(volatile int *abort, int code) {
+__device__ __forceinline__ void raise_abort(volatile int *abort, int *status) {
     *abort = 1;
-    atomicCAS(&g_tc_status, 0, code);
+    atomicCAS(status, 0, (int)SPMM_ETIMEOUT);
 }
 
 // One poll of `bar`; the thread may sleep in the hardware until the phase
@@ -156,7 +160,8 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t pari
 // Waits for the phase of `bar` with the given parity; false on abort/expiry.
 // Called by one thread per role (the rest of a warpgroup waits in a named
 // barrier), so polling costs few issue slots.
-__device__ __forceinline__ bool wait_phase(uint64_t *bar, uint32_t parity, volatile int *abort, int code) {
+__device__ __forceinline__ bool wait_phase(uint64_t *bar, uint32_t parity, volatile int *abort, int *status,
+                                           long long limit) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
     for (;;) {
@@ -164,8 +169,8 @@ __device__ __forceinline__ bool wait_phase(uint64_t *bar, uint32_t parity, volat
         for (int i = 0; i < 16; ++i)
             if (mbar_try_wait_sleep(bar, parity)) return true;
         if (*abort) return false;
-        if (clock64() - t0 > kWaitCycles) {
-            raise_abort(abort, code);
+        if (clock64() - t0 > limit) {
+            raise_abort(abort, status);
             return false;
         }
     }
@@ -479,6 +484,21 @@ __device__ __forceinline__ void rare_part(const TcParams &p, WorkerSmem<NR, PW> 
     }
 }
 
+// Rows NR, 2 NR, ... of a row group larger than NR (no kept blocks there):
+// their CSR remainder and COO tail on CUDA cores, NR rows at a time.  Kept out
+// of line: it is rare, and the worker's registers stay for the common case.
+template <int NR, int PW>
+__device__ __noinline__ void large_group_rows(const TcParams &p, WorkerSmem<NR, PW> &w, int64_t b, int32_t rbase,
+                                              int32_t nr, const float *xb, float *yb, int wt, uint32_t bar) {
+    for (int32_t r0 = NR; r0 < nr; r0 += NR) {
+        const int32_t rb = rbase + r0, nrc = nr - r0 < NR ? nr - r0 : NR;
+        for (int r = 0; r < NR; ++r) w.ys[r][wt] = 0.f;
+        if (p.rem_nnz) cuda_part<NR, PW>(p, w, b, b, rb, nrc, xb, wt, bar);
+        if (p.tail_nnz) rare_part<NR, PW>(p, w, b, b, rb, nrc, false, xb, wt);
+        for (int r = 0; r < nrc; ++r) __stcs(yb + (int64_t)__ldg(p.row_ids + rb + r) * p.K, w.ys[r][wt]);
+    }
+}
+
 // One row-group worker (a warpgroup; wt = thread in the worker, tensor-memory
 // lane wt).  `tcol`: first of its 2 NR accumulator + 2 PW panel columns.
 template <int NR, int PW>
@@ -498,7 +518,7 @@ __device__ void worker(const TcParams &p, WorkerSmem<NR, PW> &w, Ctl &ctl, uint3
     // Thread 0 waits, the warpgroup learns the (uniform) outcome at a barrier.
     auto wait_commit = [&](uint32_t c) -> bool {
         bool r = true;
-        if (wt == 0) r = wait_phase(&w.mma_bar, c & 1u, abort, 4);
+        if (wt == 0) r = wait_phase(&w.mma_bar, c & 1u, abort, p.status, p.wait_cycles);
         return bar_and(bar, 128, r);
     };
     auto prefetch = [&](int i, uint16_t (&ip)[kNzPre], float (&vp)[kNzPre]) {
@@ -524,12 +544,6 @@ __device__ void worker(const TcParams &p, WorkerSmem<NR, PW> &w, Ctl &ctl, uint3
             const int64_t be = group_end(p.blk_row_grp, p.nb, b, rg, lane);
             const int32_t rbase = __ldg(p.row_grp_ptr + rg);
             const int32_t nr = __ldg(p.row_grp_ptr + rg + 1) - rbase;
-            int32_t myrow[RH];
-#pragma unroll
-            for (int h = 0; h < RH; ++h) {
-                const int r = h * 32 + lane;
-                myrow[h] = r < nr && r < NR ? __ldg(p.row_ids + rbase + r) : -1;
-            }
             uint32_t started = 0;
             bool special = false, sparse = false;
             // ---- tensor-core blocks, listed kSegs blocks at a time ----
@@ -690,13 +704,20 @@ __device__ void worker(const TcParams &p, WorkerSmem<NR, PW> &w, Ctl &ctl, uint3
             }
             if (!ok) break;
             const bool any_dense = started != 0;
+            const int32_t nrc = nr < NR ? nr : NR;
+            int32_t myrow[RH];
+#pragma unroll
+            for (int h = 0; h < RH; ++h) {
+                const int r = h * 32 + lane;
+                myrow[h] = r < nrc ? __ldg(p.row_ids + rbase + r) : -1;
+            }
             // ---- CUDA-core part (overlaps the last block's MMAs) ----
             const bool cpart = sparse || p.rem_nnz;
             bool in_ys = cpart || p.tail_nnz;
             if (in_ys) {
 #pragma unroll
                 for (int r = 0; r < NR; ++r) w.ys[r][wt] = 0.f;
-                if (cpart) cuda_part<NR, PW>(p, w, b, be, rbase, nr, xb, wt, bar);
+                if (cpart) cuda_part<NR, PW>(p, w, b, be, rbase, nrc, xb, wt, bar);
             }
             // ---- the accumulator ----
             float acc[NR];
@@ -723,13 +744,17 @@ __device__ void worker(const TcParams &p, WorkerSmem<NR, PW> &w, Ctl &ctl, uint3
                     for (int r = 0; r < NR; ++r) w.ys[r][wt] = 0.f;
                     in_ys = true;
                 }
-                rare_part<NR, PW>(p, w, b, be, rbase, nr, special, xb, wt);
+                rare_part<NR, PW>(p, w, b, be, rbase, nrc, special, xb, wt);
             }
 #pragma unroll
             for (int r = 0; r < NR; ++r) {
                 const int32_t row = __shfl_sync(kFullMask, myrow[r / 32], r % 32);
                 if (row >= 0) __stcs(yb + (int64_t)row * p.K, in_ys ? w.ys[r][wt] + acc[r] : acc[r]);
             }
+            // A row group with a kept block has at most max_nr <= NR rows; a
+            // larger one (its blocks all spilled, or an empty group under KEEP)
+            // holds only CSR remainder and COO tail entries past row NR.
+            if (nr > NR) large_group_rows<NR, PW>(p, w, b, rbase, nr, xb, yb, wt, bar);
             b = be;
         }
     }
@@ -738,7 +763,7 @@ __device__ void worker(const TcParams &p, WorkerSmem<NR, PW> &w, Ctl &ctl, uint3
 }
 
 template <int NR, int PW, int NW>
-__global__ void __launch_bounds__(TcShape<NR, PW, NW>::kThreads, 1) boo_tc_kernel(const TcParams p) {
+__global__ void __launch_bounds__(TcShape<NR, PW, NW>::kThreads, 1) boo_tc_kernel(const __grid_constant__ TcParams p) {
     using Shape = TcShape<NR, PW, NW>;
     using W = WorkerSmem<NR, PW>;
     extern __shared__ uint8_t smem_raw[];
@@ -827,11 +852,8 @@ int launch_tc(TcParams p, int64_t batch, void *ws, size_t ws_bytes, cudaStream_t
     const int64_t gather_rows = batch * p.n_cg * (PW / 4);
     if (gather_rows > 0x7fffffffLL) return SPMM_EUNSUPPORTED;
     const size_t need = (size_t)gather_rows * (size_t)p.K * sizeof(float4);
-    void *own = nullptr;
-    if (!ws || ws_bytes < need || ((uintptr_t)ws & 15)) {
-        SPMM_CUDA_TRY(cudaMallocAsync(&own, need, s));
-        ws = own;
-    }
+    if (need && (!ws || ws_bytes < need)) return SPMM_EWORKSPACE;
+    if ((uintptr_t)ws & 15) return SPMM_EALIGN;
     p.Xt = (const float4 *)ws;
     p.n_ft = p.K / kFeat;
     // chunks of consecutive row groups, small enough for ~16 tasks per worker
@@ -856,10 +878,6 @@ int launch_tc(TcParams p, int64_t batch, void *ws, size_t ws_bytes, cudaStream_t
         e = cudaGetLastError();
         if (e == cudaSuccess) note_product_launch();
     }
-    if (own) {
-        const cudaError_t f = cudaFreeAsync(own, s);
-        if (e == cudaSuccess) e = f;
-    }
     return e == cudaSuccess ? SPMM_OK : SPMM_ECUDA;
 }
 
@@ -880,11 +898,13 @@ size_t boo_tc_workspace(const spmm_boo_dev *A, int64_t batch, int64_t K) {
 }
 
 // Tensor-core BOO product; SPMM_EUNSUPPORTED when the matrix or K does not
-// fit the kernel (caller falls back to CUDA cores).  `ws` (16-byte aligned,
-// boo_tc_workspace() bytes) may be null: the gather buffer is then taken from
-// the stream-ordered allocator and released after the launch.
+// fit the kernel (caller falls back to CUDA cores).  `ws`: the caller's
+// scratch, 16-byte aligned, boo_tc_workspace() bytes (SPMM_EWORKSPACE when
+// short).  `status`: the call's status word (null: the process-wide
+// g_tc_status); `wait_us` > 0 bounds the abortable waits to about that many
+// microseconds instead of ~2 s.
 int boo_matmul_tc(const spmm_boo_dev *A, const float *X, float *Y, int64_t batch, int64_t K, void *ws,
-                  size_t ws_bytes, cudaStream_t s) {
+                  size_t ws_bytes, int32_t *status, int32_t wait_us, cudaStream_t s) {
     if (!tc_applicable(A, K)) return SPMM_EUNSUPPORTED;
     if ((uintptr_t)X & 15) return SPMM_EUNSUPPORTED;  // 16-byte X loads
     if (!A->col_grp_ptr || !A->col_ids) return SPMM_EINVAL;
@@ -916,6 +936,14 @@ int boo_matmul_tc(const spmm_boo_dev *A, const float *X, float *Y, int64_t batch
     p.Y = Y;
     p.n_cg = A->n_cg;
     p.dense_nnz = kDenseNnz;
+    if (status) {
+        p.status = status;
+    } else {
+        void *g = nullptr;
+        SPMM_CUDA_TRY(cudaGetSymbolAddress(&g, g_tc_status));
+        p.status = (int *)g;
+    }
+    p.wait_cycles = wait_us > 0 ? (long long)wait_us * 2000 : kWaitCycles;   // ~2 GHz SM clock
     if (A->max_nr <= 32 && A->max_nc <= 32) return launch_tc<32, 32, 4>(p, batch, ws, ws_bytes, s);
     return launch_tc<64, 64, 2>(p, batch, ws, ws_bytes, s);
 }

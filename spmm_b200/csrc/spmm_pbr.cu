@@ -201,12 +201,15 @@ using namespace spmm;
 extern "C" int spmm_pbr_matmul(const spmm_pbr_dev *A, const void *X, void *Y, int64_t batch, int64_t K,
                                const spmm_launch_cfg *cfg, spmm_stream_t stream) {
     if (!A || batch < 0 || K < 0) return SPMM_EINVAL;
-    if (cfg && cfg->version != 1) return SPMM_EINVAL;
+    if (cfg && cfg->version != 1 && cfg->version != 2) return SPMM_EINVAL;
     if (A->scalar_type != SPMM_F32 && A->scalar_type != SPMM_F64) return SPMM_EINVAL;
     if (A->index_type != SPMM_INDEX_I32 && A->index_type != SPMM_INDEX_I64) return SPMM_EINVAL;
     if (A->rows < 0 || A->cols < 0 || A->nb < 0) return SPMM_EINVAL;
     if (A->block_rows <= 0 || A->block_cols <= 0 || A->block_rows * A->block_cols > 64)
         return SPMM_EINVAL;
+    // no bounded waits in the PBR kernel: its status word (if any) ends at 0
+    if (cfg && cfg->version >= 2 && cfg->status)
+        if (cudaMemsetAsync(cfg->status, 0, sizeof(int32_t), (cudaStream_t)stream) != cudaSuccess) return SPMM_ECUDA;
     if (batch == 0 || K == 0 || A->rows == 0) return SPMM_OK;
     if (!Y || (A->cols && !X) || !A->rem_indptr) return SPMM_EINVAL;
     if (A->nb && (!A->codes || !A->coords || !A->offsets || !A->data)) return SPMM_EINVAL;

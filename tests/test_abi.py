@@ -38,14 +38,27 @@ def test_library_exports_every_declared_symbol():
 
 def test_host_only_entry_points():
     L = _lib.lib()
-    assert L.spmm_abi_version() == 1
+    assert L.spmm_abi_version() == 2
     assert 'uint16' in _lib.status_string(_lib.SPMM_EOVERFLOW_U16)
+    assert 'wait expired' in _lib.status_string(_lib.SPMM_ETIMEOUT)
+    assert 'collective' in _lib.status_string(_lib.SPMM_ENCCL)
+    assert L.spmm_hem_level_slots(32) == 8 * 5 + 16 + 1
+    assert L.spmm_hem_level_slots(1) == 8 + 16 + 1
     assert _lib.status_string(12345) == 'unknown status'
     for fn in (L.spmm_boo_build_workspace_size, L.spmm_pbr_build_workspace_size):
         small = fn(10, 10, 10)
         big = fn(1000, 1000, 100000)
         assert 0 < small < big
         assert fn(-1, 0, 0) == 0
+
+
+def test_launch_cfg_layout():
+    """spmm_launch_cfg as the header lays it out (64-bit): version 2 adds the
+    status word after the workspace."""
+    assert C.sizeof(_lib.LaunchCfg) == 40
+    assert _lib.LaunchCfg.status.offset == 32 and _lib.LaunchCfg.workspace.offset == 16
+    cfg = _lib.launch_cfg('tensor_cores', wait_us=5)
+    assert (cfg.version, cfg.engine, cfg.wait_us, cfg.status) == (2, 2, 5, None)
 
 
 def test_null_arguments_are_rejected_without_touching_a_gpu():

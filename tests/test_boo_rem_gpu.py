@@ -39,8 +39,9 @@ def _check(mat, boo, x, slabs=(0,)):
         assert torch.equal(got, S.boo_matmul(dev, xd, slab_features=slab))   # deterministic
 
 
-# slab_features: auto, full width, and each narrow slab width of the dtype
-SLABS = {np.float32: (0, -1, 8, 16, 32), np.float64: (0, -1, 4, 8, 16)}
+# slab_features: the nnz-flat chunks (0, and positive values, taken as 0) and
+# the register path (< 0)
+SLABS = {np.float32: (0, -1, 16), np.float64: (0, -1, 8)}
 
 
 @pytest.mark.parametrize('dtype', [np.float32, np.float64])
@@ -121,10 +122,11 @@ def test_remainder_flat_chunk_boundaries(cuda):
         _check(mat, boo, x, (0, -1))
 
 
-def test_remainder_flat_abi_workspace_optional(cuda):
-    """Through the C ABI: the nnz-flat remainder's scratch from the caller or
-    from the stream-ordered allocator gives the same bits; the register path
-    (slab_features < 0) needs none."""
+def test_remainder_flat_abi_workspace_required(cuda):
+    """Through the C ABI: the nnz-flat remainder runs on the caller's scratch
+    and the library allocates none -- without it the call returns
+    SPMM_EWORKSPACE; the register path (slab_features < 0) needs none and gives
+    results within tolerance of the nnz-flat path."""
     import ctypes as C
     from spmm_b200 import _lib
     from spmm_b200._device import stream_handle
@@ -134,19 +136,22 @@ def test_remainder_flat_abi_workspace_optional(cuda):
     x = torch.randn(2, 4000, 192, generator=torch.Generator().manual_seed(4)).cuda()
     L = _lib.lib()
     out = []
-    for with_ws in (False, True):
-        cfg = _lib.launch_cfg('auto')
+    for slab in (0, -1):
+        cfg = _lib.launch_cfg('auto', slab_features=slab)
         ws_bytes = L.spmm_boo_matmul_workspace_size(C.byref(st), 2, 192, C.byref(cfg))
-        assert ws_bytes > 0
-        ws = torch.empty(ws_bytes, dtype=torch.uint8, device='cuda') if with_ws else None
-        if ws is not None:
-            cfg.workspace, cfg.workspace_bytes = ws.data_ptr(), ws_bytes
+        assert (ws_bytes > 0) == (slab == 0)
         y = torch.empty(2, 1500, 192, device='cuda')
-        rc = L.spmm_boo_matmul(C.byref(st), C.c_void_p(x.data_ptr()), C.c_void_p(y.data_ptr()), 2, 192,
-                               C.byref(cfg), stream_handle(x.device))
-        assert rc == 0
+        args = (C.byref(st), C.c_void_p(x.data_ptr()), C.c_void_p(y.data_ptr()), 2, 192, C.byref(cfg),
+                stream_handle(x.device))
+        if ws_bytes:
+            assert L.spmm_boo_matmul(*args) == _lib.SPMM_EWORKSPACE
+            ws = torch.empty(ws_bytes, dtype=torch.uint8, device='cuda')
+            cfg.workspace, cfg.workspace_bytes = ws.data_ptr(), ws_bytes - 1   # too short
+            assert L.spmm_boo_matmul(*args) == _lib.SPMM_EWORKSPACE
+            cfg.workspace_bytes = ws_bytes
+        assert L.spmm_boo_matmul(*args) == 0
         torch.cuda.synchronize()
         out.append(y)
-    assert torch.equal(out[0], out[1])
-    reg = _lib.launch_cfg('auto', slab_features=-1)
-    assert L.spmm_boo_matmul_workspace_size(C.byref(st), 2, 192, C.byref(reg)) == 0
+    xn = x.cpu().numpy()
+    bound = abs_bound(mat.indptr, mat.indices, mat.data, xn)
+    assert_spmm_close(out[0].cpu().numpy(), out[1].cpu().numpy(), bound, 2 * TOL[np.dtype(np.float32)])

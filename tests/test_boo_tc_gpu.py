@@ -173,9 +173,10 @@ def test_tc_not_applicable(cuda):
         S.boo_matmul(boo32.to('cuda'), x, engine='tensor')
 
 
-def test_tc_abi_workspace_optional(cuda):
-    """Through the C ABI: no workspace (scratch from the stream-ordered
-    allocator) and a caller workspace give the same bits."""
+def test_tc_abi_workspace_required(cuda):
+    """Through the C ABI: the tensor-core product's scratch (X gathered by
+    column group) comes from the caller -- none or too little gives
+    SPMM_EWORKSPACE and launches nothing -- and two calls give the same bits."""
     import ctypes as C
     from spmm_b200._device import stream_handle
     mat = workloads.fem3d(n=8)
@@ -183,24 +184,59 @@ def test_tc_abi_workspace_optional(cuda):
     st = boo._dev_struct(boo._gpu_meta)
     x = torch.randn(mat.shape[1], 256, generator=torch.Generator().manual_seed(9)).cuda()
     L = _lib.lib()
+    cfg = _lib.launch_cfg('tensor_cores')
+    ws_bytes = L.spmm_boo_matmul_workspace_size(C.byref(st), 1, 256, C.byref(cfg))
+    assert ws_bytes == boo.num_col_groups() * 32 * 256 * 4
+    y = torch.empty(mat.shape[0], 256, device='cuda')
+    args = (C.byref(st), C.c_void_p(x.data_ptr()), C.c_void_p(y.data_ptr()), 1, 256, C.byref(cfg),
+            stream_handle(x.device))
+    n0 = L.spmm_product_launches()
+    assert L.spmm_boo_matmul(*args) == _lib.SPMM_EWORKSPACE
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device='cuda')
+    cfg.workspace, cfg.workspace_bytes = ws.data_ptr(), ws_bytes - 16
+    assert L.spmm_boo_matmul(*args) == _lib.SPMM_EWORKSPACE
+    assert L.spmm_product_launches() == n0
+    cfg.workspace_bytes = ws_bytes
     out = []
-    for with_ws in (False, True):
-        cfg = _lib.launch_cfg('tensor_cores')
-        ws_bytes = L.spmm_boo_matmul_workspace_size(C.byref(st), 1, 256, C.byref(cfg))
-        assert ws_bytes == boo.num_col_groups() * 32 * 256 * 4
-        ws = torch.empty(ws_bytes, dtype=torch.uint8, device='cuda') if with_ws else None
-        if ws is not None:
-            cfg.workspace, cfg.workspace_bytes = ws.data_ptr(), ws_bytes
-        y = torch.empty(mat.shape[0], 256, device='cuda')
-        rc = L.spmm_boo_matmul(C.byref(st), C.c_void_p(x.data_ptr()), C.c_void_p(y.data_ptr()), 1, 256,
-                               C.byref(cfg), stream_handle(x.device))
-        assert rc == 0
+    for _ in range(2):
+        assert L.spmm_boo_matmul(*args) == 0
         torch.cuda.synchronize()
-        out.append(y)
+        out.append(y.clone())
     assert L.spmm_tc_status(1) == 0
     assert torch.equal(out[0], out[1])
     cc = _lib.launch_cfg('cuda_cores')
     assert L.spmm_boo_matmul_workspace_size(C.byref(st), 1, 256, C.byref(cc)) == 0
+
+
+def test_tc_status_per_call(cuda):
+    """Two products in flight on two streams each report into their own status
+    word: one whose waits are bounded to a microsecond gives up at its first
+    wait that is not already complete (SPMM_ETIMEOUT, Y incomplete), the other
+    completes (0, Y correct).  The timeout path drains the MMAs it issued and
+    releases tensor memory; the context stays usable afterwards."""
+    mat = workloads.fem3d(n=12)
+    boo = S.csr_to_boo(mat, cluster='identity', target_nr=32, target_nc=32)
+    dev = boo.to('cuda')
+    x = torch.randn(mat.shape[1], 256, generator=torch.Generator().manual_seed(2))
+    xd = x.cuda()
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(s1):
+        y_short = S.boo_matmul(dev, xd, engine='tensor_cores', wait_us=1)
+    with torch.cuda.stream(s2):
+        y_full = S.boo_matmul(dev, xd, engine='tensor_cores')
+    torch.cuda.synchronize()
+    assert S.product_status(y_short) == _lib.SPMM_ETIMEOUT
+    with pytest.raises(_lib.SpmmError):
+        S.check_product(y_short)
+    assert S.product_status(y_full) == 0
+    ref = _oracle_y(boo, x.numpy())
+    assert_spmm_close(S.check_product(y_full).cpu().numpy(), ref,
+                      abs_bound(mat.indptr, mat.indices, mat.data, x.numpy()), TOL[np.dtype(np.float32)])
+    assert _lib.lib().spmm_tc_status(1) == 0      # calls with a status word leave the shared one alone
+    again = S.boo_matmul(dev, xd, engine='tensor_cores')
+    assert S.product_status(again) == 0
+    assert torch.equal(again, y_full)
 
 
 @pytest.mark.parametrize('g,n_sparse,rem_rows', [
@@ -239,3 +275,50 @@ def test_tc_cuda_core_segment_lists(cuda, g, n_sparse, rem_rows):
     x = torch.from_numpy(rng.standard_normal((cols, 128)).astype(np.float32))
     _check(mat, boo, x, 'tensor_cores')
     _check(mat, boo, x, 'cuda_cores')
+
+
+@pytest.mark.parametrize('policy', ['remainder', 'tail_batch', 'keep'])
+def test_tc_row_groups_larger_than_blocks(cuda, policy):
+    """max_nr counts only the row groups of kept blocks, so a row group larger
+    than the tensor-core tile (100 rows here, tile 32) passes the engine's
+    check when its blocks all spilled (remainder / tail) or when it holds no
+    nonzeros at all (keep): all of its rows must still be written."""
+    rng = np.random.default_rng(41)
+    sizes = [32, 32, 100, 32, 100, 32]                 # groups 2 and 4 have 100 rows
+    rl = np.repeat(np.arange(len(sizes)), sizes)
+    rows, cols = len(rl), 256
+    dense = np.zeros((rows, cols), np.float32)
+    starts = np.concatenate([[0], np.cumsum(sizes)])
+    for g in (0, 1, 3, 5):                             # dense blocks in the 32-row groups
+        sl = slice(starts[g], starts[g + 1])
+        m = rng.random((sizes[g], cols)) < 0.3
+        dense[sl][m] = rng.standard_normal(int(m.sum()))
+    if policy != 'keep':                               # group 2: one entry per block, spilled
+        for q in range(sizes[2]):
+            dense[starts[2] + q, (q * 37) % cols] = rng.standard_normal()
+    mat = sp.csr_matrix(dense)
+    cl = np.arange(cols) // 32
+    boo = S.csr_to_boo(mat, row_labels=rl, col_labels=cl, small_block_policy=policy,
+                       small_block_threshold=4)
+    assert boo.max_nr == 32
+    x = torch.from_numpy(rng.standard_normal((cols, 128)).astype(np.float32))
+    import ctypes as C
+    from spmm_b200._device import stream_handle
+    dev = boo.to('cuda')
+    st = dev._dev_struct(dev._gpu_meta)
+    xd = x.cuda()
+    y = torch.full((rows, 128), float('nan'), device='cuda')   # stale contents must not survive
+    L = _lib.lib()
+    cfg = _lib.launch_cfg('tensor_cores')
+    ws_bytes = L.spmm_boo_matmul_workspace_size(C.byref(st), 1, 128, C.byref(cfg))
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device='cuda')
+    cfg.workspace, cfg.workspace_bytes = ws.data_ptr(), ws_bytes
+    rc = L.spmm_boo_matmul(C.byref(st), C.c_void_p(xd.data_ptr()), C.c_void_p(y.data_ptr()), 1, 128,
+                           C.byref(cfg), stream_handle(xd.device))
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert L.spmm_tc_status(1) == 0
+    got = y.cpu().numpy()
+    assert np.isfinite(got).all()
+    ref = _oracle_y(boo, x.numpy())
+    assert_spmm_close(got, ref, abs_bound(mat.indptr, mat.indices, mat.data, x.numpy()), TOL[np.dtype(np.float32)])

@@ -1,15 +1,17 @@
-"""HEM labels on the GPU (spmm_hem_labels) against the host restatement of
-the reference's multilevel heavy-edge matching (clustering.py:128-351):
-identical labels level for level's end result, across hub pruning, top-k,
-size / nnz caps, feasible-first filtering, ties and empty rows."""
+"""HEM labels on the GPU (spmm_hem_labels / spmm_hem_hierarchy) against the C
+oracle's restatement of the reference's multilevel heavy-edge matching
+(clustering.py:128-351; oracle/hem_oracle.c, itself pinned to the
+reference's labels by tests/test_clustering.py): identical labels and
+per-level hierarchy across hub pruning, top-k, size / nnz caps,
+feasible-first filtering, ties and empty rows."""
 
 import numpy as np
 import pytest
 import scipy.sparse as sp
 
 from spmm_b200 import workloads
-from spmm_b200._hem import hem_labels
-from spmm_b200.clustering import _pattern, cluster_axes, hem_labels_gpu
+from oracle import oracle as O
+from spmm_b200.clustering import _pattern, cluster_axes, cluster_axis, hem_labels_gpu
 
 pytestmark = pytest.mark.gpu
 
@@ -44,20 +46,32 @@ CASES = _cases()
 ], ids=['default', 'uncapped', 'caps_hub_topk4', 'topk_all'])
 def test_gpu_labels_equal_host(cuda, name, params):
     pat = _pattern(CASES[name])
-    host = hem_labels(pat, params['target'], params['max_size'], params['max_nnz'], params['hub_degree'],
-                      params['topk'], True, feasible_first=params['feasible_first'])
+    host = O.hem_labels(pat, params['target'], params['max_size'], params['max_nnz'], params['hub_degree'],
+                        params['topk'], feasible_first=params['feasible_first'])
     gpu = hem_labels_gpu(pat, params['target'], params['max_size'], params['max_nnz'], params['hub_degree'],
                          params['topk'], params['feasible_first'])
     np.testing.assert_array_equal(gpu, host)
 
 
 def test_cluster_axes_uses_gpu_labels(cuda):
-    """csr_to_boo's clustering (cluster='hem') gives the host restatement's labels."""
+    """csr_to_boo's clustering (cluster='hem') gives the oracle's labels after
+    the same cap enforcement."""
     mat = workloads.powerlaw(n=2000)
     rl, cl = cluster_axes(mat, method='hem', target_nr=32, target_nc=32, max_nr=32, max_nc=32, feasible_first=True)
-    from spmm_b200.clustering import _enforce_caps, _relabel_consecutive
-    pat = _pattern(mat)
-    host = hem_labels(pat, 32, 32, None, 1024, 32, True, feasible_first=True)
-    want = _relabel_consecutive(_enforce_caps(host, np.diff(pat.indptr), 32, None)).astype(np.int32)
+    want = O.hem_cluster(mat, 32, 32, None, feasible_first=True)
     np.testing.assert_array_equal(rl, want)
     np.testing.assert_array_equal(cl, want)        # symmetric pattern: one clustering for both axes
+
+
+@pytest.mark.parametrize('name', ['fem3d', 'powerlaw', 'rect_cols', 'ties', 'tiny'])
+def test_hierarchy_equals_oracle(cuda, name):
+    """hem_hierarchy=[]: identity, then the labels after every level that
+    matched, finest to coarsest, as the reference records them."""
+    pat = _pattern(CASES[name])
+    got = []
+    lab = cluster_axis(CASES[name], method='hem', target=16, max_size=16, hem_hierarchy=got)
+    _, want = O.hem_labels(pat, 16, 16, None, 1024, 32, hierarchy=True)
+    assert len(got) == len(want) >= 1
+    for g, w in zip(got, want):
+        np.testing.assert_array_equal(g, w)
+    np.testing.assert_array_equal(lab, O.hem_cluster(CASES[name], 16, 16, None))

@@ -117,3 +117,67 @@ def test_noalloc_rejects_oversized_problem_without_device_work():
     rc = _lib.lib().spmm_boo_build_noalloc(C.byref(A), 1, 1, 2, 4, 0, C.byref(out), None)
     assert rc == _lib.SPMM_ESCRATCH
     assert 'scratch' in _lib.status_string(rc)
+
+
+def _nnz_limit(rows, cols):
+    """Largest nnz whose builder workspace fits the 32 MiB scratch."""
+    L = _lib.lib()
+    lo, hi = 0, rows * cols
+    while lo < hi:
+        mid = (lo + hi + 1) // 2
+        if L.spmm_boo_build_workspace_size(rows, cols, mid) <= 32 << 20:
+            lo = mid
+        else:
+            hi = mid - 1
+    return lo
+
+
+def _exact_nnz(seed, rows, cols, nnz):
+    rng = np.random.default_rng(seed)
+    keys = np.sort(rng.choice(rows * cols, nnz, replace=False))
+    r, c = keys // cols, keys % cols
+    indptr = np.zeros(rows + 1, dtype=np.int64)
+    np.cumsum(np.bincount(r, minlength=rows), out=indptr[1:])
+    mat = sp.csr_matrix((rng.standard_normal(nnz).astype(np.float32), c, indptr), shape=(rows, cols))
+    return mat, rng.integers(0, rows // 32, rows).astype(np.int32), (np.arange(cols) // 32).astype(np.int32)
+
+
+def _assert_same_as_workspace_build(mat, rl, cl, rc, out, bufs):
+    assert rc == _lib.SPMM_OK, _lib.status_string(rc)
+    ref = S.csr_to_boo(mat, row_labels=rl, col_labels=cl)
+    assert int(out.nb) == ref.num_blocks() and int(out.rem_nnz) == ref.remainder_nnz()
+    sizes = _sizes(out)
+    for f in FIELDS:
+        got = bufs[f][:sizes[f]].cpu().numpy()
+        want = ref._dev.__dict__[f].cpu().numpy()
+        assert got.shape == want.shape and np.array_equal(got, want), f
+
+
+def test_noalloc_at_the_scratch_limit():
+    """The largest problem whose workspace fits 32 MiB builds correctly; one
+    more nonzero is rejected with SPMM_ESCRATCH before any device work."""
+    if not torch.cuda.is_available():
+        pytest.fail('CUDA device required for gpu-marked tests')
+    L = _lib.lib()
+    rows = cols = 40000
+    nmax = _nnz_limit(rows, cols)
+    assert L.spmm_boo_build_workspace_size(rows, cols, nmax) <= 32 << 20 < \
+        L.spmm_boo_build_workspace_size(rows, cols, nmax + 1)
+    mat, rl, cl = _exact_nnz(5, rows, cols, nmax)
+    _assert_same_as_workspace_build(mat, rl, cl, *_noalloc_build(mat, rl, cl, 2, 4, 0))
+    over, rl2, cl2 = _exact_nnz(6, rows, cols, nmax + 1)
+    rc, _, _ = _noalloc_build(over, rl2, cl2, 2, 4, 0)
+    assert rc == _lib.SPMM_ESCRATCH
+
+
+def test_noalloc_after_a_failed_call():
+    """A call that fails inside the build (a row label out of range) leaves
+    the shared scratch in a state the next valid call does not depend on."""
+    if not torch.cuda.is_available():
+        pytest.fail('CUDA device required for gpu-marked tests')
+    mat, rl, cl = _problem(21, 1200, 900, 0.03, np.float32)
+    bad = rl.copy()
+    bad[17] = mat.shape[0]                      # labels must lie in [0, rows)
+    rc, _, _ = _noalloc_build(mat, bad, cl, 2, 4, 0)
+    assert rc == _lib.SPMM_ELABEL
+    _assert_same_as_workspace_build(mat, rl, cl, *_noalloc_build(mat, rl, cl, 2, 4, 0))
