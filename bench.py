@@ -1,25 +1,33 @@
 """Benchmark: SpMM effective GFLOP/s (2*nnz*K/t) and % of the HBM roofline.
 
-Default workload (N=1 line): BASELINE config 2 -- 3-D FEM hex mesh, 64^3 nodes x
-3 DOF (786,432 rows, 61,731,000 nonzeros), BOO with identity grouping at
-target 32x32, X [786432, 128] fp32 ~ N(0,1); synthetic, seeded.  One step = one
-Y = A*X over the whole matrix with A, X and Y resident in HBM (1.18 GB, far
-larger than the 126 MB L2, so no flush is needed between steps).  A workload
-smaller than twice the L2 (C1) is timed step by step instead, with the L2
-flushed (an untimed write of twice its size) before every step; the
-cuSPARSE reference point follows the same rule.
+Headline (the line's `value`, N=1): BASELINE config 2 -- 3-D FEM hex mesh, 64^3
+nodes x 3 DOF (786,432 rows, 61,731,000 nonzeros), BOO with identity grouping
+at target 32x32, X [786432, 128] fp32 ~ N(0,1); synthetic, seeded.  One step =
+one Y = A*X over the whole matrix through the C ABI with A, X and Y resident
+in HBM (1.19 GB, far larger than the 126 MB L2, so no flush between steps).
+`e2e` is the same product through the public Python API with host X and Y
+(pinned H2D and D2H inside the timing).
+
+At N=1 the line also carries `per_config`: every BASELINE configuration on
+its own matrix -- C1; C2 as PBR; C3 with HEM grouping (as the config names
+it) and with identity grouping; C4 on the tensor cores and on CUDA cores; C5
+as PBR and as BOO -- each with its device time, roofline fraction, the best
+cuSPARSE CSR algorithm (cusparseSpMM with a persistent plan) and the
+reference's CPU path on a bounded sample.  A workload smaller than twice the
+L2 (C1) is timed step by step with the L2 flushed before every step; the
+cuSPARSE point follows the same rule.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
-                  [--config c2_fem3d] [--format boo|pbr]
+                  [--config c2_fem3d] [--format boo|pbr] [--no-per-config]
 
 Multi-GPU (torchrun, one process per GPU), two partitionings:
   --split features (default): A is built once on rank 0 and broadcast over
     NCCL (outside timing); every rank multiplies its own 128-column slab of X
     / Y, so the timed region has no collective (weak scaling: total K = N*128).
-  --split rows: row groups partitioned by nonzero balance; every rank builds
-    the format of its own rows; X is broadcast once (timed separately, in
-    `x_broadcast_ms`); Y shards stay local.  Weak scaling (rows = N * rows of
-    the config) for generators with a linear size, else strong scaling.
+  --split rows: BOO row groups or PBR stripes partitioned by nonzero balance;
+    every rank builds the format of its own rows; X is broadcast once (timed
+    separately, in `x_broadcast_ms`); Y shards stay local.  Weak scaling
+    (rows = N * rows of the config) for generators with a linear size.
 The time is the max over ranks of the device-measured duration.
 
 ``--impl reference`` times the reference's own CPU implementation
@@ -68,10 +76,14 @@ def parse():
     ap.add_argument('--grouping', choices=('identity', 'hem'), default='identity',
                     help="BOO row / column grouping (cluster='hem' runs the GPU HEM labels; build time only)")
     ap.add_argument('--slab-features', type=int, default=0,
-                    help='features per pass of the remainder kernels (spmm_launch_cfg.slab_features; '
-                         '0 = auto, <0 = full width)')
+                    help='remainder kernels of remainder-major BOO products (spmm_launch_cfg.slab_features: '
+                         '0 = nnz-flat chunks, <0 = register path)')
     ap.add_argument('--split', choices=('features', 'rows'), default='features',
                     help='multi-GPU partitioning (ignored at --gpus 1)')
+    ap.add_argument('--no-per-config', action='store_true',
+                    help='skip the per-config table (N=1: every BASELINE config on its own matrix)')
+    ap.add_argument('--per-config', default=None,
+                    help='comma-separated labels of the per-config table to run (default: all)')
     return ap.parse_args()
 
 
@@ -382,16 +394,254 @@ def load_peaks():
     return 6650.0, 'fallback'
 
 
+def csrc_sha16() -> str:
+    """Hash of the CUDA sources the library is built from (spmm_b200/csrc)."""
+    import hashlib
+    h = hashlib.sha256()
+    d = os.path.join(ROOT, 'spmm_b200', 'csrc')
+    for f in sorted(os.listdir(d)):
+        if f.endswith(('.cu', '.cuh')):
+            h.update(f.encode())
+            h.update(open(os.path.join(d, f), 'rb').read())
+    return h.hexdigest()[:16]
+
+
 def load_traffic(kernel_tag):
-    """DRAM bytes per launch from the committed ncu summary of this workload."""
+    """DRAM bytes per call of this workload's product from profiles/traffic.json
+    (ncu dram__bytes_read.sum + dram__bytes_write.sum of the call's kernels),
+    with the source hash they were measured on; `stale` when the CUDA sources
+    changed since."""
     path = os.path.join(PROFILES, 'traffic.json')
     if not os.path.exists(path):
         return None
     try:
-        d = json.load(open(path))
-        return d.get(kernel_tag)
+        rec = json.load(open(path)).get(kernel_tag)
     except (OSError, ValueError):
         return None
+    if not isinstance(rec, dict):
+        return None
+    out = dict(rec)
+    out['stale'] = rec.get('csrc_sha16') != csrc_sha16()
+    return out
+
+
+# ---------------------------------------------------------------------------
+# native arm
+# ---------------------------------------------------------------------------
+
+class Timer:
+    """CUDA-event timing of steps on one stream.  A workload whose compulsory
+    bytes fit in twice the L2 is timed step by step with the L2 flushed
+    (an untimed write of twice its size) before every step; larger ones as
+    one run of steps."""
+
+    def __init__(self, torch, dev, stream, alg_bytes):
+        self.torch, self.dev, self.stream = torch, dev, stream
+        l2 = int(getattr(torch.cuda.get_device_properties(dev), 'L2_cache_size', 0) or (126 << 20))
+        self.l2 = l2
+        self.flush = torch.empty(2 * l2, dtype=torch.uint8, device=dev) if alg_bytes < 2 * l2 else None
+
+    def l2_note(self, alg):
+        if self.flush is None:
+            return 'inputs larger than L2 (A+X+Y = %.2f GB), no flush' % (alg / 1e9)
+        return ('L2 flushed before every step (%d MB write, untimed; per-step CUDA events), A+X+Y = %.3f GB'
+                % ((2 * self.l2) >> 20, alg / 1e9))
+
+    def warm(self, n, fn):
+        for _ in range(max(n, 3)):
+            if self.flush is not None:
+                self.flush.zero_()
+            fn()
+        self.torch.cuda.synchronize(self.dev)
+
+    def run(self, n, fn):
+        """ms of n steps of fn."""
+        torch = self.torch
+        with torch.cuda.stream(self.stream):
+            if self.flush is None:
+                a = torch.cuda.Event(enable_timing=True)
+                b = torch.cuda.Event(enable_timing=True)
+                a.record(self.stream)
+                for _ in range(n):
+                    fn()
+                b.record(self.stream)
+                torch.cuda.synchronize(self.dev)
+                return a.elapsed_time(b)
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(n)]
+            for a, b in evs:
+                self.flush.zero_()
+                a.record(self.stream)
+                fn()
+                b.record(self.stream)
+            torch.cuda.synchronize(self.dev)
+            return sum(a.elapsed_time(b) for a, b in evs)
+
+
+def runs_on_tensor_cores(A, K, engine):
+    """True when the BOO product runs on the tensor cores for these settings
+    (spmm_boo_matmul's engine choice)."""
+    s = A._sizes
+    if A._scalar_dtype != np.float32 or engine == 'cuda_cores' or K % 128 or s['nb'] == 0:
+        return False
+    if s['max_nr'] > 64 or s['max_nc'] > 64:
+        return False
+    return engine == 'tensor_cores' or s['nnz_c'] >= 96 * s['nb']
+
+
+def product_launcher(A, fmt, x, y, engine, slab_features=0):
+    """(launch(), check(), workspace bytes, engine tag) of one C-ABI product
+    call on the current stream; workspace and status word allocated once."""
+    import torch
+    from spmm_b200 import _lib
+    L = _lib.lib()
+    st = A._dev_struct(A._gpu_meta)
+    fn = L.spmm_boo_matmul if fmt == 'boo' else L.spmm_pbr_matmul
+    K = x.shape[-1]
+    cfg = _lib.launch_cfg(engine, slab_features=slab_features)
+    ws_bytes = L.spmm_boo_matmul_workspace_size(C.byref(st), 1, K, C.byref(cfg)) if fmt == 'boo' else 0
+    off = ((ws_bytes + 255) // 256) * 256
+    buf = torch.empty(off + 256, dtype=torch.uint8, device=x.device)
+    status = buf[off:off + 4].view(torch.int32)
+    cfg.status = status.data_ptr()
+    if ws_bytes:
+        cfg.workspace, cfg.workspace_bytes = buf.data_ptr(), ws_bytes
+    sh = torch.cuda.current_stream(x.device).cuda_stream
+
+    def launch():
+        rc = fn(C.byref(st), x.data_ptr(), y.data_ptr(), 1, K, C.byref(cfg), sh)
+        if rc:
+            raise _lib.SpmmError(rc, 'bench')
+
+    def check():
+        v = int(status.item())
+        if v:
+            raise _lib.SpmmError(v, 'bench (device status)')
+
+    s = A._sizes
+    if fmt == 'pbr':
+        tag = 'pbr'
+    elif runs_on_tensor_cores(A, K, engine):
+        tag = 'tc'
+    elif s['rem_nnz'] > 0 and 2 * s['rem_nnz'] >= s['total_nnz']:
+        tag = 'rem'
+    else:
+        tag = 'cc'
+    launch.keep = (buf, cfg, st)
+    return launch, check, ws_bytes, tag
+
+
+KERNELS = {'tc': 'boo_gather_kernel + boo_tc_kernel (one spmm_boo_matmul call)',
+           'cc': 'boo_spmm_kernel',
+           'rem': 'rem_flat_plan_kernel + rem_flat_kernel + rem_flat_fix_kernel + boo_spmm_kernel '
+                  '(one spmm_boo_matmul call)',
+           'pbr': 'pbr_spmm_kernel'}
+
+
+def cusparse_best(mat, x, timer, steps):
+    """cusparseSpMM on the same CSR and X through DirectSpMM (persistent
+    descriptors, workspace, preprocessing) for every CSR algorithm; the best
+    one is the reference point (the reference's bindings_cusparse.cu:66-69)."""
+    import torch
+    from spmm_b200.timed import DirectSpMM
+    dev = x.device
+    crow = torch.from_numpy(mat.indptr.astype(np.int32)).to(dev)
+    col = torch.from_numpy(mat.indices.astype(np.int32)).to(dev)
+    val = torch.from_numpy(mat.data.astype(np.float32)).to(dev)
+    per = {}
+    for alg in ('DEFAULT', 'CSR_ALG1', 'CSR_ALG2', 'CSR_ALG3'):
+        try:
+            d = DirectSpMM(crow, col, val, x, alg)
+            if not d.supported:
+                per[alg] = None
+                continue
+            timer.warm(3, d.run)
+            nrep = max(5, min(steps, 30))
+            per[alg] = round(timer.run(nrep, d.run) / nrep, 5)
+            del d
+        except Exception as e:   # noqa: BLE001 -- reported, not fatal
+            per[alg] = f'{type(e).__name__}: {e}'[:120]
+    ok = {k: v for k, v in per.items() if isinstance(v, float)}
+    del crow, col, val
+    torch.cuda.empty_cache()
+    if not ok:
+        return {'unavailable': 'no cusparseSpMM CSR algorithm ran', 'per_alg_ms': per}
+    best = min(ok, key=ok.get)
+    return {'best_alg': best, 'ms_per_step': ok[best], 'per_alg_ms': per,
+            'what': 'cusparseSpMM CSR (DirectSpMM: persistent plan), best of DEFAULT / ALG1 / ALG2 / ALG3'}
+
+
+def measure_config(name, fmt, grouping, engine, args, dev, want_cpu=True, want_cusparse=True):
+    """One per-config entry: the product's device time and roofline on its
+    own matrix, the best cuSPARSE algorithm and the reference CPU path."""
+    import torch
+    import spmm_b200 as S
+    from spmm_b200 import workloads as W
+    cfg = W.CONFIGS[name]
+    mat = cfg['gen'](**cfg['kw'])
+    K = cfg['K']
+    t0 = time.perf_counter()
+    if fmt == 'boo':
+        A = S.csr_to_boo(mat, cluster=grouping, target_nr=cfg['target'], target_nc=cfg['target'])
+    else:
+        A = S.csr_to_pbr(mat, 8, 8, 4)
+    A.to(dev)
+    torch.cuda.synchronize(dev)
+    build_s = time.perf_counter() - t0
+    x = W.dense_x(mat.shape[1], K, seed=0).to(dev)
+    y = torch.empty((mat.shape[0], K), dtype=torch.float32, device=dev)
+    launch, check, _, tag = product_launcher(A, fmt, x, y, engine)
+    abytes, xbytes, ybytes = (format_bytes_boo if fmt == 'boo' else format_bytes_pbr)(A, K)
+    alg = abytes + xbytes + ybytes
+    stream = torch.cuda.current_stream(dev)
+    timer = Timer(torch, dev, stream, alg)
+    timer.warm(args.warmup, launch)
+    steps = max(5, min(args.steps, 50))
+    ms = timer.run(steps, launch) / steps
+    check()
+    peak, peak_kind = load_peaks()
+    flops = 2.0 * mat.nnz * K
+    achieved = alg / (ms * 1e-3) / 1e9
+    traffic = load_traffic(f'{name}:{fmt}:{grouping or "8x8"}:{tag}')
+    entry = {'format': fmt, 'grouping': grouping if fmt == 'boo' else '8x8 bitset blocks',
+             'engine': tag, 'kernel': KERNELS[tag], 'rows': int(mat.shape[0]), 'nnz': int(mat.nnz), 'K': K,
+             'ms_per_step': round(ms, 5), 'value': round(flops / (ms * 1e-3) / 1e9, 2), 'unit': 'GFLOP/s',
+             'roofline': {'bound': 'hbm', 'alg_bytes_per_launch': int(alg), 'achieved': round(achieved, 1),
+                          'peak': peak, 'unit': 'GB/s', 'frac': round(achieved / peak, 4),
+                          'peak_kind': peak_kind, 'traffic': traffic['bytes'] if traffic else None,
+                          'traffic_source': traffic},
+             'build_s': round(build_s, 3), 'l2': timer.l2_note(alg)}
+    del y, launch
+    if want_cusparse:
+        cu = cusparse_best(mat, x, timer, args.steps)
+        if 'ms_per_step' in cu:
+            cu['value'] = round(flops / (cu['ms_per_step'] * 1e-3) / 1e9, 2)
+            entry['vs_cusparse'] = round(cu['ms_per_step'] / ms, 3)
+        entry['cusparse'] = cu
+    if want_cpu:
+        try:
+            cpu = cpu_baseline(mat, cfg, x.cpu().numpy(), fmt, budget_s=3.0)
+            entry['cpu_reference'] = {k: v for k, v in cpu.items() if not k.startswith('build')}
+        except Exception as e:   # noqa: BLE001 -- reported, not fatal
+            entry['cpu_reference'] = {'unavailable': f'{type(e).__name__}: {e}'[:200]}
+    del A, x, timer
+    torch.cuda.empty_cache()
+    return entry
+
+
+# the per-config table: (config, format, grouping, engine, label); C3 as the
+# config names it (HEM grouping) and with identity grouping, C2 and C5 in
+# both formats the configs name, C4 on both engines the config compares
+PER_CONFIG = [
+    ('c1_laplacian2d', 'boo', 'identity', 'auto', 'c1_laplacian2d'),
+    ('c2_fem3d', 'pbr', None, 'auto', 'c2_fem3d_pbr'),
+    ('c3_powerlaw', 'boo', 'hem', 'auto', 'c3_powerlaw'),
+    ('c3_powerlaw', 'boo', 'identity', 'auto', 'c3_powerlaw_identity'),
+    ('c4_blockdiag', 'boo', 'identity', 'auto', 'c4_blockdiag'),
+    ('c4_blockdiag', 'boo', 'identity', 'cuda_cores', 'c4_blockdiag_cuda_cores'),
+    ('c5_uniform', 'pbr', None, 'auto', 'c5_uniform'),
+    ('c5_uniform', 'boo', 'identity', 'auto', 'c5_uniform_boo'),
+]
 
 
 def native_arm(args):
@@ -421,40 +671,39 @@ def native_arm(args):
         gen_kw = json.dumps(kw0)
     mat, cfg = make_matrix(args.config, gen_kw)
     fmt = args.format or cfg['fmt']
-    if split == 'rows' and fmt != 'boo':
-        raise SystemExit('--split rows is implemented for the BOO format')
+    grouping = args.grouping if fmt == 'boo' else '8x8'
     K = cfg['K']
     x_bcast_ms = None
     t0 = time.perf_counter()
     if split == 'rows':
         rows_all, cols_all = mat.shape
-        rs = D.RowSplitBOO(mat, np.arange(rows_all) // cfg['target'], np.arange(cols_all) // cfg['target'],
-                           dev)
-        A = rs.boo
+        if fmt == 'boo':
+            rs = D.RowSplitBOO(mat, np.arange(rows_all) // cfg['target'], np.arange(cols_all) // cfg['target'],
+                               dev)
+            A = rs.boo
+        else:
+            rs = D.RowSplitPBR(mat, 8, 8, 4, dev)
+            A = rs.pbr
         mat_full, mat = mat, D.shard_csr(mat, rs.shard)      # this rank's rows (global columns)
-    elif fmt == 'boo':
+    else:
         A = None
         if rank == 0:
-            A = S.csr_to_boo(mat, cluster=args.grouping, target_nr=cfg['target'], target_nc=cfg['target'])
+            A = (S.csr_to_boo(mat, cluster=args.grouping, target_nr=cfg['target'], target_nc=cfg['target'])
+                 if fmt == 'boo' else S.csr_to_pbr(mat, 8, 8, 4))
             A.to(dev)
-        if world > 1:
-            A = D.broadcast_boo(A, dev)                  # built once, replicated over NCCL
-    else:
-        A = S.csr_to_pbr(mat, 8, 8, 4)
+        if world > 1:                                    # built once, replicated over NCCL
+            A = D.broadcast_boo(A, dev) if fmt == 'boo' else D.broadcast_pbr(A, dev)
     torch.cuda.synchronize(dev)
     build_s = time.perf_counter() - t0
     A.to(dev)
-    meta = A._gpu_meta
-    st = A._dev_struct(meta)
     L = _lib.lib()
-    fn = L.spmm_boo_matmul if fmt == 'boo' else L.spmm_pbr_matmul
     if split == 'rows':
         # X once into every rank's HBM (timed on its own, not part of the step)
         xs = W.dense_x(mat.shape[1], K, seed=0) if rank == 0 else None
         if xs is not None:
             xs = xs.to(dev)
         torch.cuda.synchronize(dev)
-        dist.barrier()
+        D.barrier()
         b0 = torch.cuda.Event(enable_timing=True)
         b1 = torch.cuda.Event(enable_timing=True)
         b0.record()
@@ -466,51 +715,11 @@ def native_arm(args):
         x = W.dense_x(mat.shape[1], K, seed=rank).to(dev)
     y = torch.empty((mat.shape[0], K), dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream(dev)
-    sh = stream.cuda_stream
-    lcfg = _lib.launch_cfg(args.engine, slab_features=args.slab_features)
-    ws_bytes = L.spmm_boo_matmul_workspace_size(C.byref(st), 1, K, C.byref(lcfg)) if fmt == 'boo' else 0
-    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
-    lcfg.workspace, lcfg.workspace_bytes = ws.data_ptr(), ws_bytes
-
-    def launch():
-        rc = fn(C.byref(st), x.data_ptr(), y.data_ptr(), 1, K, C.byref(lcfg), sh)
-        if rc:
-            raise _lib.SpmmError(rc, 'bench')
-
+    launch, check, ws_bytes, engine = product_launcher(A, fmt, x, y, args.engine, args.slab_features)
     abytes, xbytes, ybytes = (format_bytes_boo if fmt == 'boo' else format_bytes_pbr)(A, K)
     alg = abytes + xbytes + ybytes
-    # a workload that fits in L2 (C1) is timed step by step with L2 flushed
-    # (a write of twice its size, untimed) before every step; larger ones are
-    # timed as one run of steps
-    l2 = int(getattr(torch.cuda.get_device_properties(dev), 'L2_cache_size', 0) or (126 << 20))
-    flush_buf = torch.empty(2 * l2, dtype=torch.uint8, device=dev) if alg < 2 * l2 else None
-
-    def timed_steps(n, fn_step):
-        """ms of n steps of fn_step on `stream`, measured with CUDA events."""
-        if flush_buf is None:
-            a = torch.cuda.Event(enable_timing=True)
-            b = torch.cuda.Event(enable_timing=True)
-            a.record(stream)
-            for _ in range(n):
-                fn_step()
-            b.record(stream)
-            torch.cuda.synchronize(dev)
-            return a.elapsed_time(b)
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-               for _ in range(n)]
-        for a, b in evs:
-            flush_buf.zero_()
-            a.record(stream)
-            fn_step()
-            b.record(stream)
-        torch.cuda.synchronize(dev)
-        return sum(a.elapsed_time(b) for a, b in evs)
-
-    for _ in range(max(args.warmup, 3)):
-        if flush_buf is not None:
-            flush_buf.zero_()
-        launch()
-    torch.cuda.synchronize(dev)
+    timer = Timer(torch, dev, stream, alg)
+    timer.warm(args.warmup, launch)
 
     clocks = None
     sampler = None
@@ -523,16 +732,15 @@ def native_arm(args):
         sampler = ClockSampler(gid)
         sampler.start()
     if world > 1:
-        dist.barrier()
+        D.barrier()
     torch.cuda.synchronize(dev)
     n_launch0 = L.spmm_product_launches()
-    ms = timed_steps(args.steps, launch)
+    ms = timer.run(args.steps, launch)
     gpu_launches = int(L.spmm_product_launches() - n_launch0)   # counted by the library
+    check()
     if world > 1:
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-        dist.barrier()
+        ms = D.all_reduce_max(ms, dev)
+        D.barrier()
     if sampler is not None:
         clocks = sampler.stop()
 
@@ -546,37 +754,16 @@ def native_arm(args):
 
     peak, peak_kind = load_peaks()
     achieved = alg / (ms_step * 1e-3) / 1e9
-    rem_major = fmt == 'boo' and 0 < 2 * A._sizes['rem_nnz'] and 2 * A._sizes['rem_nnz'] >= A._sizes['total_nnz']
-    engine = 'rem' if rem_major else ('tc' if ws_bytes else 'cc')
-    tag = f'{args.config}:{fmt}:{engine}'
-    traffic = load_traffic(tag)
-    kernel_name = {'tc': 'boo_gather_kernel + boo_tc_kernel (one spmm_boo_matmul call)',
-                   'cc': 'boo_spmm_kernel',
-                   'rem': 'rem_flat_plan_kernel + rem_flat_kernel + rem_flat_fix_kernel + boo_spmm_kernel '
-                          '(one spmm_boo_matmul call)',
-                   }[engine] if fmt == 'boo' else 'pbr_spmm_kernel'
+    traffic = (load_traffic(f'{args.config}:{fmt}:{grouping}:{engine}')
+               if not args.gen_kw and split != 'rows' else None)
 
-    # cuSPARSE reference point (benchmark only): torch's CSR x dense product on
-    # the same matrix and X, which runs cusparseSpMM
+    # cuSPARSE reference point (benchmark only): the best CSR algorithm
     cusparse = None
     if world == 1 and not args.no_cusparse:
-        try:
-            At = torch.sparse_csr_tensor(torch.from_numpy(mat.indptr.astype(np.int32)),
-                                         torch.from_numpy(mat.indices.astype(np.int32)),
-                                         torch.from_numpy(mat.data.astype(np.float32)), size=mat.shape,
-                                         device=dev)
-            for _ in range(3):
-                yc = torch.sparse.mm(At, x)
-            torch.cuda.synchronize(dev)
-            nrep = max(5, min(args.steps, 50))
-            cms = timed_steps(nrep, lambda: torch.sparse.mm(At, x)) / nrep   # same L2 rule
-            yc = None
-            cusparse = {'ms_per_step': round(cms, 4), 'value': round(flops_rank / (cms * 1e-3) / 1e9, 3),
-                        'unit': 'GFLOP/s', 'what': 'torch.sparse.mm (cusparseSpMM) on the same CSR, X',
-                        'speedup_of_this': round(cms / ms_step, 3)}
-            del At, yc
-        except Exception as e:   # noqa: BLE001 -- reported, not fatal
-            cusparse = {'unavailable': f'{type(e).__name__}: {e}'[:200]}
+        cusparse = cusparse_best(mat, x, timer, args.steps)
+        if 'ms_per_step' in cusparse:
+            cusparse['value'] = round(flops_rank / (cusparse['ms_per_step'] * 1e-3) / 1e9, 3)
+            cusparse['speedup_of_this'] = round(cusparse['ms_per_step'] / ms_step, 3)
 
     # e2e: the public API with host operands (pinned H2D of X, D2H of Y per step)
     x_host = x.cpu().pin_memory()
@@ -599,13 +786,12 @@ def native_arm(args):
     torch.cuda.synchronize(dev)
     e_s = (time.perf_counter() - e0) / args.e2e_steps
     if world > 1:
-        t = torch.tensor([e_s], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e_s = float(t.item())
+        e_s = D.all_reduce_max(e_s, dev)
     e2e_flops = flops_all if split == 'rows' else world * flops_rank
     e2e = {'value': round(e2e_flops / e_s / 1e9, 3), 'unit': 'GFLOP/s',
            'h2d_bytes_per_step': int(x_host.numel() * 4), 'd2h_bytes_per_step': int(yh.numel() * 4),
            'ms_per_step': round(e_s * 1e3, 3)}
+    del yh
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -631,22 +817,36 @@ def native_arm(args):
                    'nnz': int(mat_full.nnz if split == 'rows' else mat.nnz),
                    'K_per_gpu': K if split != 'rows' else None,
                    'K': K if split == 'rows' else K * world,
-                   'parallelism': (f'row-split x{world} (nnz-balanced row groups, X broadcast once)'
+                   'parallelism': (f'row-split x{world} (nnz-balanced, X broadcast once)'
                                    if split == 'rows' else f'feature-split x{world}'),
                    'x_broadcast_ms': None if x_bcast_ms is None else round(x_bcast_ms, 3),
-                   'l2': ('inputs larger than L2 (A+X+Y = %.2f GB), no flush' % (alg / 1e9)
-                          if flush_buf is None else
-                          'L2 flushed before every step (%d MB write, untimed; per-step CUDA events), '
-                          'A+X+Y = %.3f GB' % ((2 * l2) >> 20, alg / 1e9)),
+                   'l2': timer.l2_note(alg),
                    'build_s': round(build_s, 3)},
         'roofline': {'bound': 'hbm', 'achieved': round(achieved, 1), 'peak': peak,
-                     'unit': 'GB/s', 'frac': round(achieved / peak, 4), 'traffic': traffic,
-                     'peak_kind': peak_kind, 'alg_bytes_per_launch': int(alg),
-                     'kernel': kernel_name},
+                     'unit': 'GB/s', 'frac': round(achieved / peak, 4),
+                     'traffic': traffic['bytes'] if traffic else None,
+                     'traffic_source': traffic, 'peak_kind': peak_kind, 'alg_bytes_per_launch': int(alg),
+                     'kernel': KERNELS[engine]},
         'cusparse': cusparse,
         'e2e': e2e, 'gpu_launches': gpu_launches,
         'clocks': clocks, 'cpu_baseline': cpu, 'build': build,
+        'csrc_sha16': csrc_sha16(),
     }
+    del A, x, y, timer, launch, x_host
+    torch.cuda.empty_cache()
+    if world == 1 and not args.no_per_config:
+        per = {}
+        wanted = set(args.per_config.split(',')) if args.per_config else None
+        for name, pfmt, pgroup, eng, label in PER_CONFIG:
+            if wanted is not None and label not in wanted:
+                continue
+            try:
+                per[label] = measure_config(name, pfmt, pgroup, eng, args, dev,
+                                            want_cpu=not args.no_cpu_baseline, want_cusparse=not args.no_cusparse)
+            except Exception as e:   # noqa: BLE001 -- one config failing does not hide the others
+                per[label] = {'failed': f'{type(e).__name__}: {e}'[:300]}
+                torch.cuda.empty_cache()
+        line['per_config'] = per
     print(json.dumps(line), flush=True)
     return 0
 

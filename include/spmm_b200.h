@@ -152,7 +152,15 @@ typedef struct {
     int32_t *status;        /* version 2, optional: a device int32 the call sets to 0
                              * (stream-ordered) and a kernel sets to SPMM_ETIMEOUT when one
                              * of its bounded waits expired; read it after the stream */
+    int32_t flags;          /* version 2: 0, or SPMM_CFG_EXPIRE_FIRST_WAIT */
+    int32_t reserved;       /* version 2: 0 */
 } spmm_launch_cfg;
+
+/* spmm_launch_cfg::flags.  SPMM_CFG_EXPIRE_FIRST_WAIT (tests of the timeout
+ * path; needs wait_us > 0): every tensor-core worker's first bounded wait is
+ * on a barrier nothing arrives on, so it expires after wait_us, the launch
+ * stops early (Y incomplete) and the status word reads SPMM_ETIMEOUT. */
+enum spmm_cfg_flags { SPMM_CFG_EXPIRE_FIRST_WAIT = 1 };
 
 /* Which units multiply the BOO blocks.  AUTO takes the tensor cores when the
  * matrix is float32, K is a multiple of 128 and every block fits 64 x 64

@@ -72,20 +72,23 @@ class PbrDev(C.Structure):
 class LaunchCfg(C.Structure):
     _fields_ = [('version', C.c_int32), ('slab_features', C.c_int32), ('engine', C.c_int32),
                 ('wait_us', C.c_int32), ('workspace', C.c_void_p), ('workspace_bytes', C.c_uint64),
-                ('status', C.c_void_p)]
+                ('status', C.c_void_p), ('flags', C.c_int32), ('reserved', C.c_int32)]
+
+
+SPMM_CFG_EXPIRE_FIRST_WAIT = 1
 
 
 ENGINES = {'auto': 0, 'cuda_cores': 1, 'tensor_cores': 2}
 
 
 def launch_cfg(engine: str = 'auto', workspace: int = 0, workspace_bytes: int = 0,
-               slab_features: int = 0, status: int = 0, wait_us: int = 0) -> 'LaunchCfg':
+               slab_features: int = 0, status: int = 0, wait_us: int = 0, flags: int = 0) -> 'LaunchCfg':
     """spmm_launch_cfg (version 2): engine, remainder slab setting, workspace
     and the call's device status word (0 / None: none)."""
     if engine not in ENGINES:
         raise ValueError(f"engine must be one of {sorted(ENGINES)}, got {engine!r}")
     return LaunchCfg(2, int(slab_features), ENGINES[engine], int(wait_us), workspace or None, workspace_bytes,
-                     status or None)
+                     status or None, int(flags), 0)
 
 
 class SpmmError(RuntimeError):

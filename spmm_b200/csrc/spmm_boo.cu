@@ -23,7 +23,7 @@
 namespace spmm {
 
 int boo_matmul_tc(const spmm_boo_dev *A, const float *X, float *Y, int64_t batch, int64_t K, void *ws,
-                  size_t ws_bytes, int32_t *status, int32_t wait_us, cudaStream_t s);
+                  size_t ws_bytes, int32_t *status, int32_t wait_us, int32_t flags, cudaStream_t s);
 size_t boo_tc_workspace(const spmm_boo_dev *A, int64_t batch, int64_t K);
 
 namespace {
@@ -943,9 +943,9 @@ int boo_matmul_impl(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch
     const size_t ws_bytes = cfg && ws ? (size_t)cfg->workspace_bytes : 0;
     if constexpr (sizeof(S) == 4) {
         if (tc_selected(A, engine)) {
-            int32_t *status = cfg && cfg->version >= 2 ? cfg->status : nullptr;
-            const int rc = boo_matmul_tc(A, (const float *)X, (float *)Y, batch, K, ws, ws_bytes, status,
-                                         cfg ? cfg->wait_us : 0, s);
+            const bool v2 = cfg && cfg->version >= 2;
+            const int rc = boo_matmul_tc(A, (const float *)X, (float *)Y, batch, K, ws, ws_bytes,
+                                         v2 ? cfg->status : nullptr, cfg ? cfg->wait_us : 0, v2 ? cfg->flags : 0, s);
             if (rc != SPMM_EUNSUPPORTED || engine == SPMM_ENGINE_TENSOR_CORES) return rc;
         }
     } else {
@@ -1012,6 +1012,9 @@ extern "C" int spmm_boo_matmul(const spmm_boo_dev *A, const void *X, void *Y, in
     const int engine = cfg ? cfg->engine : SPMM_ENGINE_AUTO;
     if (engine < SPMM_ENGINE_AUTO || engine > SPMM_ENGINE_TENSOR_CORES) return SPMM_EINVAL;
     if (cfg && cfg->wait_us < 0) return SPMM_EINVAL;
+    if (cfg && cfg->version >= 2 && (cfg->flags & ~SPMM_CFG_EXPIRE_FIRST_WAIT)) return SPMM_EINVAL;
+    if (cfg && cfg->version >= 2 && (cfg->flags & SPMM_CFG_EXPIRE_FIRST_WAIT) && cfg->wait_us <= 0)
+        return SPMM_EINVAL;   // the expiring wait must be short
     if (A->scalar_type != SPMM_F32 && A->scalar_type != SPMM_F64) return SPMM_EINVAL;
     if (A->nz_order != SPMM_BOO_ROWMAJOR && A->nz_order != SPMM_BOO_COLMAJOR) return SPMM_EINVAL;
     if (A->rows < 0 || A->cols < 0 || A->n_rg < 0 || A->nb < 0 || A->tail_nnz < 0) return SPMM_EINVAL;

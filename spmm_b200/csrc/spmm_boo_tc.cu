@@ -94,6 +94,7 @@ struct TcParams {
     int64_t n_cg;
     int *status;          // this launch's status word (the caller's, or g_tc_status)
     long long wait_cycles;  // bound of the abortable waits, in SM clock cycles
+    int32_t expire_probe;   // tests: each worker's first wait is on a barrier nothing completes
 };
 
 // One worker's shared memory.
@@ -113,6 +114,7 @@ struct alignas(1024) WorkerSmem {
     int32_t dk0[kSegs], dk1[kSegs], dcg[kSegs];  // the row group's tensor-core blocks
     uint32_t dshift[kSegs];
     uint64_t mma_bar;               // completes once per MMA commit
+    uint64_t never_bar;             // never arrived on: the timeout test's wait target
     uint32_t kmask[2], aspecial[2];
 };
 
@@ -516,9 +518,16 @@ __device__ void worker(const TcParams &p, WorkerSmem<NR, PW> &w, Ctl &ctl, uint3
     bool ok = true;
 
     // Thread 0 waits, the warpgroup learns the (uniform) outcome at a barrier.
+    // With expire_probe (tests of the timeout path) the first wait is on a
+    // barrier that nothing arrives on, so it expires after wait_cycles.
+    bool probe = p.expire_probe != 0;
     auto wait_commit = [&](uint32_t c) -> bool {
         bool r = true;
-        if (wt == 0) r = wait_phase(&w.mma_bar, c & 1u, abort, p.status, p.wait_cycles);
+        if (wt == 0) {
+            if (probe) r = wait_phase(&w.never_bar, 0u, abort, p.status, p.wait_cycles);
+            if (r) r = wait_phase(&w.mma_bar, c & 1u, abort, p.status, p.wait_cycles);
+        }
+        probe = false;
         return bar_and(bar, 128, r);
     };
     auto prefetch = [&](int i, uint16_t (&ip)[kNzPre], float (&vp)[kNzPre]) {
@@ -773,7 +782,10 @@ __global__ void __launch_bounds__(TcShape<NR, PW, NW>::kThreads, 1) boo_tc_kerne
     const int tid = threadIdx.x, warp = tid >> 5, wk = warp >> 2;
 
     if (tid == 0) {
-        for (int k = 0; k < NW; ++k) mbar_init(&ws[k].mma_bar, 1);
+        for (int k = 0; k < NW; ++k) {
+            mbar_init(&ws[k].mma_bar, 1);
+            mbar_init(&ws[k].never_bar, 1);
+        }
         ctl.abort = 0;
         fence_mbar_init();
     }
@@ -902,9 +914,10 @@ size_t boo_tc_workspace(const spmm_boo_dev *A, int64_t batch, int64_t K) {
 // scratch, 16-byte aligned, boo_tc_workspace() bytes (SPMM_EWORKSPACE when
 // short).  `status`: the call's status word (null: the process-wide
 // g_tc_status); `wait_us` > 0 bounds the abortable waits to about that many
-// microseconds instead of ~2 s.
+// microseconds instead of ~2 s; `flags` & SPMM_CFG_EXPIRE_FIRST_WAIT makes
+// each worker's first wait expire (tests of the timeout path).
 int boo_matmul_tc(const spmm_boo_dev *A, const float *X, float *Y, int64_t batch, int64_t K, void *ws,
-                  size_t ws_bytes, int32_t *status, int32_t wait_us, cudaStream_t s) {
+                  size_t ws_bytes, int32_t *status, int32_t wait_us, int32_t flags, cudaStream_t s) {
     if (!tc_applicable(A, K)) return SPMM_EUNSUPPORTED;
     if ((uintptr_t)X & 15) return SPMM_EUNSUPPORTED;  // 16-byte X loads
     if (!A->col_grp_ptr || !A->col_ids) return SPMM_EINVAL;
@@ -944,6 +957,7 @@ int boo_matmul_tc(const spmm_boo_dev *A, const float *X, float *Y, int64_t batch
         p.status = (int *)g;
     }
     p.wait_cycles = wait_us > 0 ? (long long)wait_us * 2000 : kWaitCycles;   // ~2 GHz SM clock
+    p.expire_probe = (flags & SPMM_CFG_EXPIRE_FIRST_WAIT) ? 1 : 0;
     if (A->max_nr <= 32 && A->max_nc <= 32) return launch_tc<32, 32, 4>(p, batch, ws, ws_bytes, s);
     return launch_tc<64, 64, 2>(p, batch, ws, ws_bytes, s);
 }

@@ -7,18 +7,20 @@ neither needs a device-side remote load or a multicast:
   format is built once on the source rank and broadcast array by array
   (:func:`broadcast_boo`); every rank multiplies its own slab of X columns, so
   the product has no collective.  Suits large K with a small A (C2, C4).
-* **row split** -- row groups partitioned by nonzero balance (a prefix over
-  the per-group nonzeros, :func:`nnz_balanced_splits`).  Every rank builds
-  the format of its own rows with global column ids (:class:`RowSplitBOO`),
-  X reaches every rank once by a broadcast into local HBM
-  (:func:`broadcast_dense`), and Y shards stay local; :meth:`RowSplitBOO.gather`
-  assembles a replicated Y when a caller wants one.  Suits random gathers with
-  a large A (C3, C5).
+* **row split** -- BOO row groups or PBR stripes (``block_rows`` consecutive
+  rows) partitioned by nonzero balance (a prefix over the per-group
+  nonzeros, :func:`nnz_balanced_splits`).  Every rank builds the format of
+  its own rows with global column ids (:class:`RowSplitBOO`,
+  :class:`RowSplitPBR`), X reaches every rank once by a broadcast into local
+  HBM (:func:`broadcast_dense`), and Y shards stay local; ``gather`` assembles
+  a replicated Y when a caller wants one.  Suits random gathers with a large
+  A (C3, C5).
 
 Planning is host-side numpy, so the partition logic and the collectives are
 tested with ``gloo`` ranks on CPU; products need CUDA.  Process groups get a
 short timeout (:func:`init`), so a rank that dies makes the others' next
-collective fail instead of hanging.
+collective fail instead of hanging; every collective of this module turns
+such a failure into ``SpmmError(SPMM_ENCCL)`` (a ``RuntimeError``).
 """
 
 from __future__ import annotations
@@ -33,9 +35,33 @@ import numpy as np
 import torch
 import torch.distributed as dist
 
+from . import _lib
 from . import boo as _boo
+from . import pbr as _pbr
 
 DEFAULT_TIMEOUT_S = 60
+
+
+def _collective(what: str, fn, *args, **kw):
+    """Runs one torch.distributed collective; a failure (a peer that died, a
+    timeout, a backend error) becomes SpmmError(SPMM_ENCCL)."""
+    try:
+        return fn(*args, **kw)
+    except _lib.SpmmError:
+        raise
+    except (RuntimeError, ValueError) as e:
+        raise _lib.SpmmError(_lib.SPMM_ENCCL, f'{what} ({type(e).__name__}: {str(e)[:200]})') from e
+
+
+def barrier() -> None:
+    _collective('barrier', dist.barrier)
+
+
+def all_reduce_max(value: float, device) -> float:
+    """max of `value` over ranks (the bench's step time)."""
+    t = torch.tensor([float(value)], dtype=torch.float64, device=device)
+    _collective('all_reduce', dist.all_reduce, t, op=dist.ReduceOp.MAX)
+    return float(t.item())
 
 
 def init(backend: Optional[str] = None, timeout_s: float = DEFAULT_TIMEOUT_S,
@@ -88,6 +114,12 @@ class RowShard:
     nnz: int
 
 
+def stripe_labels(rows: int, block_rows: int) -> np.ndarray:
+    """PBR stripe of every row (row // block_rows): the row-split unit of a
+    PBR matrix, so every shard starts on a stripe boundary."""
+    return np.arange(rows, dtype=np.int64) // max(int(block_rows), 1)
+
+
 def plan_row_split(indptr: np.ndarray, row_labels: np.ndarray, parts: int) -> List[RowShard]:
     """Partition the row groups of `row_labels` (one label per row) into
     `parts` contiguous label ranges of balanced nonzeros."""
@@ -128,7 +160,7 @@ def broadcast_dense(x: Optional[torch.Tensor], shape, dtype, device, src: int = 
         out = x.to(device).contiguous()
     else:
         out = torch.empty(tuple(shape), dtype=dtype, device=device)
-    dist.broadcast(out, src)
+    _collective('broadcast', dist.broadcast, out, src)
     return out
 
 
@@ -155,7 +187,7 @@ def broadcast_boo(mat: Optional['_boo._BOOMatrix'], device, src: int = 0):
         vals = [mat._sizes[k] for k in _BOO_SIZE_KEYS]
         vals += [0 if mat._index_dtype == np.int32 else 1, 0 if mat._scalar_dtype == np.float32 else 1]
         meta.copy_(torch.tensor(vals, dtype=torch.int64))
-    dist.broadcast(meta, src)
+    _collective('broadcast', dist.broadcast, meta, src)
     m = [int(v) for v in meta.cpu()]
     sizes = dict(zip(_BOO_SIZE_KEYS, m[:len(_BOO_SIZE_KEYS)]))
     idt = np.int32 if m[-2] == 0 else np.int64
@@ -170,9 +202,52 @@ def broadcast_boo(mat: Optional['_boo._BOOMatrix'], device, src: int = 0):
         else:
             t = torch.empty(lengths[name], dtype=dt, device=device)
         if t.numel():
-            dist.broadcast(t.view(torch.uint8), src)   # byte view: no int16 collectives
+            _collective('broadcast', dist.broadcast, t.view(torch.uint8), src)   # bytes: no int16 collectives
         arrays[name] = t
     cls = _boo._boo_class(idt, sdt)
+    out = cls(sizes, types.SimpleNamespace(**arrays))
+    if torch.device(device).type == 'cuda':
+        out._gpu_meta = out._dev
+    return out
+
+
+_PBR_SIZE_KEYS = ('rows', 'cols', 'block_rows', 'block_cols', 'total_nnz', 'nb', 'nnz_c', 'rem_nnz')
+_PBR_ARRAYS = ('codes', 'coords', 'offsets', 'data', 'rem_indptr', 'rem_col_ind', 'rem_vals')
+
+
+def _pbr_lengths(sz: dict) -> dict:
+    return {'codes': sz['nb'], 'coords': 2 * sz['nb'], 'offsets': sz['nb'] + 1, 'data': sz['nnz_c'],
+            'rem_indptr': sz['rows'] + 1, 'rem_col_ind': sz['rem_nnz'], 'rem_vals': sz['rem_nnz']}
+
+
+def broadcast_pbr(mat: Optional['_pbr._PBRMatrix'], device, src: int = 0):
+    """A PBR matrix built on rank `src` replicated on every rank's `device`
+    (the feature split's A staging for the PBR format)."""
+    rank = dist.get_rank()
+    meta = torch.zeros(len(_PBR_SIZE_KEYS) + 2, dtype=torch.int64, device=device)
+    if rank == src:
+        d = mat._gpu_meta if mat._gpu_meta is not None else mat._dev
+        vals = [mat._sizes[k] for k in _PBR_SIZE_KEYS]
+        vals += [0 if d.coords.dtype == torch.int32 else 1, 0 if mat._scalar_dtype == np.float32 else 1]
+        meta.copy_(torch.tensor(vals, dtype=torch.int64))
+    _collective('broadcast', dist.broadcast, meta, src)
+    m = [int(v) for v in meta.cpu()]
+    sizes = dict(zip(_PBR_SIZE_KEYS, m[:len(_PBR_SIZE_KEYS)]))
+    tidt = torch.int32 if m[-2] == 0 else torch.int64
+    tsdt = torch.float32 if m[-1] == 0 else torch.float64
+    dtypes = {'codes': torch.int64, 'coords': tidt, 'offsets': tidt, 'data': tsdt, 'rem_indptr': tidt,
+              'rem_col_ind': tidt, 'rem_vals': tsdt}
+    lengths = _pbr_lengths(sizes)
+    arrays = {}
+    for name in _PBR_ARRAYS:
+        if rank == src:
+            t = getattr(d, name).to(device).contiguous()
+        else:
+            t = torch.empty(lengths[name], dtype=dtypes[name], device=device)
+        if t.numel():
+            _collective('broadcast', dist.broadcast, t.view(torch.uint8), src)
+        arrays[name] = t
+    cls = _pbr._pbr_class(np.int32 if m[-2] == 0 else np.int64, np.float32 if m[-1] == 0 else np.float64)
     out = cls(sizes, types.SimpleNamespace(**arrays))
     if torch.device(device).type == 'cuda':
         out._gpu_meta = out._dev
@@ -212,6 +287,32 @@ class RowSplitBOO:
         return gather_rows(y_local, self.shards, self.rows_total)
 
 
+class RowSplitPBR:
+    """This rank's share of a row-split PBR product: stripes of
+    ``block_rows`` rows partitioned by nonzero balance, so every shard starts
+    on a stripe boundary and its blocks are the global matrix's blocks of
+    those stripes (same codes, coordinates shifted by the shard's first row).
+    ``matmul(x)`` takes the full X on this rank and returns the shard's Y
+    rows (``self.shard.rows``, ascending and contiguous)."""
+
+    def __init__(self, mat, block_rows: int, block_cols: int, min_nnz_per_block: int, device,
+                 rank: Optional[int] = None, world: Optional[int] = None):
+        rank = dist.get_rank() if rank is None else rank
+        world = dist.get_world_size() if world is None else world
+        self.shards = plan_row_split(mat.indptr, stripe_labels(mat.shape[0], block_rows), world)
+        self.shard = self.shards[rank]
+        self.rows_total = mat.shape[0]
+        sub = shard_csr(mat, self.shard)
+        self.pbr = _pbr.csr_to_pbr(sub, block_rows, block_cols, min_nnz_per_block).to(device)
+        self.device = torch.device(device)
+
+    def matmul(self, x: torch.Tensor, **kw) -> torch.Tensor:
+        return _pbr.pbr_matmul(self.pbr, x, **kw)
+
+    def gather(self, y_local: torch.Tensor) -> torch.Tensor:
+        return gather_rows(y_local, self.shards, self.rows_total)
+
+
 def gather_rows(y_local: torch.Tensor, shards: List[RowShard], rows_total: int) -> torch.Tensor:
     """Y [rows_total, K] on every rank from the row shards (all_gather of
     equal-size padded shards, then a scatter by global row id)."""
@@ -221,7 +322,7 @@ def gather_rows(y_local: torch.Tensor, shards: List[RowShard], rows_total: int) 
     pad = torch.zeros((width, K), dtype=y_local.dtype, device=y_local.device)
     pad[:y_local.shape[0]] = y_local
     parts = [torch.empty_like(pad) for _ in range(world)]
-    dist.all_gather(parts, pad)
+    _collective('all_gather', dist.all_gather, parts, pad)
     y = torch.empty((rows_total, K), dtype=y_local.dtype, device=y_local.device)
     for s, part in zip(shards, parts):
         idx = torch.from_numpy(s.rows).to(y.device)

@@ -55,10 +55,11 @@ def test_host_only_entry_points():
 def test_launch_cfg_layout():
     """spmm_launch_cfg as the header lays it out (64-bit): version 2 adds the
     status word after the workspace."""
-    assert C.sizeof(_lib.LaunchCfg) == 40
-    assert _lib.LaunchCfg.status.offset == 32 and _lib.LaunchCfg.workspace.offset == 16
+    assert C.sizeof(_lib.LaunchCfg) == 48
+    assert _lib.LaunchCfg.workspace.offset == 16 and _lib.LaunchCfg.status.offset == 32
+    assert _lib.LaunchCfg.flags.offset == 40
     cfg = _lib.launch_cfg('tensor_cores', wait_us=5)
-    assert (cfg.version, cfg.engine, cfg.wait_us, cfg.status) == (2, 2, 5, None)
+    assert (cfg.version, cfg.engine, cfg.wait_us, cfg.status, cfg.flags) == (2, 2, 5, None, 0)
 
 
 def test_null_arguments_are_rejected_without_touching_a_gpu():

@@ -209,34 +209,49 @@ def test_tc_abi_workspace_required(cuda):
 
 
 def test_tc_status_per_call(cuda):
-    """Two products in flight on two streams each report into their own status
-    word: one whose waits are bounded to a microsecond gives up at its first
-    wait that is not already complete (SPMM_ETIMEOUT, Y incomplete), the other
-    completes (0, Y correct).  The timeout path drains the MMAs it issued and
-    releases tensor memory; the context stays usable afterwards."""
+    """Two products in flight on two streams report into their own status
+    words.  One runs with SPMM_CFG_EXPIRE_FIRST_WAIT: each worker's first wait
+    is on a barrier nothing arrives on, bounded to 50 us, so it expires and
+    the launch stops early (SPMM_ETIMEOUT); the other completes (0, Y right).
+    The timeout path drains the MMAs it issued and releases tensor memory:
+    the context stays usable and later products are exact."""
+    import ctypes as C
     mat = workloads.fem3d(n=12)
     boo = S.csr_to_boo(mat, cluster='identity', target_nr=32, target_nc=32)
     dev = boo.to('cuda')
+    st = dev._dev_struct(dev._gpu_meta)
     x = torch.randn(mat.shape[1], 256, generator=torch.Generator().manual_seed(2))
     xd = x.cuda()
-    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    L = _lib.lib()
+    words = torch.full((2, 64), 7, dtype=torch.int32, device='cuda')   # stale values: the call clears its own
+    ys = [torch.empty(mat.shape[0], 256, device='cuda') for _ in range(2)]
+    cfgs, keep = [], []
+    for k, flags in enumerate((_lib.SPMM_CFG_EXPIRE_FIRST_WAIT, 0)):
+        cfg = _lib.launch_cfg('tensor_cores', status=words[k].data_ptr(), wait_us=50, flags=flags)
+        n = L.spmm_boo_matmul_workspace_size(C.byref(st), 1, 256, C.byref(cfg))
+        ws = torch.empty(n, dtype=torch.uint8, device='cuda')
+        cfg.workspace, cfg.workspace_bytes = ws.data_ptr(), n
+        cfgs.append(cfg)
+        keep.append(ws)
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
     torch.cuda.synchronize()
-    with torch.cuda.stream(s1):
-        y_short = S.boo_matmul(dev, xd, engine='tensor_cores', wait_us=1)
-    with torch.cuda.stream(s2):
-        y_full = S.boo_matmul(dev, xd, engine='tensor_cores')
+    for cfg, y, stream in zip(cfgs, ys, streams):
+        rc = L.spmm_boo_matmul(C.byref(st), C.c_void_p(xd.data_ptr()), C.c_void_p(y.data_ptr()), 1, 256,
+                               C.byref(cfg), C.c_void_p(stream.cuda_stream))
+        assert rc == 0
     torch.cuda.synchronize()
-    assert S.product_status(y_short) == _lib.SPMM_ETIMEOUT
-    with pytest.raises(_lib.SpmmError):
-        S.check_product(y_short)
-    assert S.product_status(y_full) == 0
+    assert int(words[0, 0]) == _lib.SPMM_ETIMEOUT
+    assert int(words[1, 0]) == 0
     ref = _oracle_y(boo, x.numpy())
-    assert_spmm_close(S.check_product(y_full).cpu().numpy(), ref,
-                      abs_bound(mat.indptr, mat.indices, mat.data, x.numpy()), TOL[np.dtype(np.float32)])
-    assert _lib.lib().spmm_tc_status(1) == 0      # calls with a status word leave the shared one alone
+    bound = abs_bound(mat.indptr, mat.indices, mat.data, x.numpy())
+    assert_spmm_close(ys[1].cpu().numpy(), ref, bound, TOL[np.dtype(np.float32)])
+    assert L.spmm_tc_status(1) == 0      # calls with a status word leave the shared one alone
+    bad = _lib.launch_cfg('tensor_cores', flags=_lib.SPMM_CFG_EXPIRE_FIRST_WAIT)   # needs wait_us > 0
+    assert L.spmm_boo_matmul(C.byref(st), C.c_void_p(xd.data_ptr()), C.c_void_p(ys[0].data_ptr()), 1, 256,
+                             C.byref(bad), None) == _lib.SPMM_EINVAL
     again = S.boo_matmul(dev, xd, engine='tensor_cores')
     assert S.product_status(again) == 0
-    assert torch.equal(again, y_full)
+    assert_spmm_close(S.check_product(again).cpu().numpy(), ref, bound, TOL[np.dtype(np.float32)])
 
 
 @pytest.mark.parametrize('g,n_sparse,rem_rows', [

@@ -89,13 +89,15 @@ def _worker(rank, world, port, case, q):
         if case == 'fault':
             if rank == 1:
                 os._exit(3)                      # dies before the collective
+            from spmm_b200 import _lib
             try:
-                t = torch.ones(4)
-                dist.all_reduce(t)
-                dist.barrier()
+                D.all_reduce_max(1.0, 'cpu')
+                D.barrier()
                 q.put((rank, 'no error'))
-            except Exception as e:              # noqa: BLE001 -- any collective failure
-                q.put((rank, 'error: ' + type(e).__name__))
+            except _lib.SpmmError as e:         # the module's collectives report SPMM_ENCCL
+                q.put((rank, f'error: SpmmError {e.status}'))
+            except Exception as e:              # noqa: BLE001
+                q.put((rank, 'unexpected: ' + type(e).__name__))
             return
         mat = workloads.fem3d(n=6)
         rows, cols = mat.shape
@@ -117,6 +119,48 @@ def _worker(rank, world, port, case, q):
             bound = np.abs(mat) @ np.abs(x_full.numpy())
             ok = np.all(np.abs(y.numpy() - ref) <= 1e-5 * bound + 1e-30)
             q.put((rank, 'ok' if ok and sh.nnz > 0 else f'mismatch nnz={sh.nnz}'))
+        elif case == 'rowsplit_pbr':
+            mat = workloads.uniform(n=3000, k=8, seed=2)
+            rows, cols = mat.shape
+            x_full = torch.from_numpy(np.random.default_rng(5).standard_normal((cols, 24)).astype(np.float32))
+            x = D.broadcast_dense(x_full if rank == 0 else None, (cols, 24), torch.float32, 'cpu')
+            shards = D.plan_row_split(mat.indptr, D.stripe_labels(rows, 8), world)
+            sh = shards[rank]
+            assert sh.rows[0] % 8 == 0 and np.all(np.diff(sh.rows) == 1)   # stripe-aligned, contiguous
+            sub = D.shard_csr(mat, sh)
+            op = O.pbr_build(sub.indptr, sub.indices, sub.data, sub.shape[0], cols, 8, 8, 1)
+            op.update(rows=sub.shape[0], cols=cols)
+            y_local = torch.from_numpy(O.pbr_matmul(op, x.numpy()))
+            y = D.gather_rows(y_local, shards, rows)
+            full = O.pbr_build(mat.indptr, mat.indices, mat.data, rows, cols, 8, 8, 1)
+            full.update(rows=rows, cols=cols)
+            # the shards hold exactly the global matrix's blocks of their stripes
+            same_blocks = op['nb'] == int(np.sum((full['block_coords'][0::2] >= sh.rows[0]) &
+                                                  (full['block_coords'][0::2] <= sh.rows[-1])))
+            ref = O.pbr_matmul(full, x_full.numpy())
+            bound = np.abs(mat) @ np.abs(x_full.numpy())
+            ok = np.all(np.abs(y.numpy() - ref) <= 1e-5 * bound + 1e-30)
+            q.put((rank, 'ok' if ok and same_blocks and sh.nnz > 0 else f'mismatch nnz={sh.nnz} {same_blocks}'))
+        elif case == 'broadcast_pbr':
+            from spmm_b200 import pbr as P
+            full = O.pbr_build(mat.indptr, mat.indices, mat.data, rows, cols, 8, 8, 4)
+            src = None
+            if rank == 0:
+                arr = dict(codes=torch.from_numpy(full['block_codes'].view(np.int64)),
+                           coords=torch.from_numpy(full['block_coords'].astype(np.int32)),
+                           offsets=torch.from_numpy(full['block_offsets'].astype(np.int32)),
+                           data=torch.from_numpy(full['block_data']),
+                           rem_indptr=torch.from_numpy(full['remainder_indptr'].astype(np.int32)),
+                           rem_col_ind=torch.from_numpy(full['remainder_col_ind'].astype(np.int32)),
+                           rem_vals=torch.from_numpy(full['remainder_data']))
+                sizes = dict(rows=rows, cols=cols, block_rows=8, block_cols=8,
+                             total_nnz=int(mat.nnz), nb=int(full['nb']), nnz_c=int(full['nnz_c']),
+                             rem_nnz=int(full['rem_nnz']))
+                src = P.PBRMatrixInt32Float(sizes, types.SimpleNamespace(**arr))
+            got = D.broadcast_pbr(src, 'cpu')
+            same = all(np.array_equal(getattr(got, f), full[f]) for f in O.PBR_FIELDS) \
+                and type(got).__name__ == 'PBRMatrixInt32Float'
+            q.put((rank, 'ok' if same else 'mismatch'))
         elif case == 'broadcast':
             full = O.boo_build(mat.indptr, mat.indices, mat.data, rows, cols, rl, cl)
             sizes = {k: full[k] for k in D._BOO_SIZE_KEYS}
@@ -168,7 +212,23 @@ def test_broadcast_boo_over_gloo():
 
 
 @pytest.mark.timeout(300)
+def test_row_split_pbr_over_gloo():
+    out, codes = _run('rowsplit_pbr')
+    assert out == {0: 'ok', 1: 'ok'}, out
+    assert codes == [0, 0]
+
+
+@pytest.mark.timeout(300)
+def test_broadcast_pbr_over_gloo():
+    out, codes = _run('broadcast_pbr')
+    assert out == {0: 'ok', 1: 'ok'}, out
+
+
+@pytest.mark.timeout(300)
 def test_dead_rank_fails_collective_within_timeout():
+    """A rank that dies before a collective: the survivor's next collective
+    fails within the process-group timeout as SpmmError(SPMM_ENCCL)."""
+    from spmm_b200 import _lib
     out, codes = _run('fault', timeout=120)
     assert codes[1] == 3
-    assert out.get(0, '').startswith('error'), out
+    assert out.get(0, '') == f'error: SpmmError {_lib.SPMM_ENCCL}', out
