@@ -248,6 +248,18 @@ int spmm_pbr_build_emit(const spmm_csr_dev *A, int64_t block_rows, int64_t block
 int spmm_boo_matmul(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch, int64_t K,
                     const spmm_launch_cfg *cfg, spmm_stream_t stream);
 
+/* The same product restricted to row groups [rg_begin, rg_end): exactly the Y
+ * rows of those groups (row_ids[row_grp_ptr[rg_begin] .. row_grp_ptr[rg_end]))
+ * are written, and only the X rows their blocks, remainder and tail entries
+ * use are read, so a caller can multiply row groups as soon as their X rows
+ * have arrived and copy their Y rows out while later groups run (no
+ * reference counterpart; the reference has no partial product).  Same
+ * configuration and workspace as spmm_boo_matmul.  SPMM_EUNSUPPORTED for
+ * remainder-major matrices (CSR remainder >= half of the nonzeros) unless
+ * the range is the whole matrix. */
+int spmm_boo_matmul_groups(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch, int64_t K,
+                           int64_t rg_begin, int64_t rg_end, const spmm_launch_cfg *cfg, spmm_stream_t stream);
+
 /* Bytes of device scratch the BOO product needs in cfg->workspace for these
  * operands and settings: the X panels gathered by column group (tensor-core
  * product) or the chunk table and partial rows of the nnz-flat remainder

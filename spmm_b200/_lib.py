@@ -37,7 +37,8 @@ EXPORTS = ('spmm_status_string', 'spmm_abi_version', 'spmm_boo_build_workspace_s
            'spmm_pbr_build_analyze', 'spmm_pbr_build_emit', 'spmm_boo_matmul', 'spmm_pbr_matmul',
            'spmm_tc_status', 'spmm_boo_matmul_workspace_size', 'spmm_product_launches',
            'spmm_boo_to_csr_workspace_size', 'spmm_boo_to_csr', 'spmm_pbr_to_csr_workspace_size',
-           'spmm_pbr_to_csr', 'spmm_hem_labels', 'spmm_hem_level_slots', 'spmm_hem_hierarchy')
+           'spmm_pbr_to_csr', 'spmm_hem_labels', 'spmm_hem_level_slots', 'spmm_hem_hierarchy',
+           'spmm_boo_matmul_groups')
 
 
 class CsrDev(C.Structure):
@@ -128,6 +129,9 @@ def lib() -> C.CDLL:
                                       C.POINTER(LaunchCfg), C.c_void_p]
         L.spmm_pbr_matmul.argtypes = [C.POINTER(PbrDev), C.c_void_p, C.c_void_p, C.c_int64, C.c_int64,
                                       C.POINTER(LaunchCfg), C.c_void_p]
+        L.spmm_boo_matmul_groups.argtypes = [C.POINTER(BooDev), C.c_void_p, C.c_void_p, C.c_int64, C.c_int64,
+                                             C.c_int64, C.c_int64, C.POINTER(LaunchCfg), C.c_void_p]
+        L.spmm_boo_matmul_groups.restype = C.c_int
         L.spmm_boo_matmul_workspace_size.argtypes = [C.POINTER(BooDev), C.c_int64, C.c_int64,
                                                      C.POINTER(LaunchCfg)]
         L.spmm_boo_matmul_workspace_size.restype = C.c_size_t

@@ -529,6 +529,10 @@ def boo_matmul(boo_mat, x: torch.Tensor, threads: int = 256, p: int = 64,
         require_cuda('boo_matmul')
         device = default_device()
         meta = boo_mat._staged_on(device)
+        from . import pipeline
+        if pipeline.applies(boo_mat, x):     # copies in both directions overlapped with the product
+            y = pipeline.host_product(boo_mat, meta, x, device, engine, slab_features)
+            return y
         yd, status = _run_boo(boo_mat, meta, x.to(device, non_blocking=True), engine, slab_features)
         y = _to_host(yd, x)                      # synchronises: the status word is final
         if status is not None and int(status.item()):

@@ -22,8 +22,9 @@
 
 namespace spmm {
 
-int boo_matmul_tc(const spmm_boo_dev *A, const float *X, float *Y, int64_t batch, int64_t K, void *ws,
-                  size_t ws_bytes, int32_t *status, int32_t wait_us, int32_t flags, cudaStream_t s);
+int boo_matmul_tc(const spmm_boo_dev *A, const float *X, float *Y, int64_t batch, int64_t K, int64_t rg_first,
+                  int64_t rg_end, void *ws, size_t ws_bytes, int32_t *status, int32_t wait_us, int32_t flags,
+                  cudaStream_t s);
 size_t boo_tc_workspace(const spmm_boo_dev *A, int64_t batch, int64_t K);
 
 namespace {
@@ -53,7 +54,8 @@ struct BooParams {
     // nnz-flat remainder: chunks of `chunk` entries, the row holding each
     // chunk's first entry, two partial-sum rows per (batch, chunk)
     int64_t rem_nnz, nch;
-    int64_t n_rg, rgs_per_cta;   // block kernel: CTA x takes row groups [x * rgs_per_cta, ...)
+    int64_t n_rg, rgs_per_cta;   // block kernel: CTA x takes row groups rg_first + [x * rgs_per_cta, ...)
+    int64_t rg_first;            //   up to n_rg (the end of the range, exclusive)
     int32_t chunk;
     int32_t *chunk_row;
     S *part;
@@ -151,7 +153,7 @@ boo_spmm_kernel(const BooParams<S> p) {
     for (int v = 0; v < VPT; ++v) vm[v] = f0 + (int64_t)v * LPR * VEC < p.K;
 
     // row groups [rg_begin, rg_end); blocks found by one search, then walked
-    const int64_t rg_begin = (int64_t)blockIdx.x * p.rgs_per_cta;
+    const int64_t rg_begin = p.rg_first + (int64_t)blockIdx.x * p.rgs_per_cta;
     const int64_t rg_end = rg_begin + p.rgs_per_cta < p.n_rg ? rg_begin + p.rgs_per_cta : p.n_rg;
     if (warp == 0) {   // 32-way searches by warp 0
         const int64_t lo0 = warp_lower_bound(p.blk_row_grp, p.nb, rg_begin, lane);
@@ -327,11 +329,14 @@ boo_spmm_kernel(const BooParams<S> p) {
 // One CTA per row group; in add mode (skip_rem: most groups have nothing to
 // add) each CTA walks a run of groups, so the empty ones cost one load each.
 template <typename S, int VEC, int VPT, int LPR>
-int launch_boo_n(BooParams<S> p, int64_t n_rg, cudaStream_t s) {
+int launch_boo_n(BooParams<S> p, int64_t rg_first, int64_t rg_end, cudaStream_t s) {
     constexpr int SLAB = LPR * VPT * VEC;
     const int64_t slabs = ceil_div(p.K, SLAB);
+    const int64_t n_rg = rg_end - rg_first;
     if (slabs > 65535 || n_rg > 0x7fffffffLL) return SPMM_EUNSUPPORTED;
-    p.n_rg = n_rg;
+    if (n_rg <= 0) return SPMM_OK;
+    p.n_rg = rg_end;
+    p.rg_first = rg_first;
     p.rgs_per_cta = 1;
     if (p.skip_rem) {
         int dev = 0, sms = 0;
@@ -894,36 +899,36 @@ int rem_dispatch(const BooParams<S> &p, bool aligned, int slab_req, void *ws, cu
 }
 
 template <typename S>
-int boo_dispatch(const BooParams<S> &p, int64_t n_rg, bool aligned, cudaStream_t s);
+int boo_dispatch(const BooParams<S> &p, int64_t rg0, int64_t rg1, bool aligned, cudaStream_t s);
 
 template <>
-int boo_dispatch<float>(const BooParams<float> &p, int64_t n_rg, bool aligned, cudaStream_t s) {
+int boo_dispatch<float>(const BooParams<float> &p, int64_t rg0, int64_t rg1, bool aligned, cudaStream_t s) {
     const int64_t K = p.K;
     if (aligned && K % 4 == 0) {
-        if (K <= 32) return launch_boo_n<float, 4, 1, 8>(p, n_rg, s);
-        if (K <= 64) return launch_boo_n<float, 4, 1, 16>(p, n_rg, s);
-        if (K <= 128) return launch_boo_n<float, 4, 1, 32>(p, n_rg, s);
-        if (K <= 256) return launch_boo_n<float, 4, 2, 32>(p, n_rg, s);
-        return launch_boo_n<float, 4, 4, 32>(p, n_rg, s);
+        if (K <= 32) return launch_boo_n<float, 4, 1, 8>(p, rg0, rg1, s);
+        if (K <= 64) return launch_boo_n<float, 4, 1, 16>(p, rg0, rg1, s);
+        if (K <= 128) return launch_boo_n<float, 4, 1, 32>(p, rg0, rg1, s);
+        if (K <= 256) return launch_boo_n<float, 4, 2, 32>(p, rg0, rg1, s);
+        return launch_boo_n<float, 4, 4, 32>(p, rg0, rg1, s);
     }
-    if (K <= 32) return launch_boo_n<float, 1, 1, 32>(p, n_rg, s);
-    if (K <= 64) return launch_boo_n<float, 1, 2, 32>(p, n_rg, s);
-    return launch_boo_n<float, 1, 4, 32>(p, n_rg, s);
+    if (K <= 32) return launch_boo_n<float, 1, 1, 32>(p, rg0, rg1, s);
+    if (K <= 64) return launch_boo_n<float, 1, 2, 32>(p, rg0, rg1, s);
+    return launch_boo_n<float, 1, 4, 32>(p, rg0, rg1, s);
 }
 
 template <>
-int boo_dispatch<double>(const BooParams<double> &p, int64_t n_rg, bool aligned, cudaStream_t s) {
+int boo_dispatch<double>(const BooParams<double> &p, int64_t rg0, int64_t rg1, bool aligned, cudaStream_t s) {
     const int64_t K = p.K;
     if (aligned && K % 2 == 0) {
-        if (K <= 16) return launch_boo_n<double, 2, 1, 8>(p, n_rg, s);
-        if (K <= 32) return launch_boo_n<double, 2, 1, 16>(p, n_rg, s);
-        if (K <= 64) return launch_boo_n<double, 2, 1, 32>(p, n_rg, s);
-        if (K <= 128) return launch_boo_n<double, 2, 2, 32>(p, n_rg, s);
-        return launch_boo_n<double, 2, 4, 32>(p, n_rg, s);
+        if (K <= 16) return launch_boo_n<double, 2, 1, 8>(p, rg0, rg1, s);
+        if (K <= 32) return launch_boo_n<double, 2, 1, 16>(p, rg0, rg1, s);
+        if (K <= 64) return launch_boo_n<double, 2, 1, 32>(p, rg0, rg1, s);
+        if (K <= 128) return launch_boo_n<double, 2, 2, 32>(p, rg0, rg1, s);
+        return launch_boo_n<double, 2, 4, 32>(p, rg0, rg1, s);
     }
-    if (K <= 32) return launch_boo_n<double, 1, 1, 32>(p, n_rg, s);
-    if (K <= 64) return launch_boo_n<double, 1, 2, 32>(p, n_rg, s);
-    return launch_boo_n<double, 1, 4, 32>(p, n_rg, s);
+    if (K <= 32) return launch_boo_n<double, 1, 1, 32>(p, rg0, rg1, s);
+    if (K <= 64) return launch_boo_n<double, 1, 2, 32>(p, rg0, rg1, s);
+    return launch_boo_n<double, 1, 4, 32>(p, rg0, rg1, s);
 }
 
 // AUTO: the tensor-core kernel wins (measured on B200) when blocks (up to
@@ -937,14 +942,14 @@ bool tc_selected(const spmm_boo_dev *A, int engine) {
 }
 
 template <typename S>
-int boo_matmul_impl(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch, int64_t K, int engine,
-                    const spmm_launch_cfg *cfg, cudaStream_t s) {
+int boo_matmul_impl(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch, int64_t K, int64_t rg0,
+                    int64_t rg1, int engine, const spmm_launch_cfg *cfg, cudaStream_t s) {
     void *ws = cfg ? cfg->workspace : nullptr;
     const size_t ws_bytes = cfg && ws ? (size_t)cfg->workspace_bytes : 0;
     if constexpr (sizeof(S) == 4) {
         if (tc_selected(A, engine)) {
             const bool v2 = cfg && cfg->version >= 2;
-            const int rc = boo_matmul_tc(A, (const float *)X, (float *)Y, batch, K, ws, ws_bytes,
+            const int rc = boo_matmul_tc(A, (const float *)X, (float *)Y, batch, K, rg0, rg1, ws, ws_bytes,
                                          v2 ? cfg->status : nullptr, cfg ? cfg->wait_us : 0, v2 ? cfg->flags : 0, s);
             if (rc != SPMM_EUNSUPPORTED || engine == SPMM_ENGINE_TENSOR_CORES) return rc;
         }
@@ -979,6 +984,7 @@ int boo_matmul_impl(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch
     p.rowmajor = A->nz_order == SPMM_BOO_ROWMAJOR;
     p.rem_nnz = A->rem_nnz;
     p.n_rg = A->n_rg;
+    p.rg_first = 0;
     p.rgs_per_cta = 1;
     p.nch = 0;
     p.chunk = 0;
@@ -988,6 +994,7 @@ int boo_matmul_impl(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch
     // remainder-major matrices: the load-balanced remainder kernels write Y,
     // then the block kernel adds blocks and tail where a row group has any
     p.skip_rem = A->rem_nnz > 0 && 2 * A->rem_nnz >= A->total_nnz;
+    if (p.skip_rem && (rg0 != 0 || rg1 != A->n_rg)) return SPMM_EUNSUPPORTED;   // whole matrix only
     if (p.skip_rem) {
         const int slab_req = cfg ? cfg->slab_features : 0;
         if (rem_flat_applies(p, aligned, slab_req) &&
@@ -996,17 +1003,12 @@ int boo_matmul_impl(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch
         const int rc = rem_dispatch<S>(p, aligned, slab_req, ws, s);   // Y = remainder
         if (rc != SPMM_OK) return rc;
     }
-    return boo_dispatch<S>(p, A->n_rg, aligned, s);      // (+)= blocks and tail
+    return boo_dispatch<S>(p, rg0, rg1, aligned, s);      // (+)= blocks and tail
 }
 
-}  // namespace
-}  // namespace spmm
-
-
-using namespace spmm;
-
-extern "C" int spmm_boo_matmul(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch, int64_t K,
-                               const spmm_launch_cfg *cfg, spmm_stream_t stream) {
+// Checks shared by the whole-matrix and row-group-range products; then the product.
+int boo_matmul_checked(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch, int64_t K, int64_t rg0,
+                       int64_t rg1, const spmm_launch_cfg *cfg, cudaStream_t s) {
     if (!A || batch < 0 || K < 0) return SPMM_EINVAL;
     if (cfg && cfg->version != 1 && cfg->version != 2) return SPMM_EINVAL;
     const int engine = cfg ? cfg->engine : SPMM_ENGINE_AUTO;
@@ -1018,20 +1020,37 @@ extern "C" int spmm_boo_matmul(const spmm_boo_dev *A, const void *X, void *Y, in
     if (A->scalar_type != SPMM_F32 && A->scalar_type != SPMM_F64) return SPMM_EINVAL;
     if (A->nz_order != SPMM_BOO_ROWMAJOR && A->nz_order != SPMM_BOO_COLMAJOR) return SPMM_EINVAL;
     if (A->rows < 0 || A->cols < 0 || A->n_rg < 0 || A->nb < 0 || A->tail_nnz < 0) return SPMM_EINVAL;
+    if (rg0 < 0 || rg1 < rg0 || rg1 > A->n_rg) return SPMM_EINVAL;
     if (A->rows > 0x7fffffffLL || A->cols > 0x7fffffffLL) return SPMM_EUNSUPPORTED;
     if (A->max_nr > 65536 || A->max_nc > 65536) return SPMM_EUNSUPPORTED;
-    cudaStream_t s = (cudaStream_t)stream;
     if (cfg && cfg->version >= 2 && cfg->status)   // this call's status word starts at 0
         SPMM_CUDA_TRY(cudaMemsetAsync(cfg->status, 0, sizeof(int32_t), s));
-    if (batch == 0 || K == 0 || A->rows == 0) return SPMM_OK;
+    if (batch == 0 || K == 0 || A->rows == 0 || rg0 == rg1) return SPMM_OK;
     if (!Y || (A->cols && !X)) return SPMM_EINVAL;
     if (!A->row_grp_ptr || !A->row_ids || !A->rem_indptr) return SPMM_EINVAL;
     if (A->nb && (!A->blk_row_grp || !A->blk_col_grp || !A->blk_nz_ptr || !A->blk_shift ||
                   !A->nz_idx || !A->nz_val || !A->col_grp_ptr || !A->col_ids))
         return SPMM_EINVAL;
     if (A->n_rg == 0) return SPMM_EINVAL;  // rows > 0 need at least one group
-    if (A->scalar_type == SPMM_F32) return boo_matmul_impl<float>(A, X, Y, batch, K, engine, cfg, s);
-    return boo_matmul_impl<double>(A, X, Y, batch, K, engine, cfg, s);
+    if (A->scalar_type == SPMM_F32) return boo_matmul_impl<float>(A, X, Y, batch, K, rg0, rg1, engine, cfg, s);
+    return boo_matmul_impl<double>(A, X, Y, batch, K, rg0, rg1, engine, cfg, s);
+}
+
+}  // namespace
+}  // namespace spmm
+
+
+using namespace spmm;
+
+extern "C" int spmm_boo_matmul(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch, int64_t K,
+                               const spmm_launch_cfg *cfg, spmm_stream_t stream) {
+    return boo_matmul_checked(A, X, Y, batch, K, 0, A ? A->n_rg : 0, cfg, (cudaStream_t)stream);
+}
+
+extern "C" int spmm_boo_matmul_groups(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch, int64_t K,
+                                      int64_t rg_begin, int64_t rg_end, const spmm_launch_cfg *cfg,
+                                      spmm_stream_t stream) {
+    return boo_matmul_checked(A, X, Y, batch, K, rg_begin, rg_end, cfg, (cudaStream_t)stream);
 }
 
 extern "C" size_t spmm_boo_matmul_workspace_size(const spmm_boo_dev *A, int64_t batch, int64_t K,

@@ -76,6 +76,9 @@ constexpr long long kWaitCycles = 1ll << 32;  // ~2 s at 2 GHz (default bound of
 
 struct TcParams {
     int64_t rows, cols, K, nb, n_rg, rem_nnz, tail_nnz;
+    int64_t rg_first;    // row groups [rg_first, n_rg) are multiplied (n_rg: end of the range)
+    int64_t n_rg_all;    // row groups of the matrix
+    const unsigned long long *cg_range;   // null, or [min, max] column group the range's blocks use
     int32_t dense_nnz;   // blocks with at least this many nonzeros use the tensor cores
     int64_t n_chunks, n_ft, n_tasks;
     int32_t chunk_rgs;
@@ -543,7 +546,7 @@ __device__ void worker(const TcParams &p, WorkerSmem<NR, PW> &w, Ctl &ctl, uint3
     for (int64_t task = wid; task < p.n_tasks && ok; task += nworkers) {
         const int64_t ft = task % p.n_ft, chunk = (task / p.n_ft) % p.n_chunks;
         const int64_t bt = task / (p.n_ft * p.n_chunks);
-        const int64_t rg0 = chunk * p.chunk_rgs;
+        const int64_t rg0 = p.rg_first + chunk * p.chunk_rgs;
         const int64_t rg1 = rg0 + p.chunk_rgs < p.n_rg ? rg0 + p.chunk_rgs : p.n_rg;
         const float *xb = p.X + bt * p.cols * p.K + ft * kFeat + wt;
         float *yb = p.Y + bt * p.rows * p.K + ft * kFeat + wt;
@@ -823,6 +826,7 @@ __global__ void __launch_bounds__(256) boo_gather_kernel(const TcParams p) {
         xr[c] = c < nc ? p.X + (bt * p.cols + __ldg(p.col_ids + cbase + c)) * p.K : nullptr;
     }
     __syncthreads();
+    if (p.cg_range && (g < (int64_t)p.cg_range[0] || g > (int64_t)p.cg_range[1])) return;   // not used
     float4 *out = const_cast<float4 *>(p.Xt) + (bt * p.n_cg + g) * QW * p.K;
     // item = (quad q, 4 features from f): four 16-byte loads (one per column
     // of the quad), a 4 x 4 transpose in registers, four 16-byte stores
@@ -844,6 +848,31 @@ __global__ void __launch_bounds__(256) boo_gather_kernel(const TcParams p) {
     }
 }
 
+// Smallest and largest column group used by the blocks of row groups
+// [rg_first, n_rg) into cg_range[0] / [1] (initialised to ~0 / 0 by the host),
+// so that a row-group-range product gathers only those groups.
+__global__ void __launch_bounds__(256) cg_range_kernel(const TcParams p, unsigned long long *cg_range) {
+    const int lane = threadIdx.x & 31;
+    const int64_t b0 = warp_lower_bound(p.blk_row_grp, p.nb, p.rg_first, lane);
+    const int64_t b1 = warp_lower_bound(p.blk_row_grp, p.nb, p.n_rg, lane);
+    unsigned long long lo = ~0ull, hi = 0ull;
+    for (int64_t b = b0 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; b < b1; b += (int64_t)gridDim.x * blockDim.x) {
+        const unsigned long long g = (unsigned long long)__ldg(p.blk_col_grp + b);
+        lo = g < lo ? g : lo;
+        hi = g > hi ? g : hi;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        const unsigned long long l2 = __shfl_xor_sync(kFullMask, lo, o), h2 = __shfl_xor_sync(kFullMask, hi, o);
+        lo = l2 < lo ? l2 : lo;
+        hi = h2 > hi ? h2 : hi;
+    }
+    if (lane == 0 && lo != ~0ull) {
+        atomicMin(cg_range, lo);
+        atomicMax(cg_range + 1, hi);
+    }
+}
+
 int sm_count() {
     int dev = 0, n = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return -1;
@@ -851,9 +880,11 @@ int sm_count() {
     return n;
 }
 
+// Gathered X panels, then 256 bytes for the column-group range of a
+// row-group-range product.
 template <int PW>
 size_t gather_bytes(const spmm_boo_dev *A, int64_t batch, int64_t K) {
-    return (size_t)batch * (size_t)A->n_cg * PW * (size_t)K * sizeof(float);
+    return (size_t)batch * (size_t)A->n_cg * PW * (size_t)K * sizeof(float) + 256;
 }
 
 template <int NR, int PW, int NW>
@@ -863,23 +894,36 @@ int launch_tc(TcParams p, int64_t batch, void *ws, size_t ws_bytes, cudaStream_t
     if (sms <= 0) return SPMM_ECUDA;
     const int64_t gather_rows = batch * p.n_cg * (PW / 4);
     if (gather_rows > 0x7fffffffLL) return SPMM_EUNSUPPORTED;
-    const size_t need = (size_t)gather_rows * (size_t)p.K * sizeof(float4);
-    if (need && (!ws || ws_bytes < need)) return SPMM_EWORKSPACE;
+    const size_t xt_bytes = (size_t)gather_rows * (size_t)p.K * sizeof(float4);
+    if (!ws || ws_bytes < xt_bytes + 256) return SPMM_EWORKSPACE;
     if ((uintptr_t)ws & 15) return SPMM_EALIGN;
     p.Xt = (const float4 *)ws;
     p.n_ft = p.K / kFeat;
+    const int64_t n_rg = p.n_rg - p.rg_first;   // row groups of the range
+    if (n_rg <= 0) return SPMM_OK;
     // chunks of consecutive row groups, small enough for ~16 tasks per worker
     const int64_t workers = (int64_t)sms * NW;
-    int64_t c = p.n_rg / (16 * workers * p.n_ft * batch);
+    int64_t c = n_rg / (16 * workers * p.n_ft * batch);
     c = c < 1 ? 1 : (c > 8 ? 8 : c);
     p.chunk_rgs = (int32_t)c;
-    p.n_chunks = ceil_div(p.n_rg, c);
+    p.n_chunks = ceil_div(n_rg, c);
     p.n_tasks = p.n_chunks * p.n_ft * batch;
     if (p.n_tasks > 0x7fffffffLL) return SPMM_EUNSUPPORTED;
     const int64_t ctas = ceil_div(p.n_tasks, (int64_t)NW);
     const int grid = (int)(ctas < sms ? ctas : sms);
     auto kern = boo_tc_kernel<NR, PW, NW>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Shape::kSmem);
+    p.cg_range = nullptr;
+    if (e == cudaSuccess && (p.rg_first != 0 || p.n_rg != p.n_rg_all)) {   // part of the row groups
+        auto *range = reinterpret_cast<unsigned long long *>(static_cast<uint8_t *>(ws) + xt_bytes);
+        e = cudaMemsetAsync(range, 0xFF, 8, s);
+        if (e == cudaSuccess) e = cudaMemsetAsync(range + 1, 0, 8, s);
+        if (e == cudaSuccess) {
+            cg_range_kernel<<<(unsigned)(sms * 2), 256, 0, s>>>(p, range);
+            e = cudaGetLastError();
+        }
+        p.cg_range = range;
+    }
     if (e == cudaSuccess && gather_rows > 0) {
         boo_gather_kernel<PW><<<(unsigned)(batch * p.n_cg), 256, 0, s>>>(p);
         e = cudaGetLastError();
@@ -916,8 +960,9 @@ size_t boo_tc_workspace(const spmm_boo_dev *A, int64_t batch, int64_t K) {
 // g_tc_status); `wait_us` > 0 bounds the abortable waits to about that many
 // microseconds instead of ~2 s; `flags` & SPMM_CFG_EXPIRE_FIRST_WAIT makes
 // each worker's first wait expire (tests of the timeout path).
-int boo_matmul_tc(const spmm_boo_dev *A, const float *X, float *Y, int64_t batch, int64_t K, void *ws,
-                  size_t ws_bytes, int32_t *status, int32_t wait_us, int32_t flags, cudaStream_t s) {
+int boo_matmul_tc(const spmm_boo_dev *A, const float *X, float *Y, int64_t batch, int64_t K, int64_t rg_first,
+                  int64_t rg_end, void *ws, size_t ws_bytes, int32_t *status, int32_t wait_us, int32_t flags,
+                  cudaStream_t s) {
     if (!tc_applicable(A, K)) return SPMM_EUNSUPPORTED;
     if ((uintptr_t)X & 15) return SPMM_EUNSUPPORTED;  // 16-byte X loads
     if (!A->col_grp_ptr || !A->col_ids) return SPMM_EINVAL;
@@ -926,7 +971,9 @@ int boo_matmul_tc(const spmm_boo_dev *A, const float *X, float *Y, int64_t batch
     p.cols = A->cols;
     p.K = K;
     p.nb = A->nb;
-    p.n_rg = A->n_rg;
+    p.n_rg = rg_end;
+    p.rg_first = rg_first;
+    p.n_rg_all = A->n_rg;
     p.rem_nnz = A->rem_nnz;
     p.tail_nnz = A->tail_nnz;
     p.row_grp_ptr = A->row_grp_ptr;
