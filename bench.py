@@ -71,7 +71,7 @@ def parse():
     ap.add_argument('--gen-kw', default=None,
                     help='JSON overrides of the generator size (reduced cases for profiling)')
     ap.add_argument('--no-cusparse', action='store_true', help='skip the cuSPARSE reference timing')
-    ap.add_argument('--engine', choices=('auto', 'cuda_cores', 'tensor_cores'), default='auto',
+    ap.add_argument('--engine', choices=('auto', 'cuda_cores', 'tensor_cores', 'tensor_cores_tf32'), default='auto',
                     help="units that multiply the BOO blocks (spmm_launch_cfg.engine)")
     ap.add_argument('--grouping', choices=('identity', 'hem'), default='identity',
                     help="BOO row / column grouping (cluster='hem' runs the GPU HEM labels; build time only)")
@@ -92,13 +92,23 @@ def W_CONFIG_KW(cfg_name):
     return W.CONFIGS[cfg_name]['kw']
 
 
+_MATRICES = {}
+
+
 def make_matrix(cfg_name, gen_kw=None):
+    """The config's seeded matrix; the last two are kept, so the per-config
+    table does not regenerate the headline's matrix or the previous entry's."""
     from spmm_b200 import workloads as W
     cfg = W.CONFIGS[cfg_name]
-    kw = dict(cfg['kw'])
-    if gen_kw:
-        kw.update(json.loads(gen_kw))
-    return cfg['gen'](**kw), cfg
+    key = (cfg_name, gen_kw)
+    if key not in _MATRICES:
+        kw = dict(cfg['kw'])
+        if gen_kw:
+            kw.update(json.loads(gen_kw))
+        while len(_MATRICES) >= 2:
+            _MATRICES.pop(next(iter(_MATRICES)))
+        _MATRICES[key] = cfg['gen'](**kw)
+    return _MATRICES[key], cfg
 
 
 # ---------------------------------------------------------------------------
@@ -486,7 +496,7 @@ def runs_on_tensor_cores(A, K, engine):
         return False
     if s['max_nr'] > 64 or s['max_nc'] > 64:
         return False
-    return engine == 'tensor_cores' or s['nnz_c'] >= 96 * s['nb']
+    return engine in ('tensor_cores', 'tensor_cores_tf32') or s['nnz_c'] >= 96 * s['nb']
 
 
 def product_launcher(A, fmt, x, y, engine, slab_features=0):
@@ -577,8 +587,7 @@ def measure_config(name, fmt, grouping, engine, args, dev, want_cpu=True, want_c
     import torch
     import spmm_b200 as S
     from spmm_b200 import workloads as W
-    cfg = W.CONFIGS[name]
-    mat = cfg['gen'](**cfg['kw'])
+    mat, cfg = make_matrix(name)
     K = cfg['K']
     t0 = time.perf_counter()
     if fmt == 'boo':
@@ -631,7 +640,9 @@ def measure_config(name, fmt, grouping, engine, args, dev, want_cpu=True, want_c
 
 # the per-config table: (config, format, grouping, engine, label); C3 as the
 # config names it (HEM grouping) and with identity grouping, C2 and C5 in
-# both formats the configs name, C4 on both engines the config compares
+# both formats the configs name, C4 on the engines the config compares (the
+# three-term tensor-core split at float32 accuracy, CUDA cores, and the opt-in
+# one-term tf32 product, whose accuracy is tf32's: never the float32 figure)
 PER_CONFIG = [
     ('c1_laplacian2d', 'boo', 'identity', 'auto', 'c1_laplacian2d'),
     ('c2_fem3d', 'pbr', None, 'auto', 'c2_fem3d_pbr'),
@@ -639,6 +650,7 @@ PER_CONFIG = [
     ('c3_powerlaw', 'boo', 'identity', 'auto', 'c3_powerlaw_identity'),
     ('c4_blockdiag', 'boo', 'identity', 'auto', 'c4_blockdiag'),
     ('c4_blockdiag', 'boo', 'identity', 'cuda_cores', 'c4_blockdiag_cuda_cores'),
+    ('c4_blockdiag', 'boo', 'identity', 'tensor_cores_tf32', 'c4_blockdiag_tf32'),
     ('c5_uniform', 'pbr', None, 'auto', 'c5_uniform'),
     ('c5_uniform', 'boo', 'identity', 'auto', 'c5_uniform_boo'),
 ]

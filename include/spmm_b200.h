@@ -168,7 +168,9 @@ enum spmm_cfg_flags { SPMM_CFG_EXPIRE_FIRST_WAIT = 1 };
 enum spmm_engine {
     SPMM_ENGINE_AUTO = 0,
     SPMM_ENGINE_CUDA_CORES = 1,   /* fp32/fp64 FMA, the reference CPU path's summation order */
-    SPMM_ENGINE_TENSOR_CORES = 2  /* tcgen05 3xTF32; SPMM_EUNSUPPORTED when not applicable */
+    SPMM_ENGINE_TENSOR_CORES = 2, /* tcgen05 3xTF32; SPMM_EUNSUPPORTED when not applicable */
+    SPMM_ENGINE_TENSOR_CORES_TF32 = 3  /* opt-in: one tf32 product per K step (tf32 accuracy,
+                                        * about 2e-3 relative; never chosen by AUTO) */
 };
 
 /* ---- status ---------------------------------------------------------- */

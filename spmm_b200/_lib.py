@@ -79,7 +79,7 @@ class LaunchCfg(C.Structure):
 SPMM_CFG_EXPIRE_FIRST_WAIT = 1
 
 
-ENGINES = {'auto': 0, 'cuda_cores': 1, 'tensor_cores': 2}
+ENGINES = {'auto': 0, 'cuda_cores': 1, 'tensor_cores': 2, 'tensor_cores_tf32': 3}
 
 
 def launch_cfg(engine: str = 'auto', workspace: int = 0, workspace_bytes: int = 0,

@@ -494,8 +494,10 @@ def boo_matmul(boo_mat, x: torch.Tensor, threads: int = 256, p: int = 64,
 
     ``engine`` (not in the reference) picks the units that multiply the
     blocks: 'auto' (tensor cores for float32 with K a multiple of 128 and
-    blocks up to 64 x 64, else CUDA cores), 'cuda_cores', or 'tensor_cores'
-    (an error where not applicable).  ``slab_features`` (not in the
+    blocks up to 64 x 64, else CUDA cores), 'cuda_cores', 'tensor_cores'
+    (three-term tf32 split, float32 accuracy; an error where not applicable)
+    or 'tensor_cores_tf32' (opt-in, one tf32 product: tf32 accuracy, about
+    2e-3 relative, never chosen by 'auto').  ``slab_features`` (not in the
     reference) selects the remainder kernels of a remainder-major matrix: 0
     (default) the nnz-flat chunks, a negative value the register path (no
     workspace).  ``wait_us`` (not in the reference) bounds the tensor-core

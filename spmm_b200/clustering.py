@@ -39,15 +39,14 @@ DEFAULT_TOPK = 32
 
 def _pattern(mat) -> sp.csr_matrix:
     """Canonical binary CSR of the sparsity pattern: each (row, col) that
-    appears at least once, columns ascending, value 1 (int32)."""
-    coo = sp.coo_matrix(mat)
-    n, m = coo.shape
-    key = np.unique(coo.row.astype(np.int64) * max(m, 1) + coo.col.astype(np.int64))
-    rows = key // max(m, 1)
-    indptr = np.zeros(n + 1, dtype=np.int64)
-    np.cumsum(np.bincount(rows, minlength=n), out=indptr[1:])
-    return sp.csr_matrix((np.ones(key.size, dtype=np.int32), (key % max(m, 1)).astype(np.int32), indptr),
-                         shape=(n, m))
+    appears at least once, columns ascending, value 1 (int32).  A canonical
+    input (sorted, no duplicates) is used as it is; others are canonicalised
+    first."""
+    a = sp.csr_matrix(mat)
+    if not a.has_canonical_format:
+        a = a.copy()
+        a.sum_duplicates()             # sorts each row and merges repeats
+    return sp.csr_matrix((np.ones(a.nnz, dtype=np.int32), a.indices, a.indptr), shape=a.shape)
 
 
 def is_pattern_symmetric(mat) -> bool:
@@ -55,9 +54,10 @@ def is_pattern_symmetric(mat) -> bool:
     n, m = mat.shape
     if n != m:
         return False
-    coo = sp.coo_matrix(mat)
-    r, c = coo.row.astype(np.int64), coo.col.astype(np.int64)
-    return np.array_equal(np.unique(r * n + c), np.unique(c * n + r))
+    p = _pattern(mat)
+    t = p.T.tocsr()                    # canonical: the transpose's rows come out sorted
+    t.sort_indices()
+    return np.array_equal(p.indptr, t.indptr) and np.array_equal(p.indices, t.indices)
 
 
 def _runs_of(perm: np.ndarray, target: int) -> np.ndarray:

@@ -24,7 +24,7 @@ namespace spmm {
 
 int boo_matmul_tc(const spmm_boo_dev *A, const float *X, float *Y, int64_t batch, int64_t K, int64_t rg_first,
                   int64_t rg_end, void *ws, size_t ws_bytes, int32_t *status, int32_t wait_us, int32_t flags,
-                  cudaStream_t s);
+                  bool tf32_only, cudaStream_t s);
 size_t boo_tc_workspace(const spmm_boo_dev *A, int64_t batch, int64_t K);
 
 namespace {
@@ -937,7 +937,7 @@ int boo_dispatch<double>(const BooParams<double> &p, int64_t rg0, int64_t rg1, b
 // block) stays on CUDA cores (0.105 vs 0.130 ms).
 bool tc_selected(const spmm_boo_dev *A, int engine) {
     if (A->scalar_type != SPMM_F32 || engine == SPMM_ENGINE_CUDA_CORES) return false;
-    if (engine == SPMM_ENGINE_TENSOR_CORES) return true;
+    if (engine >= SPMM_ENGINE_TENSOR_CORES) return true;
     return A->max_nr <= 64 && A->max_nc <= 64 && A->nb > 0 && A->nnz_c >= 96 * A->nb;
 }
 
@@ -950,11 +950,12 @@ int boo_matmul_impl(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch
         if (tc_selected(A, engine)) {
             const bool v2 = cfg && cfg->version >= 2;
             const int rc = boo_matmul_tc(A, (const float *)X, (float *)Y, batch, K, rg0, rg1, ws, ws_bytes,
-                                         v2 ? cfg->status : nullptr, cfg ? cfg->wait_us : 0, v2 ? cfg->flags : 0, s);
-            if (rc != SPMM_EUNSUPPORTED || engine == SPMM_ENGINE_TENSOR_CORES) return rc;
+                                         v2 ? cfg->status : nullptr, cfg ? cfg->wait_us : 0, v2 ? cfg->flags : 0,
+                                         engine == SPMM_ENGINE_TENSOR_CORES_TF32, s);
+            if (rc != SPMM_EUNSUPPORTED || engine >= SPMM_ENGINE_TENSOR_CORES) return rc;
         }
     } else {
-        if (engine == SPMM_ENGINE_TENSOR_CORES) return SPMM_EUNSUPPORTED;
+        if (engine >= SPMM_ENGINE_TENSOR_CORES) return SPMM_EUNSUPPORTED;
     }
     BooParams<S> p;
     p.rows = A->rows;
@@ -1012,7 +1013,7 @@ int boo_matmul_checked(const spmm_boo_dev *A, const void *X, void *Y, int64_t ba
     if (!A || batch < 0 || K < 0) return SPMM_EINVAL;
     if (cfg && cfg->version != 1 && cfg->version != 2) return SPMM_EINVAL;
     const int engine = cfg ? cfg->engine : SPMM_ENGINE_AUTO;
-    if (engine < SPMM_ENGINE_AUTO || engine > SPMM_ENGINE_TENSOR_CORES) return SPMM_EINVAL;
+    if (engine < SPMM_ENGINE_AUTO || engine > SPMM_ENGINE_TENSOR_CORES_TF32) return SPMM_EINVAL;
     if (cfg && cfg->wait_us < 0) return SPMM_EINVAL;
     if (cfg && cfg->version >= 2 && (cfg->flags & ~SPMM_CFG_EXPIRE_FIRST_WAIT)) return SPMM_EINVAL;
     if (cfg && cfg->version >= 2 && (cfg->flags & SPMM_CFG_EXPIRE_FIRST_WAIT) && cfg->wait_us <= 0)
@@ -1060,7 +1061,7 @@ extern "C" size_t spmm_boo_matmul_workspace_size(const spmm_boo_dev *A, int64_t 
     if (cfg && cfg->version != 1 && cfg->version != 2) return 0;
     if (A->scalar_type == SPMM_F32 && tc_selected(A, cfg ? cfg->engine : SPMM_ENGINE_AUTO)) {
         const size_t w = boo_tc_workspace(A, batch, K);
-        if (w || (cfg && cfg->engine == SPMM_ENGINE_TENSOR_CORES)) return w;
+        if (w || (cfg && cfg->engine >= SPMM_ENGINE_TENSOR_CORES)) return w;
     }
     // remainder-major: the nnz-flat remainder's scratch (16-byte aligned X and Y)
     const bool rem_major = A->rem_nnz > 0 && 2 * A->rem_nnz >= A->total_nnz;

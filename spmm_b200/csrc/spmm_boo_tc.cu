@@ -506,7 +506,7 @@ __device__ __noinline__ void large_group_rows(const TcParams &p, WorkerSmem<NR, 
 
 // One row-group worker (a warpgroup; wt = thread in the worker, tensor-memory
 // lane wt).  `tcol`: first of its 2 NR accumulator + 2 PW panel columns.
-template <int NR, int PW>
+template <int NR, int PW, bool SPLIT>
 __device__ void worker(const TcParams &p, WorkerSmem<NR, PW> &w, Ctl &ctl, uint32_t tcol, int64_t wid,
                        int64_t nworkers, int wt, uint32_t bar) {
     constexpr int KS = PW / 8;
@@ -620,9 +620,13 @@ __device__ void worker(const TcParams &p, WorkerSmem<NR, PW> &w, Ctl &ctl, uint3
                                     v = 0.f;
                                 }
                                 const uint32_t off = a_offset<NR>(r, c);
-                                const float h = tf32_hi(v);
-                                *reinterpret_cast<float *>(tile + off) = h;
-                                *reinterpret_cast<float *>(tile + NR * 128 + off) = v - h;
+                                if constexpr (SPLIT) {
+                                    const float h = tf32_hi(v);
+                                    *reinterpret_cast<float *>(tile + off) = h;
+                                    *reinterpret_cast<float *>(tile + NR * 128 + off) = v - h;
+                                } else {   // one tf32 term: the tensor cores read the value's tf32 part
+                                    *reinterpret_cast<float *>(tile + off) = v;
+                                }
                                 m |= 1u << (c >> 3);
                             }
                         };
@@ -676,12 +680,12 @@ __device__ void worker(const TcParams &p, WorkerSmem<NR, PW> &w, Ctl &ctl, uint3
 #pragma unroll
                             for (int e = 0; e < 8; ++e) {
                                 const float v = x[ks * 8 + e];
-                                const float hv = tf32_hi(v);
+                                const float hv = SPLIT ? tf32_hi(v) : v;
                                 h[e] = __float_as_uint(hv);
                                 l[e] = __float_as_uint(v - hv);
                             }
                             tmem_st8(xslot + lane_addr + ks * 8, h);
-                            tmem_st8(xslot + lane_addr + PW + ks * 8, l);
+                            if constexpr (SPLIT) tmem_st8(xslot + lane_addr + PW + ks * 8, l);
                         }
                     }
                     tmem_wait_st();
@@ -698,8 +702,12 @@ __device__ void worker(const TcParams &p, WorkerSmem<NR, PW> &w, Ctl &ctl, uint3
                             if (kmask & (1u << ks)) {
                                 const uint64_t bh =
                                     bd + (uint64_t)(((ks >> 2) * (2 * NR * 128) + (ks & 3) * 32) >> 4);
-                                mma_tf32_ts(dacc, xslot + ks * 8, bh, idesc2, accum);
-                                mma_tf32_ts(dacc, xslot + PW + ks * 8, bh, idesc1, 1u);
+                                if constexpr (SPLIT) {
+                                    mma_tf32_ts(dacc, xslot + ks * 8, bh, idesc2, accum);
+                                    mma_tf32_ts(dacc, xslot + PW + ks * 8, bh, idesc1, 1u);
+                                } else {
+                                    mma_tf32_ts(dacc, xslot + ks * 8, bh, idesc1, accum);
+                                }
                                 accum = 1;
                             }
                         }
@@ -743,10 +751,11 @@ __device__ void worker(const TcParams &p, WorkerSmem<NR, PW> &w, Ctl &ctl, uint3
                     uint32_t v[16], u[16];
                     const uint32_t a0 = dacc + lane_addr + h * 16;
                     tmem_ld16(a0, v);
-                    tmem_ld16(a0 + NR, u);
+                    if constexpr (SPLIT) tmem_ld16(a0 + NR, u);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int q = 0; q < 16; ++q) acc[h * 16 + q] = __uint_as_float(v[q]) + __uint_as_float(u[q]);
+                    for (int q = 0; q < 16; ++q)
+                        acc[h * 16 + q] = SPLIT ? __uint_as_float(v[q]) + __uint_as_float(u[q]) : __uint_as_float(v[q]);
                 }
                 tc_fence_before();
             }
@@ -774,7 +783,7 @@ __device__ void worker(const TcParams &p, WorkerSmem<NR, PW> &w, Ctl &ctl, uint3
     if (wt == 0 && ncommit > 0) drain_phase(&w.mma_bar, (ncommit - 1) & 1u);
 }
 
-template <int NR, int PW, int NW>
+template <int NR, int PW, int NW, bool SPLIT>
 __global__ void __launch_bounds__(TcShape<NR, PW, NW>::kThreads, 1) boo_tc_kernel(const __grid_constant__ TcParams p) {
     using Shape = TcShape<NR, PW, NW>;
     using W = WorkerSmem<NR, PW>;
@@ -798,7 +807,7 @@ __global__ void __launch_bounds__(TcShape<NR, PW, NW>::kThreads, 1) boo_tc_kerne
     tc_fence_after();
     const uint32_t tmem = ctl.tmem_base;
 
-    worker<NR, PW>(p, ws[wk], ctl, tmem + (uint32_t)(wk * Shape::kWorkerCols), (int64_t)blockIdx.x * NW + wk,
+    worker<NR, PW, SPLIT>(p, ws[wk], ctl, tmem + (uint32_t)(wk * Shape::kWorkerCols), (int64_t)blockIdx.x * NW + wk,
                    (int64_t)gridDim.x * NW, tid & 127, 1u + (uint32_t)wk);
 
     tc_fence_before();
@@ -887,7 +896,7 @@ size_t gather_bytes(const spmm_boo_dev *A, int64_t batch, int64_t K) {
     return (size_t)batch * (size_t)A->n_cg * PW * (size_t)K * sizeof(float) + 256;
 }
 
-template <int NR, int PW, int NW>
+template <int NR, int PW, int NW, bool SPLIT>
 int launch_tc(TcParams p, int64_t batch, void *ws, size_t ws_bytes, cudaStream_t s) {
     using Shape = TcShape<NR, PW, NW>;
     const int sms = sm_count();
@@ -911,7 +920,7 @@ int launch_tc(TcParams p, int64_t batch, void *ws, size_t ws_bytes, cudaStream_t
     if (p.n_tasks > 0x7fffffffLL) return SPMM_EUNSUPPORTED;
     const int64_t ctas = ceil_div(p.n_tasks, (int64_t)NW);
     const int grid = (int)(ctas < sms ? ctas : sms);
-    auto kern = boo_tc_kernel<NR, PW, NW>;
+    auto kern = boo_tc_kernel<NR, PW, NW, SPLIT>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Shape::kSmem);
     p.cg_range = nullptr;
     if (e == cudaSuccess && (p.rg_first != 0 || p.n_rg != p.n_rg_all)) {   // part of the row groups
@@ -956,13 +965,14 @@ size_t boo_tc_workspace(const spmm_boo_dev *A, int64_t batch, int64_t K) {
 // Tensor-core BOO product; SPMM_EUNSUPPORTED when the matrix or K does not
 // fit the kernel (caller falls back to CUDA cores).  `ws`: the caller's
 // scratch, 16-byte aligned, boo_tc_workspace() bytes (SPMM_EWORKSPACE when
-// short).  `status`: the call's status word (null: the process-wide
+// short).  `tf32_only`: one tf32 product per K step instead of the three-term
+// split (SPMM_ENGINE_TENSOR_CORES_TF32, tf32 accuracy).  `status`: the call's status word (null: the process-wide
 // g_tc_status); `wait_us` > 0 bounds the abortable waits to about that many
 // microseconds instead of ~2 s; `flags` & SPMM_CFG_EXPIRE_FIRST_WAIT makes
 // each worker's first wait expire (tests of the timeout path).
 int boo_matmul_tc(const spmm_boo_dev *A, const float *X, float *Y, int64_t batch, int64_t K, int64_t rg_first,
                   int64_t rg_end, void *ws, size_t ws_bytes, int32_t *status, int32_t wait_us, int32_t flags,
-                  cudaStream_t s) {
+                  bool tf32_only, cudaStream_t s) {
     if (!tc_applicable(A, K)) return SPMM_EUNSUPPORTED;
     if ((uintptr_t)X & 15) return SPMM_EUNSUPPORTED;  // 16-byte X loads
     if (!A->col_grp_ptr || !A->col_ids) return SPMM_EINVAL;
@@ -1005,8 +1015,11 @@ int boo_matmul_tc(const spmm_boo_dev *A, const float *X, float *Y, int64_t batch
     }
     p.wait_cycles = wait_us > 0 ? (long long)wait_us * 2000 : kWaitCycles;   // ~2 GHz SM clock
     p.expire_probe = (flags & SPMM_CFG_EXPIRE_FIRST_WAIT) ? 1 : 0;
-    if (A->max_nr <= 32 && A->max_nc <= 32) return launch_tc<32, 32, 4>(p, batch, ws, ws_bytes, s);
-    return launch_tc<64, 64, 2>(p, batch, ws, ws_bytes, s);
+    if (A->max_nr <= 32 && A->max_nc <= 32)
+        return tf32_only ? launch_tc<32, 32, 4, false>(p, batch, ws, ws_bytes, s)
+                         : launch_tc<32, 32, 4, true>(p, batch, ws, ws_bytes, s);
+    return tf32_only ? launch_tc<64, 64, 2, false>(p, batch, ws, ws_bytes, s)
+                     : launch_tc<64, 64, 2, true>(p, batch, ws, ws_bytes, s);
 }
 
 }  // namespace spmm

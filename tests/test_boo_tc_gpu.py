@@ -337,3 +337,26 @@ def test_tc_row_groups_larger_than_blocks(cuda, policy):
     assert np.isfinite(got).all()
     ref = _oracle_y(boo, x.numpy())
     assert_spmm_close(got, ref, abs_bound(mat.indptr, mat.indices, mat.data, x.numpy()), TOL[np.dtype(np.float32)])
+
+
+@pytest.mark.parametrize('name,gen,kw,target,k', [
+    ('fem3d', workloads.fem3d, dict(n=10), 32, 128),
+    ('blockdiag64', workloads.blockdiag, dict(n_blocks=24, b=64), 64, 512),
+])
+def test_tf32_engine_within_tf32_tolerance(cuda, name, gen, kw, target, k):
+    """The opt-in one-term engine ('tensor_cores_tf32'): within 2e-3 (|A||X|)
+    of the oracle -- tf32's accuracy, stated apart from the float32 bar --
+    and deterministic; the three-term engine stays within 1e-5."""
+    mat = gen(**kw)
+    rows, cols = mat.shape
+    boo = S.csr_to_boo(mat, row_labels=np.arange(rows) // target, col_labels=np.arange(cols) // target)
+    x = torch.from_numpy(np.random.default_rng(8).standard_normal((cols, k)).astype(np.float32))
+    dev, xd = boo.to('cuda'), x.cuda()
+    y1 = _product(dev, xd, 'tensor_cores_tf32')
+    assert torch.equal(y1, _product(dev, xd, 'tensor_cores_tf32'))
+    ref = _oracle_y(boo, x.numpy())
+    bound = abs_bound(mat.indptr, mat.indices, mat.data, x.numpy())
+    assert_spmm_close(y1.cpu().numpy(), ref, bound, 2e-3)
+    err = np.abs(y1.cpu().numpy().astype(np.float64) - ref).max()
+    assert err > 0                        # a single tf32 term is not float32-exact
+    _check(mat, boo, x, 'tensor_cores')
