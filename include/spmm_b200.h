@@ -154,6 +154,8 @@ typedef struct {
                              * of its bounded waits expired; read it after the stream */
     int32_t flags;          /* version 2: 0, or SPMM_CFG_EXPIRE_FIRST_WAIT */
     int32_t reserved;       /* version 2: 0 */
+    const void *plan;       /* version 2, optional: this matrix's product plan
+                             * (spmm_boo_plan_build), or NULL */
 } spmm_launch_cfg;
 
 /* spmm_launch_cfg::flags.  SPMM_CFG_EXPIRE_FIRST_WAIT (tests of the timeout
@@ -261,6 +263,23 @@ int spmm_boo_matmul(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch
  * the range is the whole matrix. */
 int spmm_boo_matmul_groups(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch, int64_t K,
                            int64_t rg_begin, int64_t rg_end, const spmm_launch_cfg *cfg, spmm_stream_t stream);
+
+/* ---- BOO product plan (replaces the reference's execution plans,
+ * torch_fast_spdmm/torch_fast_spdmm/boo_plan.py:11-123, which precompute
+ * launch tables once per matrix) --------------------------------------------
+ * Per-matrix tables the product reads through spmm_launch_cfg::plan instead
+ * of recomputing them every call: the first block of every row group, and
+ * for remainder-major matrices whose blocks and tail hold at least 1/64 of the
+ * entries, a row-ordered copy of every entry that one load-balanced pass
+ * multiplies (the layout follows from A's size fields).  The plan is a
+ * caller-owned device buffer of spmm_boo_plan_size() bytes, 256-byte
+ * aligned; building it takes spmm_boo_plan_workspace_size() bytes of scratch
+ * (0 when no row-ordered copy is made).  A plan stays valid while the
+ * matrix's arrays are unchanged; it must not be used with another matrix. */
+size_t spmm_boo_plan_size(const spmm_boo_dev *A);
+size_t spmm_boo_plan_workspace_size(const spmm_boo_dev *A);
+int spmm_boo_plan_build(const spmm_boo_dev *A, void *plan, size_t plan_bytes, void *workspace,
+                        size_t workspace_bytes, spmm_stream_t stream);
 
 /* Bytes of device scratch the BOO product needs in cfg->workspace for these
  * operands and settings: the X panels gathered by column group (tensor-core

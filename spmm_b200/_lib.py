@@ -38,7 +38,8 @@ EXPORTS = ('spmm_status_string', 'spmm_abi_version', 'spmm_boo_build_workspace_s
            'spmm_tc_status', 'spmm_boo_matmul_workspace_size', 'spmm_product_launches',
            'spmm_boo_to_csr_workspace_size', 'spmm_boo_to_csr', 'spmm_pbr_to_csr_workspace_size',
            'spmm_pbr_to_csr', 'spmm_hem_labels', 'spmm_hem_level_slots', 'spmm_hem_hierarchy',
-           'spmm_boo_matmul_groups')
+           'spmm_boo_matmul_groups', 'spmm_boo_plan_size', 'spmm_boo_plan_workspace_size',
+           'spmm_boo_plan_build')
 
 
 class CsrDev(C.Structure):
@@ -73,7 +74,7 @@ class PbrDev(C.Structure):
 class LaunchCfg(C.Structure):
     _fields_ = [('version', C.c_int32), ('slab_features', C.c_int32), ('engine', C.c_int32),
                 ('wait_us', C.c_int32), ('workspace', C.c_void_p), ('workspace_bytes', C.c_uint64),
-                ('status', C.c_void_p), ('flags', C.c_int32), ('reserved', C.c_int32)]
+                ('status', C.c_void_p), ('flags', C.c_int32), ('reserved', C.c_int32), ('plan', C.c_void_p)]
 
 
 SPMM_CFG_EXPIRE_FIRST_WAIT = 1
@@ -83,13 +84,14 @@ ENGINES = {'auto': 0, 'cuda_cores': 1, 'tensor_cores': 2, 'tensor_cores_tf32': 3
 
 
 def launch_cfg(engine: str = 'auto', workspace: int = 0, workspace_bytes: int = 0,
-               slab_features: int = 0, status: int = 0, wait_us: int = 0, flags: int = 0) -> 'LaunchCfg':
+               slab_features: int = 0, status: int = 0, wait_us: int = 0, flags: int = 0,
+               plan: int = 0) -> 'LaunchCfg':
     """spmm_launch_cfg (version 2): engine, remainder slab setting, workspace
     and the call's device status word (0 / None: none)."""
     if engine not in ENGINES:
         raise ValueError(f"engine must be one of {sorted(ENGINES)}, got {engine!r}")
     return LaunchCfg(2, int(slab_features), ENGINES[engine], int(wait_us), workspace or None, workspace_bytes,
-                     status or None, int(flags), 0)
+                     status or None, int(flags), 0, plan or None)
 
 
 class SpmmError(RuntimeError):
@@ -132,6 +134,12 @@ def lib() -> C.CDLL:
         L.spmm_boo_matmul_groups.argtypes = [C.POINTER(BooDev), C.c_void_p, C.c_void_p, C.c_int64, C.c_int64,
                                              C.c_int64, C.c_int64, C.POINTER(LaunchCfg), C.c_void_p]
         L.spmm_boo_matmul_groups.restype = C.c_int
+        for n in ('spmm_boo_plan_size', 'spmm_boo_plan_workspace_size'):
+            getattr(L, n).argtypes = [C.POINTER(BooDev)]
+            getattr(L, n).restype = C.c_size_t
+        L.spmm_boo_plan_build.argtypes = [C.POINTER(BooDev), C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t,
+                                          C.c_void_p]
+        L.spmm_boo_plan_build.restype = C.c_int
         L.spmm_boo_matmul_workspace_size.argtypes = [C.POINTER(BooDev), C.c_int64, C.c_int64,
                                                      C.POINTER(LaunchCfg)]
         L.spmm_boo_matmul_workspace_size.restype = C.c_size_t

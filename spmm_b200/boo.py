@@ -429,6 +429,29 @@ def boo_to_csr(boo_mat) -> sp.csr_matrix:
 # SpMM
 # ---------------------------------------------------------------------------
 
+def product_plan(boo_mat, meta) -> torch.Tensor:
+    """The matrix's product plan on the device of ``meta`` (spmm_boo_plan_build:
+    each row group's first block, and for remainder-major matrices with
+    scattered blocks a row-ordered copy of every entry), built on first use
+    and kept with the staging."""
+    plan = getattr(meta, 'plan', None)
+    if plan is not None:
+        return plan
+    L = _lib.lib()
+    st = boo_mat._dev_struct(meta)
+    n = L.spmm_boo_plan_size(C.byref(st))
+    w = L.spmm_boo_plan_workspace_size(C.byref(st))
+    device = meta.nz_val.device
+    with torch.cuda.device(device):
+        plan = torch.empty(max(n, 256), dtype=torch.uint8, device=device)
+        ws = torch.empty(max(w, 16), dtype=torch.uint8, device=device) if w else None
+        rc = L.spmm_boo_plan_build(C.byref(st), ptr(plan), n, ptr(ws), w, stream_handle(device))
+        _lib.check(rc, 'boo_plan')
+        del ws
+    meta.plan = plan
+    return plan
+
+
 def _run_boo(boo_mat, meta, x: torch.Tensor, engine: str = 'auto', slab_features: int = 0,
              wait_us: int = 0) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
     """(Y, the call's device status word).  One scratch buffer per call from
@@ -443,7 +466,8 @@ def _run_boo(boo_mat, meta, x: torch.Tensor, engine: str = 'auto', slab_features
         if y.numel():
             st = boo_mat._dev_struct(meta)
             L = _lib.lib()
-            cfg = _lib.launch_cfg(engine, slab_features=slab_features, wait_us=wait_us)
+            cfg = _lib.launch_cfg(engine, slab_features=slab_features, wait_us=wait_us,
+                                  plan=product_plan(boo_mat, meta).data_ptr())
             ws_bytes = L.spmm_boo_matmul_workspace_size(C.byref(st), batch, K, C.byref(cfg))
             off = (ws_bytes + 255) // 256 * 256
             buf = torch.empty(off + 256, dtype=torch.uint8, device=device)

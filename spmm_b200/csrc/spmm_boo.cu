@@ -17,6 +17,7 @@
 // 336-396), with fused multiply-adds.
 #include <climits>
 
+#include "plan.cuh"
 #include "ptx.cuh"
 #include "spmm_common.cuh"
 
@@ -24,7 +25,7 @@ namespace spmm {
 
 int boo_matmul_tc(const spmm_boo_dev *A, const float *X, float *Y, int64_t batch, int64_t K, int64_t rg_first,
                   int64_t rg_end, void *ws, size_t ws_bytes, int32_t *status, int32_t wait_us, int32_t flags,
-                  bool tf32_only, cudaStream_t s);
+                  bool tf32_only, const int32_t *rg_blk, cudaStream_t s);
 size_t boo_tc_workspace(const spmm_boo_dev *A, int64_t batch, int64_t K);
 
 namespace {
@@ -56,6 +57,7 @@ struct BooParams {
     int64_t rem_nnz, nch;
     int64_t n_rg, rgs_per_cta;   // block kernel: CTA x takes row groups rg_first + [x * rgs_per_cta, ...)
     int64_t rg_first;            //   up to n_rg (the end of the range, exclusive)
+    const int32_t *rg_blk;       // plan: first block of every row group (null: search blk_row_grp)
     int32_t chunk;
     int32_t *chunk_row;
     S *part;
@@ -155,15 +157,21 @@ boo_spmm_kernel(const BooParams<S> p) {
     // row groups [rg_begin, rg_end); blocks found by one search, then walked
     const int64_t rg_begin = p.rg_first + (int64_t)blockIdx.x * p.rgs_per_cta;
     const int64_t rg_end = rg_begin + p.rgs_per_cta < p.n_rg ? rg_begin + p.rgs_per_cta : p.n_rg;
-    if (warp == 0) {   // 32-way searches by warp 0
+    if (warp == 0 && !p.rg_blk) {   // 32-way searches by warp 0 (no plan)
         const int64_t lo0 = warp_lower_bound(p.blk_row_grp, p.nb, rg_begin, lane);
         if (lane == 0) sm.blk_hi = lo0;
     }
     for (int64_t rg = rg_begin; rg < rg_end; ++rg) {
     __syncthreads();   // the previous group's readers of sm are done
     if (warp == 0) {
-        const int64_t lo = sm.blk_hi;
-        const int64_t hi = group_end(p.blk_row_grp, p.nb, lo, rg, lane);
+        int64_t lo, hi;
+        if (p.rg_blk) {             // the plan's table
+            lo = __ldg(p.rg_blk + rg);
+            hi = __ldg(p.rg_blk + rg + 1);
+        } else {
+            lo = sm.blk_hi;
+            hi = group_end(p.blk_row_grp, p.nb, lo, rg, lane);
+        }
         if (lane == 0) {
             sm.blk_lo = lo;
             sm.blk_hi = hi;
@@ -946,12 +954,15 @@ int boo_matmul_impl(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch
                     int64_t rg1, int engine, const spmm_launch_cfg *cfg, cudaStream_t s) {
     void *ws = cfg ? cfg->workspace : nullptr;
     const size_t ws_bytes = cfg && ws ? (size_t)cfg->workspace_bytes : 0;
+    const uint8_t *plan = cfg && cfg->version >= 2 ? static_cast<const uint8_t *>(cfg->plan) : nullptr;
+    const PlanLayout pl = plan_layout(A);
+    const int32_t *rg_blk = plan ? reinterpret_cast<const int32_t *>(plan + pl.rg_blk) : nullptr;
     if constexpr (sizeof(S) == 4) {
         if (tc_selected(A, engine)) {
             const bool v2 = cfg && cfg->version >= 2;
             const int rc = boo_matmul_tc(A, (const float *)X, (float *)Y, batch, K, rg0, rg1, ws, ws_bytes,
                                          v2 ? cfg->status : nullptr, cfg ? cfg->wait_us : 0, v2 ? cfg->flags : 0,
-                                         engine == SPMM_ENGINE_TENSOR_CORES_TF32, s);
+                                         engine == SPMM_ENGINE_TENSOR_CORES_TF32, rg_blk, s);
             if (rc != SPMM_EUNSUPPORTED || engine >= SPMM_ENGINE_TENSOR_CORES) return rc;
         }
     } else {
@@ -986,6 +997,7 @@ int boo_matmul_impl(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch
     p.rem_nnz = A->rem_nnz;
     p.n_rg = A->n_rg;
     p.rg_first = 0;
+    p.rg_blk = rg_blk;
     p.rgs_per_cta = 1;
     p.nch = 0;
     p.chunk = 0;
@@ -996,6 +1008,18 @@ int boo_matmul_impl(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch
     // then the block kernel adds blocks and tail where a row group has any
     p.skip_rem = A->rem_nnz > 0 && 2 * A->rem_nnz >= A->total_nnz;
     if (p.skip_rem && (rg0 != 0 || rg1 != A->n_rg)) return SPMM_EUNSUPPORTED;   // whole matrix only
+    if (plan && pl.row_view) {
+        // the plan's row-ordered copy of every entry: one load-balanced pass writes Y
+        p.rem_indptr = reinterpret_cast<const int32_t *>(plan + pl.rv_ptr);
+        p.rem_col = reinterpret_cast<const int32_t *>(plan + pl.rv_col);
+        p.rem_val = reinterpret_cast<const S *>(plan + pl.rv_val);
+        p.rem_nnz = pl.entries;
+        const int slab_req = cfg ? cfg->slab_features : 0;
+        if (rem_flat_applies(p, aligned, slab_req) &&
+            (!ws || ws_bytes < rem_flat_workspace(pl.entries, batch, K, sizeof(S))))
+            return SPMM_EWORKSPACE;
+        return rem_dispatch<S>(p, aligned, slab_req, ws, s);
+    }
     if (p.skip_rem) {
         const int slab_req = cfg ? cfg->slab_features : 0;
         if (rem_flat_applies(p, aligned, slab_req) &&
@@ -1063,9 +1087,11 @@ extern "C" size_t spmm_boo_matmul_workspace_size(const spmm_boo_dev *A, int64_t 
         const size_t w = boo_tc_workspace(A, batch, K);
         if (w || (cfg && cfg->engine >= SPMM_ENGINE_TENSOR_CORES)) return w;
     }
-    // remainder-major: the nnz-flat remainder's scratch (16-byte aligned X and Y)
+    // remainder-major: the nnz-flat remainder's scratch (16-byte aligned X and Y),
+    // over the plan's row-ordered copy of every entry when the plan has one
     const bool rem_major = A->rem_nnz > 0 && 2 * A->rem_nnz >= A->total_nnz;
     const size_t elem = A->scalar_type == SPMM_F32 ? 4 : 8;
     if (!rem_major || (cfg && cfg->slab_features < 0) || K % (int64_t)(16 / elem)) return 0;
-    return rem_flat_workspace(A->rem_nnz, batch, K, elem);
+    const bool row_view = cfg && cfg->version >= 2 && cfg->plan && plan_row_view(A);
+    return rem_flat_workspace(row_view ? A->nnz_c + A->rem_nnz + A->tail_nnz : A->rem_nnz, batch, K, elem);
 }

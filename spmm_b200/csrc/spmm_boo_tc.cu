@@ -79,6 +79,7 @@ struct TcParams {
     int64_t rg_first;    // row groups [rg_first, n_rg) are multiplied (n_rg: end of the range)
     int64_t n_rg_all;    // row groups of the matrix
     const unsigned long long *cg_range;   // null, or [min, max] column group the range's blocks use
+    const int32_t *rg_blk;   // plan: first block of every row group (null: search blk_row_grp)
     int32_t dense_nnz;   // blocks with at least this many nonzeros use the tensor cores
     int64_t n_chunks, n_ft, n_tasks;
     int32_t chunk_rgs;
@@ -551,9 +552,10 @@ __device__ void worker(const TcParams &p, WorkerSmem<NR, PW> &w, Ctl &ctl, uint3
         const float *xb = p.X + bt * p.cols * p.K + ft * kFeat + wt;
         float *yb = p.Y + bt * p.rows * p.K + ft * kFeat + wt;
         const float4 *xt = p.Xt + bt * p.n_cg * (PW / 4) * p.K + ft * kFeat + wt;
-        int64_t b = warp_lower_bound(p.blk_row_grp, p.nb, rg0, lane);   // every warp: same answer
+        int64_t b = p.rg_blk ? (int64_t)__ldg(p.rg_blk + rg0)
+                             : warp_lower_bound(p.blk_row_grp, p.nb, rg0, lane);   // every warp: same answer
         for (int64_t rg = rg0; rg < rg1 && ok; ++rg) {
-            const int64_t be = group_end(p.blk_row_grp, p.nb, b, rg, lane);
+            const int64_t be = p.rg_blk ? (int64_t)__ldg(p.rg_blk + rg + 1) : group_end(p.blk_row_grp, p.nb, b, rg, lane);
             const int32_t rbase = __ldg(p.row_grp_ptr + rg);
             const int32_t nr = __ldg(p.row_grp_ptr + rg + 1) - rbase;
             uint32_t started = 0;
@@ -972,7 +974,7 @@ size_t boo_tc_workspace(const spmm_boo_dev *A, int64_t batch, int64_t K) {
 // each worker's first wait expire (tests of the timeout path).
 int boo_matmul_tc(const spmm_boo_dev *A, const float *X, float *Y, int64_t batch, int64_t K, int64_t rg_first,
                   int64_t rg_end, void *ws, size_t ws_bytes, int32_t *status, int32_t wait_us, int32_t flags,
-                  bool tf32_only, cudaStream_t s) {
+                  bool tf32_only, const int32_t *rg_blk, cudaStream_t s) {
     if (!tc_applicable(A, K)) return SPMM_EUNSUPPORTED;
     if ((uintptr_t)X & 15) return SPMM_EUNSUPPORTED;  // 16-byte X loads
     if (!A->col_grp_ptr || !A->col_ids) return SPMM_EINVAL;
@@ -984,6 +986,7 @@ int boo_matmul_tc(const spmm_boo_dev *A, const float *X, float *Y, int64_t batch
     p.n_rg = rg_end;
     p.rg_first = rg_first;
     p.n_rg_all = A->n_rg;
+    p.rg_blk = rg_blk;
     p.rem_nnz = A->rem_nnz;
     p.tail_nnz = A->tail_nnz;
     p.row_grp_ptr = A->row_grp_ptr;

@@ -127,7 +127,8 @@ def host_product(boo_mat, meta, x: torch.Tensor, device: torch.device, engine: s
         y_dev = torch.empty((rows, K), dtype=x.dtype, device=device)
         y_host = torch.empty((rows, K), dtype=x.dtype, pin_memory=True)
         st = boo_mat._dev_struct(meta)
-        cfg = _lib.launch_cfg(engine, slab_features=slab_features)
+        from .boo import product_plan
+        cfg = _lib.launch_cfg(engine, slab_features=slab_features, plan=product_plan(boo_mat, meta).data_ptr())
         ws_bytes = L.spmm_boo_matmul_workspace_size(C.byref(st), 1, K, C.byref(cfg))
         n_chunks = len(pl.rg_bounds) - 1
         off = (ws_bytes + 255) // 256 * 256

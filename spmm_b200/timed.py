@@ -143,7 +143,14 @@ class BOOTimedSpMM(_Timed):
         self._info = dict(diagnostic=self._diag, row_seg=bool(row_seg), nnzflat_fpt=int(nnzflat_fpt),
                           nnzflat_reference=bool(nnzflat_reference), engine=engine)
         L = _lib.lib()
-        self._cfg = _lib.launch_cfg(engine)
+        with torch.cuda.device(self._device):   # the product plan, built once (spmm_boo_plan_build)
+            n, w = L.spmm_boo_plan_size(C.byref(st)), L.spmm_boo_plan_workspace_size(C.byref(st))
+            self._plan = torch.empty(max(n, 256), dtype=torch.uint8, device=self._device)
+            pws = torch.empty(max(w, 16), dtype=torch.uint8, device=self._device)
+            _lib.check(L.spmm_boo_plan_build(C.byref(st), self._plan.data_ptr(), n, pws.data_ptr(), w,
+                                             stream_handle(self._device)), 'BOOTimedSpMM')
+            del pws
+        self._cfg = _lib.launch_cfg(engine, plan=self._plan.data_ptr())
         ws = L.spmm_boo_matmul_workspace_size(C.byref(st), batch, K, C.byref(self._cfg))
         with torch.cuda.device(self._device):
             self._y = torch.empty((batch, rows, K), dtype=torch.float32, device=self._device)

@@ -55,7 +55,7 @@ def test_host_only_entry_points():
 def test_launch_cfg_layout():
     """spmm_launch_cfg as the header lays it out (64-bit): version 2 adds the
     status word after the workspace."""
-    assert C.sizeof(_lib.LaunchCfg) == 48
+    assert C.sizeof(_lib.LaunchCfg) == 56 and _lib.LaunchCfg.plan.offset == 48
     assert _lib.LaunchCfg.workspace.offset == 16 and _lib.LaunchCfg.status.offset == 32
     assert _lib.LaunchCfg.flags.offset == 40
     cfg = _lib.launch_cfg('tensor_cores', wait_us=5)

@@ -308,9 +308,9 @@ def test_tc_row_groups_larger_than_blocks(cuda, policy):
         sl = slice(starts[g], starts[g + 1])
         m = rng.random((sizes[g], cols)) < 0.3
         dense[sl][m] = rng.standard_normal(int(m.sum()))
-    if policy != 'keep':                               # group 2: one entry per block, spilled
-        for q in range(sizes[2]):
-            dense[starts[2] + q, (q * 37) % cols] = rng.standard_normal()
+    if policy != 'keep':                               # group 2: one entry per block, spilled,
+        for k, q in enumerate((5, 33, 40, 64, 70, 90, 99)):   # rows past the tile's 32 included
+            dense[starts[2] + q, 32 * k + (q % 32)] = rng.standard_normal()
     mat = sp.csr_matrix(dense)
     cl = np.arange(cols) // 32
     boo = S.csr_to_boo(mat, row_labels=rl, col_labels=cl, small_block_policy=policy,

@@ -1,0 +1,114 @@
+"""BOO product plans (spmm_boo_plan_build): per-matrix tables the product
+reads instead of recomputing them -- each row group's first block, and for
+remainder-major matrices with scattered blocks a row-ordered copy of every
+entry.  Products with and without a plan agree (bit for bit where the plan
+only replaces a search; within the float tolerance where the row-ordered
+pass sums a row's entries in column order) and match the oracle."""
+
+import ctypes as C
+
+import numpy as np
+import pytest
+import scipy.sparse as sp
+import torch
+
+import spmm_b200 as S
+from oracle import oracle as O
+from spmm_b200 import _lib, workloads
+from spmm_b200._device import stream_handle
+from tests.conftest import TOL, abs_bound, assert_spmm_close
+
+pytestmark = pytest.mark.gpu
+
+
+def _product(dev, x, engine='auto', with_plan=True):
+    L = _lib.lib()
+    st = dev._dev_struct(dev._gpu_meta)
+    plan = S.boo.product_plan(dev, dev._gpu_meta) if with_plan else None
+    cfg = _lib.launch_cfg(engine, plan=plan.data_ptr() if plan is not None else 0)
+    n = L.spmm_boo_matmul_workspace_size(C.byref(st), x.shape[0] if x.dim() == 3 else 1, x.shape[-1],
+                                         C.byref(cfg))
+    ws = torch.empty(max(n, 16), dtype=torch.uint8, device='cuda')
+    if n:
+        cfg.workspace, cfg.workspace_bytes = ws.data_ptr(), n
+    batch = x.shape[0] if x.dim() == 3 else 1
+    y = torch.empty((batch, dev.rows, x.shape[-1]), device='cuda', dtype=x.dtype)
+    rc = L.spmm_boo_matmul(C.byref(st), C.c_void_p(x.data_ptr()), C.c_void_p(y.data_ptr()), batch, x.shape[-1],
+                           C.byref(cfg), stream_handle(x.device))
+    assert rc == 0, _lib.status_string(rc)
+    torch.cuda.synchronize()
+    return y.squeeze(0) if x.dim() == 2 else y
+
+
+def _oracle(boo, xn):
+    d = {f: getattr(boo, f) for f in O.BOO_FIELDS}
+    d.update(rows=boo.rows, cols=boo.cols)
+    return O.boo_matmul(d, xn)
+
+
+@pytest.mark.parametrize('engine', ['tensor_cores', 'cuda_cores'])
+def test_group_table_gives_the_same_bits(cuda, engine):
+    mat = workloads.fem3d(n=9)
+    dev = S.csr_to_boo(mat, cluster='identity', target_nr=32, target_nc=32).to('cuda')
+    x = torch.randn(mat.shape[1], 128, generator=torch.Generator().manual_seed(1)).cuda()
+    assert torch.equal(_product(dev, x, engine, True), _product(dev, x, engine, False))
+
+
+@pytest.mark.parametrize('dtype', [np.float32, np.float64])
+@pytest.mark.parametrize('k', [64, 96])
+def test_row_view_of_scattered_blocks(cuda, dtype, k):
+    """HEM groups on a power-law graph: remainder-major, with a share of the
+    entries in small scattered blocks -- the plan's row-ordered pass."""
+    mat = workloads.powerlaw(n=3000).astype(dtype)
+    boo = S.csr_to_boo(mat, cluster='hem', target_nr=32, target_nc=32)
+    s = boo._sizes
+    assert 2 * s['rem_nnz'] >= s['total_nnz'] and 64 * s['nnz_c'] >= s['total_nnz']
+    dev = boo.to('cuda')
+    L = _lib.lib()
+    st = dev._dev_struct(dev._gpu_meta)
+    entries = s['nnz_c'] + s['rem_nnz'] + s['tail_nnz']
+    sb = np.dtype(dtype).itemsize
+    al = lambda v: (v + 255) // 256 * 256          # noqa: E731
+    assert L.spmm_boo_plan_size(C.byref(st)) == al(4 * (s['n_rg'] + 1)) + al(4 * (s['rows'] + 1)) + \
+        al(4 * entries) + al(sb * entries)
+    tdt = torch.float32 if dtype == np.float32 else torch.float64
+    x = torch.from_numpy(np.random.default_rng(k).standard_normal((2, mat.shape[1], k))).to(tdt)
+    ref = _oracle(boo, x.numpy())
+    bound = abs_bound(mat.indptr, mat.indices, mat.data, x.numpy())
+    with_plan = _product(dev, x.cuda(), 'auto', True).cpu().numpy()
+    without = _product(dev, x.cuda(), 'auto', False).cpu().numpy()
+    assert_spmm_close(with_plan, ref, bound, TOL[np.dtype(dtype)])
+    assert_spmm_close(without, ref, bound, TOL[np.dtype(dtype)])
+    got = S.boo_matmul(dev, x.cuda()).cpu().numpy()          # the public API uses the plan
+    np.testing.assert_array_equal(got, with_plan)
+
+
+def test_plan_without_row_view(cuda):
+    """A remainder-major matrix whose blocks are nearly empty keeps the
+    two-step path; its plan is only the group table."""
+    mat = workloads.uniform(n=4096)
+    boo = S.csr_to_boo(mat, cluster='identity', target_nr=32, target_nc=32)
+    dev = boo.to('cuda')
+    st = dev._dev_struct(dev._gpu_meta)
+    L = _lib.lib()
+    assert L.spmm_boo_plan_size(C.byref(st)) == (4 * (boo.num_row_groups() + 1) + 255) // 256 * 256
+    assert L.spmm_boo_plan_workspace_size(C.byref(st)) == 0
+    x = torch.randn(mat.shape[1], 64, generator=torch.Generator().manual_seed(3)).cuda()
+    assert torch.equal(_product(dev, x, 'auto', True), _product(dev, x, 'auto', False))
+
+
+def test_plan_arguments(cuda):
+    mat = workloads.fem3d(n=4)
+    dev = S.csr_to_boo(mat, cluster='identity', target_nr=32, target_nc=32).to('cuda')
+    st = dev._dev_struct(dev._gpu_meta)
+    L = _lib.lib()
+    n = L.spmm_boo_plan_size(C.byref(st))
+    buf = torch.empty(n + 512, dtype=torch.uint8, device='cuda')
+    assert L.spmm_boo_plan_build(C.byref(st), buf.data_ptr(), n - 1, None, 0, None) == _lib.SPMM_EWORKSPACE
+    assert L.spmm_boo_plan_build(C.byref(st), buf.data_ptr() + 16, n, None, 0, None) == _lib.SPMM_EALIGN
+    assert L.spmm_boo_plan_build(C.byref(st), None, n, None, 0, None) == _lib.SPMM_EINVAL
+    assert L.spmm_boo_plan_build(C.byref(st), buf.data_ptr(), n, None, 0, None) == 0
+    torch.cuda.synchronize()
+    rg_blk = buf[:4 * (dev.num_row_groups() + 1)].view(torch.int32).cpu().numpy()
+    want = np.searchsorted(dev.blk_row_grp, np.arange(dev.num_row_groups() + 1), side='left')
+    np.testing.assert_array_equal(rg_blk, want)
