@@ -54,13 +54,34 @@ def test_group_table_gives_the_same_bits(cuda, engine):
     assert torch.equal(_product(dev, x, engine, True), _product(dev, x, engine, False))
 
 
+def _scattered(n, seed, dtype):
+    """Remainder-major with scattered small blocks, as HEM leaves a power-law
+    graph: 8 random columns per row (the remainder) plus blocks of 6 entries
+    inside 32 x 32 boxes, many of them in one hub row group."""
+    rng = np.random.default_rng(seed)
+    r = np.repeat(np.arange(n), 8)
+    c = rng.integers(0, n, r.size)
+    boxes = [(int(rng.integers(0, n // 32)), int(rng.integers(0, n // 32))) for _ in range(200)]
+    boxes += [(3, int(g)) for g in rng.choice(n // 32, 120, replace=False)]     # the hub group 3
+    br, bc = [], []
+    for gr, gc in boxes:
+        br += list(32 * gr + rng.integers(0, 32, 6))
+        bc += list(32 * gc + rng.integers(0, 32, 6))
+    rr = np.concatenate([r, br])
+    cc = np.concatenate([c, bc])
+    mat = sp.csr_matrix((rng.standard_normal(rr.size), (rr, cc)), shape=(n, n))
+    mat.sum_duplicates()
+    mat.sort_indices()
+    return mat.astype(dtype)
+
+
 @pytest.mark.parametrize('dtype', [np.float32, np.float64])
 @pytest.mark.parametrize('k', [64, 96])
 def test_row_view_of_scattered_blocks(cuda, dtype, k):
-    """HEM groups on a power-law graph: remainder-major, with a share of the
-    entries in small scattered blocks -- the plan's row-ordered pass."""
-    mat = workloads.powerlaw(n=3000).astype(dtype)
-    boo = S.csr_to_boo(mat, cluster='hem', target_nr=32, target_nc=32)
+    """A remainder-major matrix with a share of its entries in scattered
+    blocks (a hub group among them): the plan's row-ordered pass."""
+    mat = _scattered(6400, 5, dtype)
+    boo = S.csr_to_boo(mat, cluster='identity', target_nr=32, target_nc=32, small_block_threshold=4)
     s = boo._sizes
     assert 2 * s['rem_nnz'] >= s['total_nnz'] and 64 * s['nnz_c'] >= s['total_nnz']
     dev = boo.to('cuda')
