@@ -9,8 +9,18 @@
 
 namespace spmm {
 
+// Blocks with at least kDenseNnz nonzeros go through the tensor cores as
+// dense tiles of their own (shared by the product and the plan builder).
+constexpr int kDenseNnz = 48;
+
 struct PlanLayout {
     size_t rg_blk;      // int32[n_rg + 1]: first block of each row group (blocks sorted by group)
+    size_t packed;      // tensor-core matrices (packing): uint8[nb], 1 = the block's entries go
+                        //   through a packed tensor-core tile, not the CUDA cores;
+    size_t rg_slot;     //   int32[n_rg + 1]: first packed slot of each row group;
+    size_t slots;       //   int32[2 nb]: packed slots, block * 16 + quad (4 columns of its group)
+    bool packing;
+    int pw;             //   panel width of the tensor-core product (32 or 64 columns)
     size_t rv_ptr;      // row view (row_view only): int32[rows + 1] row pointers,
     size_t rv_col;      //   int32[entries] columns,
     size_t rv_val;      //   scalar[entries] values: every stored entry, rows ordered by (column, value)
@@ -33,14 +43,32 @@ inline bool plan_row_view(const spmm_boo_dev *A) {
            A->rows <= 0x7fffffffLL;
 }
 
+// Matrices the tensor-core product can take (float32, groups up to 64 x 64):
+// their sparse blocks whose entries lie in at most two 4-column quads are
+// packed, quad by quad, into extra tensor-core tiles (plan_build).
+inline bool plan_packing(const spmm_boo_dev *A) {
+    return A->scalar_type == SPMM_F32 && A->nb > 0 && A->nb < (1ll << 27) && A->max_nr <= 64 &&
+           A->max_nc <= 64;
+}
+
 inline PlanLayout plan_layout(const spmm_boo_dev *A) {
     PlanLayout L{};
     const size_t sb = A->scalar_type == SPMM_F64 ? 8 : 4;
     L.entries = A->nnz_c + A->rem_nnz + A->tail_nnz;
     L.row_view = plan_row_view(A);
+    L.packing = plan_packing(A);
+    L.pw = A->max_nr <= 32 && A->max_nc <= 32 ? 32 : 64;
     size_t off = 0;
     L.rg_blk = off;
     off += plan_align(4 * (size_t)(A->n_rg + 1));
+    if (L.packing) {
+        L.packed = off;
+        off += plan_align((size_t)A->nb);
+        L.rg_slot = off;
+        off += plan_align(4 * (size_t)(A->n_rg + 1));
+        L.slots = off;
+        off += plan_align(8 * (size_t)A->nb);
+    }
     if (L.row_view) {
         L.rv_ptr = off;
         off += plan_align(4 * (size_t)(A->rows + 1));

@@ -25,7 +25,7 @@ namespace spmm {
 
 int boo_matmul_tc(const spmm_boo_dev *A, const float *X, float *Y, int64_t batch, int64_t K, int64_t rg_first,
                   int64_t rg_end, void *ws, size_t ws_bytes, int32_t *status, int32_t wait_us, int32_t flags,
-                  bool tf32_only, const int32_t *rg_blk, cudaStream_t s);
+                  bool tf32_only, const uint8_t *plan, cudaStream_t s);
 size_t boo_tc_workspace(const spmm_boo_dev *A, int64_t batch, int64_t K);
 
 namespace {
@@ -962,7 +962,7 @@ int boo_matmul_impl(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch
             const bool v2 = cfg && cfg->version >= 2;
             const int rc = boo_matmul_tc(A, (const float *)X, (float *)Y, batch, K, rg0, rg1, ws, ws_bytes,
                                          v2 ? cfg->status : nullptr, cfg ? cfg->wait_us : 0, v2 ? cfg->flags : 0,
-                                         engine == SPMM_ENGINE_TENSOR_CORES_TF32, rg_blk, s);
+                                         engine == SPMM_ENGINE_TENSOR_CORES_TF32, plan, s);
             if (rc != SPMM_EUNSUPPORTED || engine >= SPMM_ENGINE_TENSOR_CORES) return rc;
         }
     } else {

@@ -50,7 +50,9 @@
 // flag and stops, outstanding MMAs are drained, tensor memory is released and
 // a status word readable through spmm_tc_status() is set.
 #include <climits>
+#include <type_traits>
 
+#include "plan.cuh"
 #include "ptx.cuh"
 #include "spmm_common.cuh"
 
@@ -63,11 +65,11 @@ __device__ int g_tc_status;
 namespace {
 
 constexpr int kFeat = 128;           // features per task: MMA M, tensor-memory lanes
-// Blocks with at least kDenseNnz nonzeros go through the tensor cores; the
-// others (and the CSR remainder) are summed on CUDA cores.  An M = 128 MMA
-// costs ~50 cycles whatever N is, so a 32 x 32 block needs a few dozen
-// nonzeros before two MMAs per 8 used columns beat per-nonzero FMAs.
-constexpr int kDenseNnz = 48;
+// Blocks with at least kDenseNnz (plan.cuh: 48) nonzeros go through the
+// tensor cores; the others (and the CSR remainder) are summed on CUDA cores,
+// except the ones a plan packs by quad into extra tensor-core tiles.  An M =
+// 128 MMA costs ~50 cycles whatever N is, so a 32 x 32 block needs a few
+// dozen nonzeros before two MMAs per 8 used columns beat per-nonzero FMAs.
 constexpr int kSegs = 32;            // blocks or rows listed per pass
 constexpr int kWin = 3;              // windows of 32 candidate segments loaded at once
 constexpr int kListCap = 512;        // staged (row, column, value) entries per pass
@@ -80,6 +82,8 @@ struct TcParams {
     int64_t n_rg_all;    // row groups of the matrix
     const unsigned long long *cg_range;   // null, or [min, max] column group the range's blocks use
     const int32_t *rg_blk;   // plan: first block of every row group (null: search blk_row_grp)
+    const uint8_t *packed;   // plan (packing): 1 for sparse blocks multiplied in packed tiles
+    const int32_t *rg_slot, *slots;   // plan (packing): each group's packed quad slots
     int32_t dense_nnz;   // blocks with at least this many nonzeros use the tensor cores
     int64_t n_chunks, n_ft, n_tasks;
     int32_t chunk_rgs;
@@ -301,7 +305,7 @@ __device__ __forceinline__ void seg_table(const TcParams &p, WorkerSmem<NR, PW> 
             cb[u] = -1;
             aux[u] = 0;
             if (sc < nblk) {
-                if (t1[u] - t0[u] < p.dense_nnz) {
+                if (t1[u] - t0[u] < p.dense_nnz && !(p.packed && __ldg(p.packed + bs + sc))) {
                     cnt[u] = t1[u] - t0[u];
                     base[u] = t0[u];
                     cb[u] = __ldg(p.col_grp_ptr + t2[u]);
@@ -463,7 +467,7 @@ __device__ __forceinline__ void rare_part(const TcParams &p, WorkerSmem<NR, PW> 
     if (special) {
         for (int64_t b = bs; b < be; ++b) {
             const int32_t k0 = __ldg(p.blk_nz_ptr + b), k1 = __ldg(p.blk_nz_ptr + b + 1);
-            if (k1 - k0 < p.dense_nnz) continue;
+            if (k1 - k0 < p.dense_nnz && !(p.packed && __ldg(p.packed + b))) continue;   // on CUDA cores
             const uint32_t shift = __ldg(p.blk_shift + b), cm = (1u << shift) - 1u;
             const int32_t cbase = __ldg(p.col_grp_ptr + __ldg(p.blk_col_grp + b));
             for (int32_t k = k0; k < k1; ++k) {
@@ -560,78 +564,66 @@ __device__ void worker(const TcParams &p, WorkerSmem<NR, PW> &w, Ctl &ctl, uint3
             const int32_t nr = __ldg(p.row_grp_ptr + rg + 1) - rbase;
             uint32_t started = 0;
             bool special = false, sparse = false;
-            // ---- tensor-core blocks, listed kSegs blocks at a time ----
-            for (int64_t b0 = b; b0 < be && ok; b0 += kSegs) {
-                const int nblk = be - b0 < kSegs ? (int)(be - b0) : kSegs;
-                int nd;
-                {
-                    const int64_t bb = b0 + lane;
-                    int32_t k0 = 0, k1 = 0;
-                    if (lane < nblk) {
-                        k0 = __ldg(p.blk_nz_ptr + bb);
-                        k1 = __ldg(p.blk_nz_ptr + bb + 1);
-                    }
-                    const bool dense = lane < nblk && k1 - k0 >= p.dense_nnz;
-                    const unsigned dm = __ballot_sync(kFullMask, dense);
-                    nd = __popc(dm);
-                    if (wt < 32 && dense) {
-                        const int slot = __popc(dm & ((1u << lane) - 1u));
-                        w.dk0[slot] = k0;
-                        w.dk1[slot] = k1;
-                        w.dcg[slot] = __ldg(p.blk_col_grp + bb);
-                        w.dshift[slot] = __ldg(p.blk_shift + bb);
-                    }
-                }
-                if (nd < nblk) sparse = true;
-                named_bar_sync(bar, 128);
-                uint16_t i1[kNzPre], i2[kNzPre];
-                float v1[kNzPre], v2[kNzPre];
-                if (nd > 0) prefetch(0, i1, v1);
-                for (int i = 0; i < nd; ++i) {
-                    const int t = (int)(ncommit & 1u);
-                    uint8_t *tile = w.tile[t];
-                    // 1. this block's panel: 16-byte loads of the group's columns
+            uint16_t i1[kNzPre], i2[kNzPre];
+            float v1[kNzPre], v2[kNzPre];
+            // One tensor-core tile: dense block i of the listing (ns == 0), or a
+            // packed tile of ns quad slots, listed as (first entry, end, Xt quad
+            // index, shift | quad << 8) in dk0 / dk1 / dcg / dshift.  False on abort.
+            auto tile_step = [&](auto packed_tile, int i, int ns, bool has_next) -> bool {
+                constexpr bool PACKED = decltype(packed_tile)::value;
+                const int t = (int)(ncommit & 1u);
+                uint8_t *tile = w.tile[t];
+                // 1. the panel: 16-byte loads of the tile's quads
+                float x[PW];
+                if constexpr (!PACKED) {
                     const float4 *xq = xt + (int64_t)w.dcg[i] * (PW / 4) * p.K;
-                    float x[PW];
 #pragma unroll
                     for (int q = 0; q < PW / 4; ++q) {
                         const float4 a = __ldg(xq + q * p.K);
                         x[4 * q] = a.x; x[4 * q + 1] = a.y; x[4 * q + 2] = a.z; x[4 * q + 3] = a.w;
                     }
                     // 2. next block's nonzeros
-                    if (i + 1 < nd) prefetch(i + 1, i2, v2);
-                    // 3. zero the tile (its MMAs, two blocks back, are complete) and scatter
-                    {
-                        float4 *z = reinterpret_cast<float4 *>(tile);
+                    if (has_next) prefetch(i + 1, i2, v2);
+                } else {
 #pragma unroll
-                        for (int u = 0; u < WorkerSmem<NR, PW>::kTileBytes / 16 / 128; ++u)
-                            z[wt + 128 * u] = make_float4(0.f, 0.f, 0.f, 0.f);
-                        if (wt == 0) {
-                            w.kmask[t] = 0u;
-                            w.aspecial[t] = 0u;
-                        }
-                        named_bar_sync(bar, 128);
-                        const uint32_t shift = w.dshift[i], cm = (1u << shift) - 1u;
-                        uint32_t m = 0u;
-                        bool asp = false;
-                        auto put = [&](uint32_t idx, float v) {
-                            const uint32_t r = idx >> shift, c = idx & cm;
-                            if (r < (uint32_t)NR && c < (uint32_t)PW) {
-                                if (!finite(v)) {
-                                    asp = true;
-                                    v = 0.f;
-                                }
-                                const uint32_t off = a_offset<NR>(r, c);
-                                if constexpr (SPLIT) {
-                                    const float h = tf32_hi(v);
-                                    *reinterpret_cast<float *>(tile + off) = h;
-                                    *reinterpret_cast<float *>(tile + NR * 128 + off) = v - h;
-                                } else {   // one tf32 term: the tensor cores read the value's tf32 part
-                                    *reinterpret_cast<float *>(tile + off) = v;
-                                }
-                                m |= 1u << (c >> 3);
+                    for (int q = 0; q < PW / 4; ++q) {
+                        const float4 a = q < ns ? __ldg(xt + (int64_t)w.dcg[q] * p.K) : make_float4(0.f, 0.f, 0.f, 0.f);
+                        x[4 * q] = a.x; x[4 * q + 1] = a.y; x[4 * q + 2] = a.z; x[4 * q + 3] = a.w;
+                    }
+                }
+                // 3. zero the tile (its MMAs, two tiles back, are complete) and scatter
+                {
+                    float4 *z = reinterpret_cast<float4 *>(tile);
+#pragma unroll
+                    for (int u = 0; u < WorkerSmem<NR, PW>::kTileBytes / 16 / 128; ++u)
+                        z[wt + 128 * u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (wt == 0) {
+                        w.kmask[t] = 0u;
+                        w.aspecial[t] = 0u;
+                    }
+                    named_bar_sync(bar, 128);
+                    uint32_t m = 0u;
+                    bool asp = false;
+                    auto place = [&](uint32_t r, uint32_t c, float v) {
+                        if (r < (uint32_t)NR && c < (uint32_t)PW) {
+                            if (!finite(v)) {
+                                asp = true;
+                                v = 0.f;
                             }
-                        };
+                            const uint32_t off = a_offset<NR>(r, c);
+                            if constexpr (SPLIT) {
+                                const float h = tf32_hi(v);
+                                *reinterpret_cast<float *>(tile + off) = h;
+                                *reinterpret_cast<float *>(tile + NR * 128 + off) = v - h;
+                            } else {   // one tf32 term: the tensor cores read the value's tf32 part
+                                *reinterpret_cast<float *>(tile + off) = v;
+                            }
+                            m |= 1u << (c >> 3);
+                        }
+                    };
+                    if constexpr (!PACKED) {
+                        const uint32_t shift = w.dshift[i], cm = (1u << shift) - 1u;
+                        auto put = [&](uint32_t idx, float v) { place(idx >> shift, idx & cm, v); };
                         const int32_t k0 = w.dk0[i];
                         const int n = w.dk1[i] - k0;
 #pragma unroll
@@ -651,77 +643,137 @@ __device__ void worker(const TcParams &p, WorkerSmem<NR, PW> &w, Ctl &ctl, uint3
                             for (int u = 0; u < 8; ++u)
                                 if (e0 + 128 * u < n) put(ib[u], vb[u]);
                         }
-                        m = __reduce_or_sync(kFullMask, m);
-                        if (lane == 0 && m) atomicOr(&w.kmask[t], m);
-                        if (__any_sync(kFullMask, asp) && lane == 0) w.aspecial[t] = 1u;
+                    } else {
+                        // slot s's entries in its quad go to columns 4 s .. 4 s + 3
+                        constexpr int TPS = 128 / (PW / 4);   // threads per slot
+                        const int sl = wt / TPS, tt = wt % TPS;
+                        if (sl < ns) {
+                            const uint32_t sh = w.dshift[sl] & 0xFFu, qd = w.dshift[sl] >> 8, cm = (1u << sh) - 1u;
+                            const int32_t e1 = w.dk1[sl];
+                            for (int32_t e = w.dk0[sl] + tt; e < e1; e += TPS) {
+                                const uint32_t idx = __ldg(p.nz_idx + e), c = idx & cm;
+                                if ((c >> 2) == qd) place(idx >> sh, 4u * (uint32_t)sl + (c & 3u), __ldg(p.nz_val + e));
+                            }
+                        }
                     }
-                    // 4. the previous block's MMAs are done: the panel slot is free
-                    if (ncommit > 0 && !(ok = wait_commit(ncommit - 1))) break;
-                    if (ncommit == 0) named_bar_sync(bar, 128);
+                    m = __reduce_or_sync(kFullMask, m);
+                    if (lane == 0 && m) atomicOr(&w.kmask[t], m);
+                    if (__any_sync(kFullMask, asp) && lane == 0) w.aspecial[t] = 1u;
+                }
+                // 4. the previous tile's MMAs are done: the panel slot is free
+                if (ncommit > 0 && !wait_commit(ncommit - 1)) return false;
+                if (ncommit == 0) named_bar_sync(bar, 128);
+                tc_fence_after();
+                const uint32_t kmask = w.kmask[t];
+                // 5. split and store the panel: hi at xslot, lo at xslot + PW
+                // x * 0 is NaN exactly for a non-finite x: one FMA per value
+                // detects them; the rare panel that has one is cleaned
+                float chk = 0.f;
+#pragma unroll
+                for (int ks = 0; ks < KS; ++ks)
+                    if (kmask & (1u << ks))
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) chk = fmaf(x[ks * 8 + e], 0.f, chk);
+                const bool xsp = chk != chk;
+                if (xsp) {
+#pragma unroll
+                    for (int c = 0; c < PW; ++c)
+                        if (!finite(x[c])) x[c] = 0.f;
+                }
+#pragma unroll
+                for (int ks = 0; ks < KS; ++ks) {
+                    if (kmask & (1u << ks)) {
+                        uint32_t h[8], l[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) {
+                            const float v = x[ks * 8 + e];
+                            const float hv = SPLIT ? tf32_hi(v) : v;
+                            h[e] = __float_as_uint(hv);
+                            l[e] = __float_as_uint(v - hv);
+                        }
+                        tmem_st8(xslot + lane_addr + ks * 8, h);
+                        if constexpr (SPLIT) tmem_st8(xslot + lane_addr + PW + ks * 8, l);
+                    }
+                }
+                tmem_wait_st();
+                tc_fence_before();
+                fence_proxy_async_smem();
+                if (bar_or(bar, 128, xsp) || w.aspecial[t]) special = true;
+                // 6. MMAs of the tile, issued by one thread
+                if (wt == 0) {
                     tc_fence_after();
-                    const uint32_t kmask = w.kmask[t];
-                    // 5. split and store the panel: hi at xslot, lo at xslot + PW
-                    // x * 0 is NaN exactly for a non-finite x: one FMA per value
-                    // detects them; the rare panel that has one is cleaned
-                    float chk = 0.f;
-#pragma unroll
-                    for (int ks = 0; ks < KS; ++ks)
-                        if (kmask & (1u << ks))
-#pragma unroll
-                            for (int e = 0; e < 8; ++e) chk = fmaf(x[ks * 8 + e], 0.f, chk);
-                    const bool xsp = chk != chk;
-                    if (xsp) {
-#pragma unroll
-                        for (int c = 0; c < PW; ++c)
-                            if (!finite(x[c])) x[c] = 0.f;
-                    }
+                    const uint64_t bd = b_desc_sw128(smem_u32(tile));
+                    uint32_t accum = started;   // 0: the first MMA of the group overwrites
 #pragma unroll
                     for (int ks = 0; ks < KS; ++ks) {
                         if (kmask & (1u << ks)) {
-                            uint32_t h[8], l[8];
-#pragma unroll
-                            for (int e = 0; e < 8; ++e) {
-                                const float v = x[ks * 8 + e];
-                                const float hv = SPLIT ? tf32_hi(v) : v;
-                                h[e] = __float_as_uint(hv);
-                                l[e] = __float_as_uint(v - hv);
+                            const uint64_t bh = bd + (uint64_t)(((ks >> 2) * (2 * NR * 128) + (ks & 3) * 32) >> 4);
+                            if constexpr (SPLIT) {
+                                mma_tf32_ts(dacc, xslot + ks * 8, bh, idesc2, accum);
+                                mma_tf32_ts(dacc, xslot + PW + ks * 8, bh, idesc1, 1u);
+                            } else {
+                                mma_tf32_ts(dacc, xslot + ks * 8, bh, idesc1, accum);
                             }
-                            tmem_st8(xslot + lane_addr + ks * 8, h);
-                            if constexpr (SPLIT) tmem_st8(xslot + lane_addr + PW + ks * 8, l);
+                            accum = 1;
                         }
                     }
-                    tmem_wait_st();
-                    tc_fence_before();
-                    fence_proxy_async_smem();
-                    if (bar_or(bar, 128, xsp) || w.aspecial[t]) special = true;
-                    // 6. MMAs of the block, issued by one thread
-                    if (wt == 0) {
-                        tc_fence_after();
-                        const uint64_t bd = b_desc_sw128(smem_u32(tile));
-                        uint32_t accum = started;   // 0: the first MMA of the group overwrites
-#pragma unroll
-                        for (int ks = 0; ks < KS; ++ks) {
-                            if (kmask & (1u << ks)) {
-                                const uint64_t bh =
-                                    bd + (uint64_t)(((ks >> 2) * (2 * NR * 128) + (ks & 3) * 32) >> 4);
-                                if constexpr (SPLIT) {
-                                    mma_tf32_ts(dacc, xslot + ks * 8, bh, idesc2, accum);
-                                    mma_tf32_ts(dacc, xslot + PW + ks * 8, bh, idesc1, 1u);
-                                } else {
-                                    mma_tf32_ts(dacc, xslot + ks * 8, bh, idesc1, accum);
-                                }
-                                accum = 1;
-                            }
-                        }
-                        mma_commit(&w.mma_bar);
-                    }
-                    if (kmask) started = 1;   // uniform: every thread read kmask
-                    ++ncommit;
+                    mma_commit(&w.mma_bar);
+                }
+                if (kmask) started = 1;   // uniform: every thread read kmask
+                ++ncommit;
+                if constexpr (!PACKED) {
 #pragma unroll
                     for (int u = 0; u < kNzPre; ++u) {
                         i1[u] = i2[u];
                         v1[u] = v2[u];
                     }
+                }
+                return true;
+            };
+            // ---- dense blocks, listed kSegs blocks at a time ----
+            for (int64_t b0 = b; b0 < be && ok; b0 += kSegs) {
+                const int nblk = be - b0 < kSegs ? (int)(be - b0) : kSegs;
+                int nd;
+                {
+                    const int64_t bb = b0 + lane;
+                    int32_t k0 = 0, k1 = 0;
+                    if (lane < nblk) {
+                        k0 = __ldg(p.blk_nz_ptr + bb);
+                        k1 = __ldg(p.blk_nz_ptr + bb + 1);
+                    }
+                    const bool dense = lane < nblk && k1 - k0 >= p.dense_nnz;
+                    const bool pk = p.packed && lane < nblk && !dense && __ldg(p.packed + bb);
+                    const unsigned dm = __ballot_sync(kFullMask, dense);
+                    nd = __popc(dm);
+                    if (nd + __popc(__ballot_sync(kFullMask, pk)) < nblk) sparse = true;   // CUDA-core blocks
+                    if (wt < 32 && dense) {
+                        const int slot = __popc(dm & ((1u << lane) - 1u));
+                        w.dk0[slot] = k0;
+                        w.dk1[slot] = k1;
+                        w.dcg[slot] = __ldg(p.blk_col_grp + bb);
+                        w.dshift[slot] = __ldg(p.blk_shift + bb);
+                    }
+                }
+                named_bar_sync(bar, 128);
+                if (nd > 0) prefetch(0, i1, v1);
+                for (int i = 0; i < nd && ok; ++i) ok = tile_step(std::false_type{}, i, 0, i + 1 < nd);
+            }
+            // ---- packed tiles: quads of the group's packed sparse blocks ----
+            if (p.rg_slot && ok) {
+                const int32_t s0 = __ldg(p.rg_slot + rg), s1 = __ldg(p.rg_slot + rg + 1);
+                for (int32_t t0 = s0; t0 < s1 && ok; t0 += PW / 4) {
+                    const int ns = s1 - t0 < PW / 4 ? s1 - t0 : PW / 4;
+                    if (wt < ns) {
+                        const int32_t sl = __ldg(p.slots + t0 + wt);
+                        const int64_t bb = sl >> 4;
+                        const uint32_t qd = (uint32_t)(sl & 15);
+                        w.dk0[wt] = __ldg(p.blk_nz_ptr + bb);
+                        w.dk1[wt] = __ldg(p.blk_nz_ptr + bb + 1);
+                        w.dcg[wt] = __ldg(p.blk_col_grp + bb) * (PW / 4) + (int32_t)qd;
+                        w.dshift[wt] = (uint32_t)__ldg(p.blk_shift + bb) | (qd << 8);
+                    }
+                    named_bar_sync(bar, 128);
+                    ok = tile_step(std::true_type{}, 0, ns, false);
                 }
             }
             if (!ok) break;
@@ -974,7 +1026,7 @@ size_t boo_tc_workspace(const spmm_boo_dev *A, int64_t batch, int64_t K) {
 // each worker's first wait expire (tests of the timeout path).
 int boo_matmul_tc(const spmm_boo_dev *A, const float *X, float *Y, int64_t batch, int64_t K, int64_t rg_first,
                   int64_t rg_end, void *ws, size_t ws_bytes, int32_t *status, int32_t wait_us, int32_t flags,
-                  bool tf32_only, const int32_t *rg_blk, cudaStream_t s) {
+                  bool tf32_only, const uint8_t *plan, cudaStream_t s) {
     if (!tc_applicable(A, K)) return SPMM_EUNSUPPORTED;
     if ((uintptr_t)X & 15) return SPMM_EUNSUPPORTED;  // 16-byte X loads
     if (!A->col_grp_ptr || !A->col_ids) return SPMM_EINVAL;
@@ -986,7 +1038,15 @@ int boo_matmul_tc(const spmm_boo_dev *A, const float *X, float *Y, int64_t batch
     p.n_rg = rg_end;
     p.rg_first = rg_first;
     p.n_rg_all = A->n_rg;
-    p.rg_blk = rg_blk;
+    if (plan) {   // the matrix's plan: group table, and packed tiles when built for this panel width
+        const PlanLayout L = plan_layout(A);
+        p.rg_blk = reinterpret_cast<const int32_t *>(plan + L.rg_blk);
+        if (L.packing) {
+            p.packed = plan + L.packed;
+            p.rg_slot = reinterpret_cast<const int32_t *>(plan + L.rg_slot);
+            p.slots = reinterpret_cast<const int32_t *>(plan + L.slots);
+        }
+    }
     p.rem_nnz = A->rem_nnz;
     p.tail_nnz = A->tail_nnz;
     p.row_grp_ptr = A->row_grp_ptr;

@@ -133,3 +133,64 @@ def test_plan_arguments(cuda):
     rg_blk = buf[:4 * (dev.num_row_groups() + 1)].view(torch.int32).cpu().numpy()
     want = np.searchsorted(dev.blk_row_grp, np.arange(dev.num_row_groups() + 1), side='left')
     np.testing.assert_array_equal(rg_blk, want)
+
+
+def _packing_rule(boo):
+    """The plan's packing, restated: sparse blocks (< 48 entries) whose
+    entries lie in one or two 4-column quads with >= 3 entries per quad;
+    slots = (block, quad) in block order, quads ascending."""
+    ptr = np.asarray(boo.blk_nz_ptr, dtype=np.int64)
+    idx = np.asarray(boo.nz_idx).astype(np.int64)
+    shift = np.asarray(boo.blk_shift).astype(np.int64)
+    packed = np.zeros(boo.num_blocks(), dtype=np.uint8)
+    slots = []
+    for b in range(boo.num_blocks()):
+        k0, k1 = ptr[b], ptr[b + 1]
+        if k1 - k0 >= 48:
+            continue
+        quads = np.unique((idx[k0:k1] & ((1 << shift[b]) - 1)) >> 2)
+        if 1 <= quads.size <= 2 and k1 - k0 >= 3 * quads.size:
+            packed[b] = 1
+            slots += [b * 16 + int(q) for q in quads]
+    return packed, np.array(slots, dtype=np.int64)
+
+
+@pytest.mark.parametrize('name,gen,kw,target', [
+    ('fem3d', workloads.fem3d, dict(n=8), 32),
+    ('blockdiag', workloads.blockdiag, dict(n_blocks=12, b=64), 64),
+])
+def test_packed_slots_follow_the_rule(cuda, name, gen, kw, target):
+    mat = gen(**kw)
+    boo = S.csr_to_boo(mat, cluster='identity', target_nr=target, target_nc=target)
+    dev = boo.to('cuda')
+    plan = S.boo.product_plan(dev, dev._gpu_meta).cpu().numpy()
+    s = boo._sizes
+    al = lambda v: (v + 255) // 256 * 256          # noqa: E731
+    off_packed = al(4 * (s['n_rg'] + 1))
+    off_rgslot = off_packed + al(s['nb'])
+    off_slots = off_rgslot + al(4 * (s['n_rg'] + 1))
+    packed = plan[off_packed:off_packed + s['nb']]
+    rg_slot = plan[off_rgslot:off_rgslot + 4 * (s['n_rg'] + 1)].view(np.int32)
+    want_packed, want_slots = _packing_rule(boo)
+    np.testing.assert_array_equal(packed, want_packed)
+    assert rg_slot[-1] == want_slots.size
+    slots = plan[off_slots:off_slots + 4 * want_slots.size].view(np.int32)
+    np.testing.assert_array_equal(slots, want_slots)
+    if name == 'fem3d':
+        assert want_slots.size > 0                  # the mesh's corner blocks are packed
+
+
+@pytest.mark.parametrize('n,k', [(8, 128), (11, 256)])
+def test_packed_tiles_product(cuda, n, k):
+    """Tensor-core product with the plan (corner blocks in packed tiles) and
+    without it (corner blocks on CUDA cores): both within 1e-5 of the oracle."""
+    mat = workloads.fem3d(n=n)
+    boo = S.csr_to_boo(mat, cluster='identity', target_nr=32, target_nc=32)
+    dev = boo.to('cuda')
+    x = torch.from_numpy(np.random.default_rng(n).standard_normal((mat.shape[1], k)).astype(np.float32))
+    ref = _oracle(boo, x.numpy())
+    bound = abs_bound(mat.indptr, mat.indices, mat.data, x.numpy())
+    for with_plan in (True, False):
+        got = _product(dev, x.cuda(), 'tensor_cores', with_plan).cpu().numpy()
+        assert_spmm_close(got, ref, bound, TOL[np.dtype(np.float32)])
+    assert _lib.lib().spmm_tc_status(1) == 0
