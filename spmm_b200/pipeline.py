@@ -34,8 +34,8 @@ from . import _lib
 from ._device import ptr
 
 MIN_X_BYTES = 32 << 20     # below this the copies are short and a plain call is as fast
-CHUNKS = 8                 # row-group chunks per call
-PIECES = 16                # H2D pieces of X per call
+CHUNKS = 16                # row-group chunks per call
+PIECES = 32                # H2D pieces of X per call
 
 
 def _group_max_col(boo_mat) -> np.ndarray:
