@@ -1,5 +1,5 @@
 """Row split and format broadcast over NCCL on two GPUs (one process each),
-against the oracle.  NVLS is switched off (plain NCCL rings) and every
+for BOO and PBR, against the oracle.  NVLS is switched off (plain NCCL rings) and every
 collective has a bounded process-group timeout."""
 
 import os
@@ -57,7 +57,22 @@ def _worker(rank, world, port, q):
         ys = S.boo_matmul(A, slab).cpu().numpy()
         msgs.append(bool(np.all(np.abs(ys - ref[:, rank * 64:(rank + 1) * 64])
                                 <= TOL[np.dtype(np.float32)] * bound[:, rank * 64:(rank + 1) * 64] + 1e-30)))
-        dist.barrier()
+        # PBR: row split over stripes, and the format broadcast for a feature split
+        um = workloads.uniform(n=6000, seed=4)
+        ux = torch.from_numpy(np.random.default_rng(3).standard_normal((6000, 64)).astype(np.float32))
+        ufull = O.pbr_build(um.indptr, um.indices, um.data, 6000, 6000, 8, 8, 1)
+        ufull.update(rows=6000, cols=6000)
+        uref = O.pbr_matmul(ufull, ux.numpy())
+        ubound = abs_bound(um.indptr, um.indices, um.data, ux.numpy())
+        rp = D.RowSplitPBR(um, 8, 8, 1, dev)
+        uxd = D.broadcast_dense(ux.to(dev) if rank == 0 else None, (6000, 64), torch.float32, dev)
+        uy = rp.gather(rp.matmul(uxd)).cpu().numpy()
+        msgs.append(bool(np.all(np.abs(uy - uref) <= TOL[np.dtype(np.float32)] * ubound + 1e-30)))
+        P = S.csr_to_pbr(um, 8, 8, 1).to(dev) if rank == 0 else None
+        P = D.broadcast_pbr(P, dev)
+        py = S.pbr_matmul(P, uxd).cpu().numpy()
+        msgs.append(bool(np.all(np.abs(py - uref) <= TOL[np.dtype(np.float32)] * ubound + 1e-30)))
+        D.barrier()
         dist.destroy_process_group()
         q.put((rank, 'ok' if all(msgs) else f'mismatch {msgs}'))
     except Exception as e:      # noqa: BLE001
