@@ -19,11 +19,12 @@ from .pbr import (BlockFillStats, BlockStripeStats, DataOrder, PBRInfo, PBRMatri
                   pbr_analyze_csr, pbr_batched_matmul_chunkcols_cuda, pbr_batched_matmul_cpu,
                   pbr_batched_matmul_cuda, pbr_batched_matmul_nnzflat_cuda,
                   pbr_batched_matmul_variant_cuda, pbr_info, pbr_matmul, pbr_to_csr)
+from ._lib import SpmmError
 from .timed import BOOTimedSpMM, DirectSpMM, PBRTimedSpMM
 
 __all__ = [
     'csr_to_boo', 'boo_to_csr', 'boo_info', 'boo_matmul', 'boo_arena_bytes', 'BOOInfo',
-    'product_status', 'check_product',
+    'product_status', 'check_product', 'SpmmError',
     'SMALL_BLOCK_POLICIES', 'NZ_ORDERS', 'cluster_axes', 'cluster_axis', 'CLUSTER_METHODS',
     'csr_to_pbr', 'pbr_to_csr', 'pbr_analyze_csr', 'pbr_info', 'PBRInfo', 'BlockFillStats',
     'BlockStripeStats', 'pbr_matmul', 'pbr_batched_matmul_cpu', 'pbr_batched_matmul_cuda',
