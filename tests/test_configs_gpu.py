@@ -1,8 +1,9 @@
 """The five benchmark configurations on the GPU.
 
 Reduced sizes: every format array bit-exact against the oracle, Y within
-tol * (|A||X|) of the oracle's CPU SpMM.  Full sizes (C1, C2, C5): the oracle
-would take minutes, so size-independent properties are checked instead --
+tol * (|A||X|) of the oracle's CPU SpMM.  Full sizes (C1 bit-exact; C2, C3 with
+HEM grouping as configured, C4, C5 by properties): the oracle would take
+minutes, so size-independent properties are checked instead --
 exact agreement of the builder's counts with a host recount, linearity of the
 product, and a float64 recomputation of a random sample of output rows."""
 
@@ -122,3 +123,30 @@ def test_c5_full_size_properties(cuda):
     pbr = S.csr_to_pbr(mat, 8, 8, 4).to('cuda')
     assert pbr.compressed_nnz() + pbr.remainder_nnz() == mat.nnz
     _properties(mat, lambda x: S.pbr_matmul(pbr, x), 64)
+
+
+def test_c3_full_size_hem_properties(cuda):
+    """C3 as the configuration names it: 2 M power-law rows grouped by HEM
+    (labels on the GPU), remainder-major with scattered blocks -- the plan's
+    row-ordered pass.  Also the same matrix with identity grouping."""
+    mat = W.powerlaw()
+    boo = S.csr_to_boo(mat, cluster='hem', target_nr=32, target_nc=32).to('cuda')
+    s = boo._sizes
+    assert boo.compressed_nnz() + boo.remainder_nnz() + boo.tail_nnz() == mat.nnz
+    assert 2 * s['rem_nnz'] >= s['total_nnz'] and s['nnz_c'] > 0
+    counts = np.bincount(boo.row_grp_ptr[1:] - boo.row_grp_ptr[:-1])
+    assert counts.size <= 33                         # groups capped at the target
+    _properties(mat, lambda x: S.boo_matmul(boo, x), 256)
+    ident = S.csr_to_boo(mat, cluster='identity', target_nr=32, target_nc=32).to('cuda')
+    _properties(mat, lambda x: S.boo_matmul(ident, x), 256, seed=3)
+
+
+def test_c4_full_size_properties(cuda):
+    """C4 at full size (4,096 dense 64 x 64 blocks + noise, K = 512) on the
+    tensor cores and on CUDA cores."""
+    mat = W.blockdiag()
+    boo = S.csr_to_boo(mat, cluster='identity', target_nr=64, target_nc=64).to('cuda')
+    assert boo.num_row_groups() == 4096
+    assert boo.compressed_nnz() + boo.remainder_nnz() == mat.nnz
+    _properties(mat, lambda x: S.boo_matmul(boo, x, engine='tensor_cores'), 512)
+    _properties(mat, lambda x: S.boo_matmul(boo, x, engine='cuda_cores'), 512, seed=7)
