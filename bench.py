@@ -547,8 +547,9 @@ def product_launcher(A, fmt, x, y, engine, slab_features=0):
 
 KERNELS = {'tc': 'boo_gather_kernel + boo_tc_kernel (one spmm_boo_matmul call)',
            'cc': 'boo_spmm_kernel',
-           'rem': 'rem_flat_plan_kernel + rem_flat_kernel + rem_flat_fix_kernel + boo_spmm_kernel '
-                  '(one spmm_boo_matmul call)',
+           'rem': 'rem_flat_plan_kernel + rem_flat_kernel + rem_flat_fix_kernel (+ boo_spmm_kernel adding '
+                  'blocks and tail, unless the product plan holds a row-ordered copy of every entry; one '
+                  'spmm_boo_matmul call)',
            'pbr': 'pbr_spmm_kernel'}
 
 
