@@ -3,8 +3,9 @@
 // Replaces the reference's per-block kernel pbr_spmm_vec_kernel /
 // pbr_spmm_zero_idle_kernel plus the concurrent CSR-remainder kernel over a
 // memset Y (torch_fast_spdmm/kernels/pbr_kernel.cu:12-326 and 976-1135,
-// bindings/bindings_kernels.cu:18-123) with ONE launch in which each group of
-// LPR lanes owns an output row:
+// bindings/bindings_kernels.cu:18-123) with ONE launch: for block-major
+// matrices a warp per stripe (pbr_stripe_kernel below), otherwise
+// pbr_spmm_kernel, in which each group of LPR lanes owns an output row:
 //   * the row's stripe (row / block_rows) has a contiguous run of blocks; the
 //     CTA finds the runs of its stripes with one binary search each;
 //   * per block the row's bits are (code >> (r % BR) * BC) & mask; the value
@@ -141,6 +142,116 @@ pbr_spmm_kernel(const PbrParams<S, I> p) {
     }
 }
 
+// Block-major matrices (most entries in blocks, e.g. a mesh stiffness pattern
+// in 8 x 8 blocks): a warp owns one stripe of BR rows and a slab of 32 VEC
+// features, with the BR rows' sums in registers.  Per block the warp loads
+// the block's values once (two coalesced loads, handed out by shuffles at
+// each bit's rank -- the reference's bit-order consumption) and one X row per
+// block column that has a set bit, instead of one X row per nonzero; then
+// the BR rows' remainder entries; every Y element is stored once.
+constexpr int kStripeWarps = 8;
+
+template <typename S, typename I, int VEC, int BR, int BC>
+__global__ void __launch_bounds__(32 * kStripeWarps, 2)
+pbr_stripe_kernel(const PbrParams<S, I> p) {
+    static_assert(BR * BC <= 64 && BR <= 8 && BC <= 8, "block shape");
+    const int lane = threadIdx.x & 31;
+    const int64_t stripe = (int64_t)blockIdx.x * kStripeWarps + (threadIdx.x >> 5);
+    const int64_t row0 = stripe * BR;
+    if (row0 >= p.rows) return;
+    const int64_t f0 = (int64_t)blockIdx.y * 32 * VEC + (int64_t)lane * VEC;
+    const bool fm = f0 < p.K;
+    // the stripe's block run (blocks grouped by stripe, ascending)
+    const int64_t b0 = first_block_of_stripe(p.coords, p.nb, row0);
+    const int64_t b1 = first_block_of_stripe(p.coords, p.nb, row0 + BR);
+    for (int64_t bt = blockIdx.z; bt < p.batch; bt += gridDim.z) {
+        const S *xl = p.X + bt * p.cols * p.K + f0;
+        Frag<S, VEC> acc[BR];
+#pragma unroll
+        for (int r = 0; r < BR; ++r)
+#pragma unroll
+            for (int q = 0; q < VEC; ++q) acc[r].v[q] = S(0);
+        for (int64_t b = b0; b < b1; ++b) {
+            const uint64_t code = __ldg(p.codes + b);
+            const int64_t off = (int64_t)__ldg(p.offsets + b);
+            const int64_t col0 = (int64_t)__ldg(p.coords + 2 * b + 1);
+            const int n = __popcll(code);
+            const S v_lo = lane < n ? __ldg(p.data + off + lane) : S(0);
+            const S v_hi = lane + 32 < n ? __ldg(p.data + off + 32 + lane) : S(0);
+#pragma unroll
+            for (int c = 0; c < BC; ++c) {
+                uint64_t colbits = 0;
+#pragma unroll
+                for (int r = 0; r < BR; ++r) colbits |= code & (1ull << (r * BC + c));
+                if (!colbits || col0 + c >= p.cols) continue;   // uniform across the warp
+                Frag<S, VEC> x;
+                if (fm) x = ldg_frag<S, VEC>(xl + (col0 + c) * p.K);
+#pragma unroll
+                for (int r = 0; r < BR; ++r) {
+                    const int bit = r * BC + c;
+                    if ((code >> bit) & 1ull) {
+                        const int rank = __popcll(code & ((1ull << bit) - 1ull));
+                        const S lo = __shfl_sync(kFullMask, v_lo, rank & 31);
+                        const S hi = __shfl_sync(kFullMask, v_hi, rank & 31);
+                        const S a = rank < 32 ? lo : hi;
+                        if (fm)
+#pragma unroll
+                            for (int q = 0; q < VEC; ++q) acc[r].v[q] = fma(a, x.v[q], acc[r].v[q]);
+                    }
+                }
+            }
+        }
+        S *yb = p.Y + bt * p.rows * p.K + f0;
+#pragma unroll
+        for (int r = 0; r < BR; ++r) {
+            const int64_t row = row0 + r;
+            if (row >= p.rows) break;
+            const int64_t j0 = (int64_t)__ldg(p.rem_indptr + row), j1 = (int64_t)__ldg(p.rem_indptr + row + 1);
+            for (int64_t jb = j0; jb < j1; jb += 32) {
+                const int64_t j = jb + lane;
+                const int64_t cj = j < j1 ? (int64_t)__ldg(p.rem_col + j) : 0;
+                const S aj = j < j1 ? __ldg(p.rem_val + j) : S(0);
+                const int m = j1 - jb < 32 ? (int)(j1 - jb) : 32;
+                int u = 0;
+                for (; u + 2 <= m; u += 2) {
+                    const int64_t c0 = __shfl_sync(kFullMask, cj, u), c1 = __shfl_sync(kFullMask, cj, u + 1);
+                    const S a0 = __shfl_sync(kFullMask, aj, u), a1 = __shfl_sync(kFullMask, aj, u + 1);
+                    if (fm) {
+                        const Frag<S, VEC> x0 = ldg_frag<S, VEC>(xl + c0 * p.K);
+                        const Frag<S, VEC> x1 = ldg_frag<S, VEC>(xl + c1 * p.K);
+#pragma unroll
+                        for (int q = 0; q < VEC; ++q) {
+                            acc[r].v[q] = fma(a0, x0.v[q], acc[r].v[q]);
+                            acc[r].v[q] = fma(a1, x1.v[q], acc[r].v[q]);
+                        }
+                    }
+                }
+                if (u < m) {
+                    const int64_t c0 = __shfl_sync(kFullMask, cj, u);
+                    const S a0 = __shfl_sync(kFullMask, aj, u);
+                    if (fm) {
+                        const Frag<S, VEC> x0 = ldg_frag<S, VEC>(xl + c0 * p.K);
+#pragma unroll
+                        for (int q = 0; q < VEC; ++q) acc[r].v[q] = fma(a0, x0.v[q], acc[r].v[q]);
+                    }
+                }
+            }
+            if (fm) st_frag<S, VEC>(yb + row * p.K, acc[r]);
+        }
+    }
+}
+
+template <typename S, typename I, int VEC, int BR, int BC>
+int launch_pbr_stripe(const PbrParams<S, I> &p, cudaStream_t s) {
+    const int64_t slabs = ceil_div(p.K, 32 * VEC);
+    const int64_t ctas = ceil_div(ceil_div(p.rows, (int64_t)BR), (int64_t)kStripeWarps);
+    if (slabs > 65535 || ctas > 0x7fffffffLL) return SPMM_EUNSUPPORTED;
+    dim3 grid((unsigned)ctas, (unsigned)slabs, (unsigned)(p.batch < 65535 ? p.batch : 65535));
+    pbr_stripe_kernel<S, I, VEC, BR, BC><<<grid, 32 * kStripeWarps, 0, s>>>(p);
+    SPMM_PRODUCT_LAUNCHED();
+    return SPMM_OK;
+}
+
 template <typename S, typename I, int VEC, int VPT, int LPR>
 int launch_pbr(const PbrParams<S, I> &p, cudaStream_t s) {
     constexpr int SLAB = LPR * VPT * VEC;
@@ -154,9 +265,16 @@ int launch_pbr(const PbrParams<S, I> &p, cudaStream_t s) {
 }
 
 template <typename S, typename I>
-int pbr_dispatch(const PbrParams<S, I> &p, bool aligned, cudaStream_t s) {
+int pbr_dispatch(const PbrParams<S, I> &p, bool aligned, bool block_major, cudaStream_t s) {
     const int64_t K = p.K;
     constexpr int V = sizeof(S) == 4 ? 4 : 2;
+    // block-major matrices with at least one full warp slab of features: a
+    // warp per stripe (the reference's launchable shapes 2x2, 4x4, 8x8)
+    if (aligned && K % V == 0 && K >= 32 * V && block_major && p.br == p.bc) {
+        if (p.br == 8) return launch_pbr_stripe<S, I, V, 8, 8>(p, s);
+        if (p.br == 4) return launch_pbr_stripe<S, I, V, 4, 4>(p, s);
+        if (p.br == 2) return launch_pbr_stripe<S, I, V, 2, 2>(p, s);
+    }
     if (aligned && K % V == 0) {
         if (K <= 8 * V) return launch_pbr<S, I, V, 1, 8>(p, s);
         if (K <= 16 * V) return launch_pbr<S, I, V, 1, 16>(p, s);
@@ -190,7 +308,7 @@ int pbr_matmul_impl(const spmm_pbr_dev *A, const void *X, void *Y, int64_t batch
     p.X = (const S *)X;
     p.Y = (S *)Y;
     const uintptr_t mis = ((uintptr_t)X | (uintptr_t)Y) & 15;
-    return pbr_dispatch<S, I>(p, mis == 0, s);
+    return pbr_dispatch<S, I>(p, mis == 0, 2 * A->nnz_c >= A->nnz_c + A->rem_nnz, s);
 }
 
 }  // namespace

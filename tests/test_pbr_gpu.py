@@ -169,3 +169,26 @@ def test_staging_cpu_x_and_errors(cuda):
     pbr.to('cpu')
     assert pbr._gpu_meta is None
     torch.testing.assert_close(S.pbr_matmul(pbr, x), y_cpu, rtol=0, atol=0)
+
+
+@pytest.mark.parametrize('dtype', [np.float32, np.float64])
+@pytest.mark.parametrize('bs', [8, 4, 2])
+@pytest.mark.parametrize('k', [128, 192, 256])
+def test_block_major_stripe_path(cuda, dtype, bs, k):
+    """Block-major matrices (most entries in blocks: a mesh stiffness pattern)
+    take the warp-per-stripe kernel: every shape the reference launches, a
+    partial last feature slab (K = 192), a batch of two, a partial last
+    stripe (rows not a multiple of the block size) and rows with remainder
+    entries next to blocks."""
+    from spmm_b200 import workloads
+    mat = workloads.fem3d(n=7).astype(dtype)[:1027]          # 1027 rows: a partial last stripe
+    mat = sp.csr_matrix(mat)
+    extra = sp.random(1027, mat.shape[1], density=0.002, format='csr', random_state=bs, dtype=dtype)
+    mat = (mat + extra).tocsr()
+    mat.sum_duplicates()
+    mat.sort_indices()
+    pbr = S.csr_to_pbr(mat, bs, bs, 4)
+    assert 2 * pbr.compressed_nnz() >= pbr.total_nnz and pbr.remainder_nnz() > 0
+    tdt = torch.float32 if dtype == np.float32 else torch.float64
+    x = torch.from_numpy(np.random.default_rng(k + bs).standard_normal((2, mat.shape[1], k))).to(tdt)
+    _check_product(mat, pbr.to('cuda'), x.cuda())
