@@ -23,7 +23,8 @@ def _groups_call(dev, x, y, rg0, rg1, engine):
     L = _lib.lib()
     st = dev._dev_struct(dev._gpu_meta)
     K = x.shape[-1]
-    cfg = _lib.launch_cfg(engine)
+    plan = S.boo.product_plan(dev, dev._gpu_meta)      # as the whole-matrix call through the API
+    cfg = _lib.launch_cfg(engine, plan=plan.data_ptr())
     n = L.spmm_boo_matmul_workspace_size(C.byref(st), 1, K, C.byref(cfg))
     ws = torch.empty(max(n, 16), dtype=torch.uint8, device='cuda')
     if n:
