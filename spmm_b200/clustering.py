@@ -68,7 +68,13 @@ def _runs_of(perm: np.ndarray, target: int) -> np.ndarray:
 
 
 def _dense_rank(labels: np.ndarray) -> np.ndarray:
-    """Labels renumbered 0, 1, ... in ascending label order."""
+    """Labels renumbered 0, 1, ... in ascending label order (labels are
+    nonnegative; a presence count when they are bounded by the member count,
+    as every method's are, else a sort)."""
+    if labels.size and 0 <= labels.min() and labels.max() < 4 * labels.size:
+        present = np.bincount(labels, minlength=1) > 0
+        rank = np.cumsum(present) - 1
+        return rank[labels].astype(np.int64)
     u = np.unique(labels)
     return np.searchsorted(u, labels).astype(np.int64)
 
@@ -86,6 +92,9 @@ def _enforce_caps(labels: np.ndarray, row_nnz: np.ndarray, max_size: Optional[in
     """
     if max_size is None and max_nnz is None:
         return labels
+    if max_nnz is None and labels.size and labels.max() < 4 * labels.size \
+            and np.bincount(labels).max() <= max_size:
+        return labels                                  # no group over the size cap
     n = labels.size
     order = np.lexsort((np.arange(n), labels))          # by group, members ascending
     g = labels[order]
@@ -117,6 +126,30 @@ def _enforce_caps(labels: np.ndarray, row_nnz: np.ndarray, max_size: Optional[in
     out = np.empty(n, dtype=np.int64)
     out[order] = np.repeat(first, glen) + piece
     return out
+
+
+_COUNT_METHODS = ('identity', 'random', 'degree')
+
+
+def _axis_nnz(csr: sp.csr_matrix) -> Tuple[np.ndarray, np.ndarray]:
+    """Distinct nonzero columns per row and distinct nonzero rows per column."""
+    a = csr if csr.has_canonical_format else _pattern(csr)
+    return np.diff(a.indptr), np.bincount(a.indices, minlength=a.shape[1])
+
+
+def _count_labels(method: str, row_nnz: np.ndarray, target: int, max_size: Optional[int],
+                  max_nnz: Optional[int], seed: int) -> np.ndarray:
+    """Labels of the methods that need only the members' nonzero counts."""
+    n = row_nnz.size
+    if n == 0:
+        return np.zeros(0, dtype=np.int32)
+    if method == 'identity':
+        labels = np.arange(n, dtype=np.int64) // max(target, 1)
+    elif method == 'random':
+        labels = _runs_of(np.random.default_rng(seed).permutation(n), target)
+    else:
+        labels = _runs_of(np.argsort(row_nnz, kind='stable'), target)
+    return _dense_rank(_enforce_caps(labels, row_nnz, max_size, max_nnz)).astype(np.int32)
 
 
 def hem_labels_gpu(pat: sp.csr_matrix, target: int, max_size: Optional[int], max_nnz: Optional[int],
@@ -179,6 +212,8 @@ def cluster_axis(mat, method: str = 'hem', target: int = 32, max_size: Optional[
     if method == 'metis':
         raise ImportError("cluster='metis' requires pymetis, which is not installed; "
                           'no HEM fallback is performed')
+    if method in _COUNT_METHODS:
+        return _count_labels(method, _axis_nnz(sp.csr_matrix(mat))[0], target, max_size, max_nnz, seed)
     pat = _pattern(mat)
     n = pat.shape[0]
     if n == 0:
@@ -186,13 +221,7 @@ def cluster_axis(mat, method: str = 'hem', target: int = 32, max_size: Optional[
             hem_hierarchy.append(np.zeros(0, dtype=np.int64))
         return np.zeros(0, dtype=np.int32)
     row_nnz = np.diff(pat.indptr)
-    if method == 'identity':
-        labels = np.arange(n, dtype=np.int64) // max(target, 1)
-    elif method == 'random':
-        labels = _runs_of(np.random.default_rng(seed).permutation(n), target)
-    elif method == 'degree':
-        labels = _runs_of(np.argsort(row_nnz, kind='stable'), target)
-    elif method == 'rcm':
+    if method == 'rcm':
         if pat.shape[0] != pat.shape[1]:
             raise ValueError("cluster method 'rcm' requires a square matrix")
         from scipy.sparse.csgraph import reverse_cuthill_mckee
@@ -216,6 +245,15 @@ def cluster_axes(mat, method: str = 'hem', target_nr: int = 32, target_nc: int =
     otherwise rows and columns (the transpose's rows) are clustered apart.
     ``symmetric`` overrides the detection."""
     csr = sp.csr_matrix(mat)
+    if method in _COUNT_METHODS:
+        # These labels depend on each axis's member count and nonzero counts
+        # only: a symmetric pattern gives equal row and column counts, so the
+        # columns' own labels equal the rows' and no symmetry test is needed.
+        row_nnz, col_nnz = _axis_nnz(csr)
+        rows = _count_labels(method, row_nnz, target_nr, max_nr, max_block_nnz, seed)
+        if symmetric:
+            return rows, rows.copy()
+        return rows, _count_labels(method, col_nnz, target_nc, max_nc, max_block_nnz, seed)
     if symmetric is None:
         symmetric = target_nr == target_nc and is_pattern_symmetric(csr)
     common = dict(method=method, max_nnz=max_block_nnz, seed=seed, hub_degree=hub_degree, topk=topk,

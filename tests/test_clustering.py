@@ -101,6 +101,32 @@ def test_caps_respected(method):
     assert np.all((nnz <= 200) | (counts == 1))
 
 
+@pytest.mark.parametrize('method', ['identity', 'random', 'degree'])
+@pytest.mark.parametrize('max_nnz', [None, 40])
+def test_count_methods_need_no_symmetry_test(method, max_nnz):
+    """identity / random / degree label each axis from its own counts; on a
+    symmetric pattern that equals reusing the row labels (the reference's
+    symmetric branch), also for an input with repeated entries."""
+    rng = np.random.default_rng(5)
+    r, c = rng.integers(0, 200, 1500), rng.integers(0, 200, 1500)
+    rows, cols = np.r_[r, c, r[:100]], np.r_[c, r, c[:100]]       # 100 entries repeated
+    order = np.argsort(rows, kind='stable')
+    a = sp.csr_matrix((np.ones(rows.size), cols[order], np.r_[0, np.cumsum(np.bincount(rows, minlength=200))]),
+                      shape=(200, 200))
+    assert not a.has_canonical_format
+    kw = dict(method=method, target_nr=16, target_nc=16, max_nr=16, max_nc=16, max_block_nnz=max_nnz)
+    rl, cl = cluster_axes(a, **kw)
+    sr, sc = cluster_axes(a, symmetric=True, **kw)
+    assert np.array_equal(rl, sr) and np.array_equal(cl, sc)
+    pat = O.binary_pattern(a)
+    want = cluster_axis(pat, method=method, target=16, max_size=16, max_nnz=max_nnz)
+    assert np.array_equal(rl, want)
+    t = sp.random(90, 150, density=0.05, format='csr', random_state=2)
+    tr, tc = cluster_axes(t, **kw)
+    assert np.array_equal(tc, cluster_axis(t.T.tocsr(), method=method, target=16, max_size=16, max_nnz=max_nnz))
+    assert tr.size == 90 and tc.size == 150
+
+
 def test_missing_backends_do_not_fall_back():
     a = sp.eye(10, format='csr')
     for m in ('graclus', 'metis'):

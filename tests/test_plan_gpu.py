@@ -116,9 +116,10 @@ def test_row_view_of_scattered_blocks(cuda, dtype, k):
 
 
 def test_plan_without_row_view(cuda):
-    """A remainder-major matrix whose blocks are nearly empty keeps the
-    two-step path; its plan is only the group table."""
-    mat = workloads.uniform(n=4096)
+    """A remainder-major matrix whose blocks hold under 1/64 of its entries
+    (1,974 of 131,072 here) keeps the two-step path; its plan is the group
+    table and the packing arrays, and the product is the plan-less one."""
+    mat = workloads.uniform(n=16384)
     boo = S.csr_to_boo(mat, cluster='identity', target_nr=32, target_nc=32)
     dev = boo.to('cuda')
     st = dev._dev_struct(dev._gpu_meta)
