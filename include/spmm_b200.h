@@ -10,8 +10,12 @@
  *   - Ownership: the caller owns every buffer (inputs, outputs, workspace).
  *     Device memory the library allocates itself, all of it named here:
  *       * spmm_hem_labels / spmm_hem_hierarchy take their per-level scratch
- *         from the stream-ordered allocator (cudaMallocAsync / cudaFreeAsync)
- *         and release it before returning;
+ *         from the device's default stream-ordered pool (cudaMallocAsync /
+ *         cudaFreeAsync) and release it before returning; while they run the
+ *         pool's release threshold is raised so freed scratch stays mapped
+ *         between levels, and on return the threshold is restored and the
+ *         pool trimmed to it (other users of that pool see the raised
+ *         threshold meanwhile);
  *       * spmm_boo_build_noalloc uses a fixed 32 MiB array compiled into the
  *         library (one per device that loads it, held until exit);
  *     the builders, products and conversions allocate nothing: their scratch

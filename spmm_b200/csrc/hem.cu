@@ -122,22 +122,24 @@ __global__ void transpose_kernel(const int64_t *__restrict__ ptr, const int32_t 
         }
 }
 
-// Warp per row i of [r0, r1): every incidence (i, j) through a kept column as
-// key (i - r0) << jb | j; j == i becomes the all-ones sentinel (sorts last).
+// Warp per listed row b (row i = list[b]): every incidence (i, j) through a
+// kept column as key b << jb | j at start[b] - start[0] on; j == i becomes the
+// all-ones sentinel (sorts last).
 __global__ void gen_pairs_kernel(const int64_t *__restrict__ ptr, const int32_t *__restrict__ idx,
                                  const int64_t *__restrict__ tptr, const int32_t *__restrict__ trow,
-                                 const int64_t *__restrict__ pstart, int64_t r0, int64_t r1, int jb,
-                                 uint64_t sentinel, uint64_t *__restrict__ keys) {
+                                 const int64_t *__restrict__ list, const int64_t *__restrict__ start, int64_t rows,
+                                 int jb, uint64_t sentinel, uint64_t *__restrict__ keys) {
     const int lane = threadIdx.x & 31;
     const int64_t nw = (int64_t)gridDim.x * (blockDim.x / 32);
-    for (int64_t i = r0 + ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32; i < r1; i += nw) {
-        int64_t o = pstart[i] - pstart[r0];
+    for (int64_t b = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32; b < rows; b += nw) {
+        const int64_t i = list[b];
+        int64_t o = start[b] - start[0];
         for (int64_t k = ptr[i]; k < ptr[i + 1]; ++k) {
             const int32_t c = idx[k];
             const int64_t t0 = tptr[c], t1 = tptr[c + 1];
             for (int64_t t = t0 + lane; t < t1; t += 32) {
                 const int64_t j = trow[t];
-                keys[o + (t - t0)] = j == i ? sentinel : ((uint64_t)(i - r0) << jb) | (uint64_t)j;
+                keys[o + (t - t0)] = j == i ? sentinel : ((uint64_t)b << jb) | (uint64_t)j;
             }
             o += t1 - t0;
         }
@@ -183,14 +185,14 @@ __global__ void topk_flags_kernel(const uint64_t *__restrict__ keys, int64_t n, 
 }
 
 __global__ void topk_emit_kernel(const uint64_t *__restrict__ keys, int64_t n, const int64_t *__restrict__ flag,
-                                 const int64_t *__restrict__ pos, int64_t r0, int jb, int wb, int64_t ebase,
-                                 uint64_t *__restrict__ ekey, uint32_t *__restrict__ ew) {
+                                 const int64_t *__restrict__ pos, const int64_t *__restrict__ list, int jb, int wb,
+                                 int64_t ebase, uint64_t *__restrict__ ekey, uint32_t *__restrict__ ew) {
     const int sh = wb + jb;
     const uint64_t wmax = (1ull << wb) - 1ull, jm = (1ull << jb) - 1ull;
     for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < n; k += (int64_t)gridDim.x * blockDim.x) {
         if (!flag[k]) continue;
         const uint64_t key = keys[k];
-        const uint64_t i = (key >> sh) + (uint64_t)r0, j = key & jm;
+        const uint64_t i = (uint64_t)list[key >> sh], j = key & jm;
         const uint32_t w = (uint32_t)(wmax - ((key >> jb) & wmax));
         const int64_t o = ebase + 2 * pos[k];
         ekey[o] = (i << jb) | j;   // both directions; equal pairs collapse after the sort
@@ -227,6 +229,50 @@ struct Caps {
     }
 };
 
+// Edge order of the pick: (w desc, pair hash desc, column asc); c < 0 is "none".
+__device__ __forceinline__ bool better_edge(uint32_t w, uint64_t h, int64_t c, uint32_t bw, uint64_t bh, int64_t bc) {
+    return c >= 0 && (bc < 0 || w > bw || (w == bw && (h > bh || (h == bh && c < bc))));
+}
+
+// This thread's best over the edges [e0, e1) of vertex r, stepping by `step`.
+__device__ __forceinline__ void best_over(const int32_t *__restrict__ gcol, const uint32_t *__restrict__ gw,
+                                          int64_t r, int64_t e0, int64_t e1, int64_t step,
+                                          const uint8_t *__restrict__ active, const int64_t *__restrict__ size,
+                                          const int64_t *__restrict__ nnz, const Caps &caps, int feasible_first,
+                                          uint32_t &bw, uint64_t &bh, int64_t &bc) {
+    for (int64_t e = e0; e < e1; e += step) {
+        const int64_t c = gcol[e];
+        if (!active[c] || (feasible_first && !caps.ok(size, nnz, r, c))) continue;
+        const uint32_t w = gw[e];
+        const uint64_t h = pair_hash(r, c);
+        if (better_edge(w, h, c, bw, bh, bc)) {
+            bw = w;
+            bh = h;
+            bc = c;
+        }
+    }
+}
+
+__device__ __forceinline__ void warp_best(uint32_t &bw, uint64_t &bh, int64_t &bc) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const uint32_t ow = __shfl_xor_sync(kFullMask, bw, o);
+        const uint64_t oh = __shfl_xor_sync(kFullMask, bh, o);
+        const int64_t oc = __shfl_xor_sync(kFullMask, bc, o);
+        if (better_edge(ow, oh, oc, bw, bh, bc)) {
+            bw = ow;
+            bh = oh;
+            bc = oc;
+        }
+    }
+}
+
+// Vertices of more than kHeavyEdges edges (vertices that many rows keep among
+// their top k) are picked by a CTA each (best_heavy_kernel); a warp per
+// vertex takes the rest.
+constexpr int64_t kHeavyEdges = 4096;
+constexpr int kHeavyThreads = 512;
+
 // Warp per vertex: its best live edge by (w desc, hash desc, column asc).
 __global__ void best_kernel(const unsigned long long *__restrict__ gptr, const int32_t *__restrict__ gcol,
                             const uint32_t *__restrict__ gw, int64_t n, const uint8_t *__restrict__ active,
@@ -235,34 +281,57 @@ __global__ void best_kernel(const unsigned long long *__restrict__ gptr, const i
     const int lane = threadIdx.x & 31;
     const int64_t nw = (int64_t)gridDim.x * (blockDim.x / 32);
     for (int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32; r < n; r += nw) {
+        const int64_t e0 = (int64_t)gptr[r], e1 = (int64_t)gptr[r + 1];
+        if (e1 - e0 > kHeavyEdges) continue;   // best_heavy_kernel's vertex
         uint32_t bw = 0;
         uint64_t bh = 0;
         int64_t bc = -1;
-        if (active[r]) {
-            for (int64_t e = (int64_t)gptr[r] + lane; e < (int64_t)gptr[r + 1]; e += 32) {
-                const int64_t c = gcol[e];
-                if (!active[c] || (feasible_first && !caps.ok(size, nnz, r, c))) continue;
-                const uint32_t w = gw[e];
-                const uint64_t h = pair_hash(r, c);
-                if (bc < 0 || w > bw || (w == bw && (h > bh || (h == bh && c < bc)))) {
-                    bw = w;
-                    bh = h;
-                    bc = c;
-                }
-            }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const uint32_t ow = __shfl_xor_sync(kFullMask, bw, o);
-            const uint64_t oh = __shfl_xor_sync(kFullMask, bh, o);
-            const int64_t oc = __shfl_xor_sync(kFullMask, bc, o);
-            if (oc >= 0 && (bc < 0 || ow > bw || (ow == bw && (oh > bh || (oh == bh && oc < bc))))) {
-                bw = ow;
-                bh = oh;
-                bc = oc;
-            }
-        }
+        if (active[r]) best_over(gcol, gw, r, e0 + lane, e1, 32, active, size, nnz, caps, feasible_first, bw, bh, bc);
+        warp_best(bw, bh, bc);
         if (lane == 0) best[r] = bc;
+    }
+}
+
+// Vertices of the level graph with more than kHeavyEdges edges, in any order.
+__global__ void heavy_list_kernel(const unsigned long long *__restrict__ gptr, int64_t n,
+                                  unsigned long long *__restrict__ count, int64_t *__restrict__ list) {
+    for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < n; r += (int64_t)gridDim.x * blockDim.x)
+        if ((int64_t)(gptr[r + 1] - gptr[r]) > kHeavyEdges) list[atomicAdd(count, 1ull)] = r;
+}
+
+// CTA per heavy vertex: the same pick as best_kernel.
+__global__ void __launch_bounds__(kHeavyThreads) best_heavy_kernel(
+    const unsigned long long *__restrict__ gptr, const int32_t *__restrict__ gcol, const uint32_t *__restrict__ gw,
+    const int64_t *__restrict__ list, int64_t n_heavy, const uint8_t *__restrict__ active,
+    const int64_t *__restrict__ size, const int64_t *__restrict__ nnz, Caps caps, int feasible_first,
+    int64_t *__restrict__ best) {
+    __shared__ uint32_t sw[kHeavyThreads / 32];
+    __shared__ uint64_t sh[kHeavyThreads / 32];
+    __shared__ int64_t sc[kHeavyThreads / 32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int64_t v = blockIdx.x; v < n_heavy; v += gridDim.x) {
+        const int64_t r = list[v];
+        uint32_t bw = 0;
+        uint64_t bh = 0;
+        int64_t bc = -1;
+        if (active[r])
+            best_over(gcol, gw, r, (int64_t)gptr[r] + threadIdx.x, (int64_t)gptr[r + 1], kHeavyThreads, active, size,
+                      nnz, caps, feasible_first, bw, bh, bc);
+        warp_best(bw, bh, bc);
+        __syncthreads();   // the previous vertex's reduction has been read
+        if (lane == 0) {
+            sw[warp] = bw;
+            sh[warp] = bh;
+            sc[warp] = bc;
+        }
+        __syncthreads();
+        if (warp == 0) {
+            bw = lane < kHeavyThreads / 32 ? sw[lane] : 0u;
+            bh = lane < kHeavyThreads / 32 ? sh[lane] : 0ull;
+            bc = lane < kHeavyThreads / 32 ? sc[lane] : -1;
+            warp_best(bw, bh, bc);
+            if (lane == 0) best[r] = bc;
+        }
     }
 }
 
@@ -288,50 +357,101 @@ __global__ void root_flags_kernel(const int64_t *__restrict__ mate, int64_t n, i
         flag[r] = (mate[r] >= 0 && mate[r] < r) ? 0 : 1;
 }
 
-// new_id of every vertex; sizes / nnz summed into the new rows; the new
-// pattern's row lengths (union of the pair's sorted columns).
+// lower_bound of x in the sorted run a[0, n).
+__device__ __forceinline__ int64_t lower_bound_run(const int32_t *__restrict__ a, int64_t n, int32_t x) {
+    int64_t lo = 0, hi = n;
+    while (lo < hi) {
+        const int64_t mid = (lo + hi) >> 1;
+        if (a[mid] < x) lo = mid + 1;
+        else hi = mid;
+    }
+    return lo;
+}
+
+// Warp per vertex: new_id of every vertex; sizes / nnz summed into the new
+// rows; the new pattern's row lengths (a matched pair: |A u B| = |A| + |B|
+// minus the entries of B found in A, one binary search per entry of B).
 __global__ void contract_kernel(const int64_t *__restrict__ mate, int64_t n, const int64_t *__restrict__ rank,
                                 const int64_t *__restrict__ size, const int64_t *__restrict__ nnz,
                                 const int64_t *__restrict__ ptr, const int32_t *__restrict__ idx,
                                 int64_t *__restrict__ new_id, unsigned long long *__restrict__ nsize,
                                 unsigned long long *__restrict__ nnnz, int64_t *__restrict__ nlen) {
-    for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < n; r += (int64_t)gridDim.x * blockDim.x) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = (int64_t)gridDim.x * (blockDim.x / 32);
+    for (int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32; r < n; r += nw) {
         const int64_t m = mate[r];
         const int64_t root = (m >= 0 && m < r) ? m : r;
         const int64_t id = rank[root];
-        new_id[r] = id;
-        atomicAdd(nsize + id, (unsigned long long)size[r]);
-        atomicAdd(nnnz + id, (unsigned long long)nnz[r]);
-        if (root != r) continue;
-        int64_t len = ptr[r + 1] - ptr[r];
-        if (m > r) {   // |A u B| of two sorted lists
-            int64_t a = ptr[r], ae = ptr[r + 1], b = ptr[m], be = ptr[m + 1];
-            len = 0;
-            while (a < ae || b < be) {
-                const int32_t x = a < ae ? idx[a] : INT32_MAX, y = b < be ? idx[b] : INT32_MAX;
-                if (x <= y) ++a;
-                if (y <= x) ++b;
-                ++len;
-            }
+        if (lane == 0) {
+            new_id[r] = id;
+            atomicAdd(nsize + id, (unsigned long long)size[r]);
+            atomicAdd(nnnz + id, (unsigned long long)nnz[r]);
         }
-        nlen[id] = len;
+        if (root != r) continue;
+        const int64_t la = ptr[r + 1] - ptr[r];
+        int64_t len = la;
+        if (m > r) {
+            const int32_t *A = idx + ptr[r], *B = idx + ptr[m];
+            const int64_t lb = ptr[m + 1] - ptr[m];
+            int64_t dup = 0;
+            for (int64_t j = lane; j < lb; j += 32) {
+                const int64_t p = lower_bound_run(A, la, B[j]);
+                dup += p < la && A[p] == B[j];
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) dup += __shfl_xor_sync(kFullMask, dup, o);
+            len = la + lb - dup;
+        }
+        if (lane == 0) nlen[id] = len;
     }
 }
 
+// Warp per new row: its sorted column list.  An unmatched row is copied; a
+// pair's union places A's entry i at i + (B entries below it that are not in
+// A) and B's entries missing from A at (their rank among those) + (A entries
+// below them), each found by a binary search, the ranks by warp ballots.
 __global__ void contract_emit_kernel(const int64_t *__restrict__ mate, int64_t n, const int64_t *__restrict__ rank,
                                      const int64_t *__restrict__ ptr, const int32_t *__restrict__ idx,
                                      const int64_t *__restrict__ nptr, int32_t *__restrict__ nidx) {
-    for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < n; r += (int64_t)gridDim.x * blockDim.x) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = (int64_t)gridDim.x * (blockDim.x / 32);
+    for (int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32; r < n; r += nw) {
         const int64_t m = mate[r];
         if (m >= 0 && m < r) continue;
-        int64_t o = nptr[rank[r]];
-        int64_t a = ptr[r], ae = ptr[r + 1];
-        int64_t b = m > r ? ptr[m] : 0, be = m > r ? ptr[m + 1] : 0;
-        while (a < ae || b < be) {
-            const int32_t x = a < ae ? idx[a] : INT32_MAX, y = b < be ? idx[b] : INT32_MAX;
-            nidx[o++] = x <= y ? x : y;
-            if (x <= y) ++a;
-            if (y <= x) ++b;
+        int32_t *out = nidx + nptr[rank[r]];
+        const int32_t *A = idx + ptr[r];
+        const int64_t la = ptr[r + 1] - ptr[r];
+        if (m < 0) {
+            for (int64_t i = lane; i < la; i += 32) out[i] = A[i];
+            continue;
+        }
+        const int32_t *B = idx + ptr[m];
+        const int64_t lb = ptr[m + 1] - ptr[m];
+        int64_t common = 0;   // A entries below the current chunk that are in B
+        for (int64_t i0 = 0; i0 < la; i0 += 32) {
+            const int64_t i = i0 + lane;
+            int64_t p = 0;
+            bool in_b = false;
+            if (i < la) {
+                p = lower_bound_run(B, lb, A[i]);
+                in_b = p < lb && B[p] == A[i];
+            }
+            const unsigned mask = __ballot_sync(kFullMask, in_b);
+            if (i < la) out[i + p - (common + __popc(mask & lanemask_lt()))] = A[i];
+            common += __popc(mask);
+        }
+        int64_t missing = 0;  // B entries below the current chunk that are not in A
+        for (int64_t j0 = 0; j0 < lb; j0 += 32) {
+            const int64_t j = j0 + lane;
+            int64_t q = 0;
+            bool out_a = false;
+            if (j < lb) {
+                q = lower_bound_run(A, la, B[j]);
+                out_a = !(q < la && A[q] == B[j]);
+            }
+            const unsigned mask = __ballot_sync(kFullMask, out_a);
+            if (out_a) out[missing + __popc(mask & lanemask_lt()) + q] = B[j];
+            missing += __popc(mask);
         }
     }
 }
@@ -367,7 +487,7 @@ __global__ void diff_kernel(const int64_t *__restrict__ ptr, int64_t n, int64_t 
         out[i] = ptr[i + 1] - ptr[i];
 }
 
-// ---- per-row counting by hashing (top-k >= 0) ----
+// ---- per-row counting by hashing (top-k > 0) ----
 //
 // A CTA per row: the row's incidences are counted in an open-addressing
 // table (shared memory, or a global region for rows whose table would not
@@ -378,6 +498,14 @@ constexpr int kHashThreads = 256;
 constexpr int kSmemSlots = 8192;    // small rows: 64 KB of (key, count) slots, 3 CTAs per SM
 constexpr int kMidSlots = 16384;    // mid rows: 128 KB, one CTA of 512 threads per SM
 
+// Slots of a row's table: a power of two, at least 64 and twice the row's incidences (0: no table).
+inline int64_t table_slots(int64_t inc) {
+    if (inc <= 1) return 0;
+    int64_t S = 64;
+    while (S < 2 * inc) S <<= 1;
+    return S;
+}
+
 __device__ __forceinline__ uint32_t slot_of(uint32_t j, int lg) {
     return lg ? (j * 0x9E3779B1u) >> (32 - lg) : 0u;
 }
@@ -385,6 +513,102 @@ __device__ __forceinline__ uint32_t slot_of(uint32_t j, int lg) {
 // SLOTS: the shared-memory table of this launch's rows (tables of up to SLOTS
 // and more than SLOTS / 2 slots, the smallest class from 64); 0: rows whose
 // table exceeds kMidSlots, in global memory.
+struct SelectSmem {
+    uint32_t hist[256];
+    unsigned long long red_u, red_w, sel_prefix;
+    long long sel_k;
+};
+
+// Over the slots [0, S) of a counted table (key >= 0: occupied): U = the
+// occupied slots, W = the heaviest count and kth = the topk-th smallest key
+// (W - w) << jb | j (~0 when U <= topk: every entry kept), by a radix select
+// a byte at a time.  Every thread of the CTA calls it after a barrier and gets
+// the same three values.
+template <int THREADS>
+__device__ void count_and_select(const int32_t *key, const uint32_t *cnt, int64_t S, int jb, long long topk,
+                                 SelectSmem &sm, unsigned long long &U, unsigned long long &W,
+                                 unsigned long long &kth) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) {
+        sm.red_u = 0;
+        sm.red_w = 0;
+    }
+    __syncthreads();
+    unsigned long long u = 0, wm = 0;
+    for (int64_t t = tid; t < S; t += THREADS)
+        if (key[t] >= 0) {
+            ++u;
+            wm = cnt[t] > wm ? cnt[t] : wm;
+        }
+    atomicAdd(&sm.red_u, u);
+    atomicMax(&sm.red_w, wm);
+    __syncthreads();
+    U = sm.red_u;
+    W = sm.red_w;
+    kth = ~0ull;
+    if ((long long)U <= topk) return;
+    const int bits = jb + (64 - __clzll((long long)W));   // key (W - w) << jb | j
+    if (tid == 0) {
+        sm.sel_prefix = 0;
+        sm.sel_k = topk;
+    }
+    unsigned long long mask = 0;
+    for (int shift = ((bits + 7) / 8 - 1) * 8; shift >= 0; shift -= 8) {
+        for (int b = tid; b < 256; b += THREADS) sm.hist[b] = 0;
+        __syncthreads();
+        const unsigned long long prefix = sm.sel_prefix;
+        for (int64_t t = tid; t < S; t += THREADS) {
+            if (key[t] < 0) continue;
+            const unsigned long long K = ((W - cnt[t]) << jb) | (unsigned long long)key[t];
+            if ((K & mask) == prefix) atomicAdd(&sm.hist[(K >> shift) & 255], 1u);
+        }
+        __syncthreads();
+        if (warp == 0) {
+            // the first byte value v whose running count reaches k (255 when
+            // none before it does): lanes own 8 bins each, one warp scan
+            const long long k = sm.sel_k;
+            unsigned c[8];
+            long long own = 0;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                c[q] = sm.hist[lane * 8 + q];
+                own += c[q];
+            }
+            long long incl = own;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const long long up = __shfl_up_sync(kFullMask, incl, o);
+                if (lane >= o) incl += up;
+            }
+            long long cum = incl - own;
+            if (cum < k && (k <= incl || lane == 31)) {
+                int v = lane * 8;
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    if (v == 255 || cum + c[q] >= k) break;
+                    cum += c[q];
+                    ++v;
+                }
+                sm.sel_k = k - cum;
+                sm.sel_prefix = prefix | ((unsigned long long)v << shift);
+            }
+        }
+        mask |= 255ull << shift;
+        __syncthreads();
+    }
+    kth = sm.sel_prefix;
+}
+
+__device__ __forceinline__ void emit_edge(int64_t i, int32_t j, uint32_t w, int jb,
+                                          unsigned long long *__restrict__ ecount, uint64_t *__restrict__ ekey,
+                                          uint32_t *__restrict__ ew) {
+    const unsigned long long o = atomicAdd(ecount, 2ull);
+    ekey[o] = ((uint64_t)i << jb) | (uint64_t)j;
+    ekey[o + 1] = ((uint64_t)j << jb) | (uint64_t)i;
+    ew[o] = w;
+    ew[o + 1] = w;
+}
+
 template <int THREADS, int SLOTS>
 __global__ void __launch_bounds__(THREADS) hash_topk_kernel(
     const int64_t *__restrict__ ptr, const int32_t *__restrict__ idx, const int64_t *__restrict__ tptr,
@@ -394,10 +618,7 @@ __global__ void __launch_bounds__(THREADS) hash_topk_kernel(
     extern __shared__ uint32_t hsm[];
     int32_t *skey = reinterpret_cast<int32_t *>(hsm);
     uint32_t *scnt = hsm + (SLOTS > 0 ? SLOTS : 1);
-    __shared__ uint32_t hist[256];
-    __shared__ unsigned long long red_u, red_w;
-    __shared__ unsigned long long sel_prefix;
-    __shared__ long long sel_k;
+    __shared__ SelectSmem sm;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     for (int64_t i = blockIdx.x; i < n; i += gridDim.x) {
         const int64_t inc = pinc[i];
@@ -410,7 +631,7 @@ __global__ void __launch_bounds__(THREADS) hash_topk_kernel(
         if (S <= lo_cap || S > hi_cap) continue;   // another launch's rows
         int32_t *key = skey;
         uint32_t *cnt = scnt;
-        if (SLOTS == 0) {
+        if (SLOTS == 0) {   // the row's region of the global tables
             key = gkey + goff[i];
             cnt = gcnt + goff[i];
         }
@@ -418,10 +639,6 @@ __global__ void __launch_bounds__(THREADS) hash_topk_kernel(
         for (int64_t t = tid; t < S; t += THREADS) {
             key[t] = -1;
             cnt[t] = 0;
-        }
-        if (tid == 0) {
-            red_u = 0;
-            red_w = 0;
         }
         __syncthreads();
         // insert: warps take the row's columns, lanes the column's rows
@@ -442,64 +659,15 @@ __global__ void __launch_bounds__(THREADS) hash_topk_kernel(
             }
         }
         __syncthreads();
-        // occupied slots and the heaviest weight
-        unsigned long long u = 0, wm = 0;
-        for (int64_t t = tid; t < S; t += THREADS)
-            if (key[t] >= 0) {
-                ++u;
-                wm = cnt[t] > wm ? cnt[t] : wm;
-            }
-        atomicAdd(&red_u, u);
-        atomicMax(&red_w, wm);
-        __syncthreads();
-        const unsigned long long U = red_u, W = red_w;
+        unsigned long long U, W, kth;
+        count_and_select<THREADS>(key, cnt, S, jb, topk, sm, U, W, kth);
         if (U == 0) continue;
-        const int bits = jb + (64 - __clzll((long long)W));   // key (W - w) << jb | j
-        // threshold: the topk-th smallest key (all kept when U <= topk)
-        unsigned long long kth = ~0ull;
-        if ((long long)U > topk) {
-            if (tid == 0) {
-                sel_prefix = 0;
-                sel_k = topk;
-            }
-            unsigned long long mask = 0;
-            for (int shift = ((bits + 7) / 8 - 1) * 8; shift >= 0; shift -= 8) {
-                for (int b = tid; b < 256; b += THREADS) hist[b] = 0;
-                __syncthreads();
-                const unsigned long long prefix = sel_prefix;
-                for (int64_t t = tid; t < S; t += THREADS) {
-                    if (key[t] < 0) continue;
-                    const unsigned long long K = ((W - cnt[t]) << jb) | (unsigned long long)key[t];
-                    if ((K & mask) == prefix) atomicAdd(&hist[(K >> shift) & 255], 1u);
-                }
-                __syncthreads();
-                if (tid == 0) {
-                    long long k = sel_k, cum = 0;
-                    int v = 0;
-                    for (; v < 255; ++v) {
-                        if (cum + hist[v] >= k) break;
-                        cum += hist[v];
-                    }
-                    sel_k = k - cum;
-                    sel_prefix = prefix | ((unsigned long long)v << shift);
-                }
-                mask |= 255ull << shift;
-                __syncthreads();
-            }
-            kth = sel_prefix;
-        }
         // emit the kept entries, both directions
         for (int64_t t = tid; t < S; t += THREADS) {
             const int32_t j = key[t];
             if (j < 0) continue;
             const uint32_t w = cnt[t];
-            const unsigned long long K = ((W - w) << jb) | (unsigned long long)j;
-            if (K > kth) continue;
-            const unsigned long long o = atomicAdd(ecount, 2ull);
-            ekey[o] = ((uint64_t)i << jb) | (uint64_t)j;
-            ekey[o + 1] = ((uint64_t)j << jb) | (uint64_t)i;
-            ew[o] = w;
-            ew[o + 1] = w;
+            if ((((W - w) << jb) | (unsigned long long)j) <= kth) emit_edge(i, j, w, jb, ecount, ekey, ew);
         }
     }
 }
@@ -574,24 +742,44 @@ int similarity_graph(const int64_t *ptr, const int32_t *idx, int64_t n, int64_t 
         transpose_kernel<<<warps_grid(n), kHemThreads, 0, s>>>(pptr.p, pidx.p, n, tptr.p, tcur.p, trow.p);
         SPMM_LAUNCH_CHECK();
     }
-    // incidences per chunk of rows; row chunks from the host copy of the prefix
+    if (topk == 0) return SPMM_OK;   // no row keeps an edge
+    // topk > 0: every row is counted by hashing (hash_topk_kernel); topk < 0
+    // (every pair kept): by sorting the rows' incidences in chunks.
     std::vector<int64_t> hstart((size_t)n + 1);
     SPMM_TRY(to_host(hstart.data(), pstart.p, n + 1, s));
+    std::vector<int64_t> big;   // rows counted by sorting, ascending
+    if (topk < 0)
+        for (int64_t r = 0; r < n; ++r)
+            if (hstart[r + 1] > hstart[r]) big.push_back(r);
+    std::vector<int64_t> bstart(1, 0);
+    for (int64_t r : big) bstart.push_back(bstart.back() + hstart[r + 1] - hstart[r]);
+    std::vector<std::pair<int64_t, int64_t>> chunks;   // ranges of `big` of at most kPairBudget incidences
+    for (size_t b0 = 0; b0 < big.size();) {
+        size_t b1 = b0 + 1;
+        while (b1 < big.size() && bstart[b1 + 1] - bstart[b0] <= kPairBudget) ++b1;
+        chunks.push_back({(int64_t)b0, (int64_t)b1});
+        b0 = b1;
+    }
+    int64_t ecap = 0;
+    if (topk > 0) {
+        ecap = 2 * n * topk;
+    } else {
+        for (auto &c : chunks) ecap += 2 * (bstart[c.second] - bstart[c.first]);
+    }
     DBuf<uint64_t> ek0, ek1;
     DBuf<uint32_t> ew0;
+    SPMM_TRY(ek0.alloc(ecap, s));
+    SPMM_TRY(ew0.alloc(ecap, s));
     int64_t ecount = 0;
-    if (topk >= 0) {
-        // hashing path: global tables for the rows whose table exceeds shared memory
+    DBuf<int64_t> dlist, dstart;
+    if (topk > 0) {
+        // global tables for the rows whose table exceeds shared memory
         std::vector<int64_t> hoff((size_t)n + 1, 0);
         int64_t gslots = 0;
         for (int64_t r = 0; r < n; ++r) {
-            const int64_t inc = hstart[r + 1] - hstart[r];
             hoff[r] = gslots;
-            if (inc > 1) {
-                int64_t S = 64;
-                while (S < 2 * inc) S <<= 1;
-                if (S > kMidSlots) gslots += S;
-            }
+            const int64_t S = table_slots(hstart[r + 1] - hstart[r]);
+            if (S > kMidSlots) gslots += S;
         }
         DBuf<int64_t> goff;
         DBuf<int32_t> gkey;
@@ -600,110 +788,91 @@ int similarity_graph(const int64_t *ptr, const int32_t *idx, int64_t n, int64_t 
         SPMM_CUDA_TRY(cudaMemcpyAsync(goff.p, hoff.data(), (size_t)(n + 1) * 8, cudaMemcpyHostToDevice, s));
         SPMM_TRY(gkey.alloc(gslots, s));
         SPMM_TRY(gcnt.alloc(gslots, s));
-        const int64_t ecap = 2 * n * (topk > 0 ? topk : 1);
-        SPMM_TRY(ek0.alloc(ecap, s));
-        SPMM_TRY(ew0.alloc(ecap, s));
         DBuf<unsigned long long> ecnt;
         SPMM_TRY(ecnt.alloc(1, s));
         SPMM_CUDA_TRY(cudaMemsetAsync(ecnt.p, 0, 8, s));
-        if (topk > 0) {
-            const size_t smem = (size_t)kSmemSlots * 8;
-            auto small = hash_topk_kernel<kHashThreads, kSmemSlots>;
-            auto mid = hash_topk_kernel<512, kMidSlots>;
-            SPMM_CUDA_TRY(cudaFuncSetAttribute(small, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-            SPMM_CUDA_TRY(cudaFuncSetAttribute(mid, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               (int)((size_t)kMidSlots * 8)));
-            int dev = 0, sms = 0;
-            SPMM_CUDA_TRY(cudaGetDevice(&dev));
-            SPMM_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-            const int64_t grid = std::min<int64_t>(n, (int64_t)sms * 3);
-            small<<<(unsigned)grid, kHashThreads, smem, s>>>(pptr.p, pidx.p, tptr.p, trow.p, pinc.p, goff.p, gkey.p,
-                                                             gcnt.p, n, jb, topk, ecnt.p, ek0.p, ew0.p);
-            SPMM_LAUNCH_CHECK();
-            mid<<<(unsigned)std::min<int64_t>(n, sms), 512, (size_t)kMidSlots * 8, s>>>(
+        const size_t smem = (size_t)kSmemSlots * 8;
+        auto small = hash_topk_kernel<kHashThreads, kSmemSlots>;
+        auto mid = hash_topk_kernel<512, kMidSlots>;
+        SPMM_CUDA_TRY(cudaFuncSetAttribute(small, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        SPMM_CUDA_TRY(cudaFuncSetAttribute(mid, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)((size_t)kMidSlots * 8)));
+        int dev = 0, sms = 0;
+        SPMM_CUDA_TRY(cudaGetDevice(&dev));
+        SPMM_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        const int64_t grid = std::min<int64_t>(n, (int64_t)sms * 3);
+        small<<<(unsigned)grid, kHashThreads, smem, s>>>(pptr.p, pidx.p, tptr.p, trow.p, pinc.p, goff.p, gkey.p,
+                                                         gcnt.p, n, jb, topk, ecnt.p, ek0.p, ew0.p);
+        SPMM_LAUNCH_CHECK();
+        mid<<<(unsigned)std::min<int64_t>(n, sms), 512, (size_t)kMidSlots * 8, s>>>(
+            pptr.p, pidx.p, tptr.p, trow.p, pinc.p, goff.p, gkey.p, gcnt.p, n, jb, topk, ecnt.p, ek0.p, ew0.p);
+        SPMM_LAUNCH_CHECK();
+        if (gslots > 0) {   // rows with global tables: 1,024 threads each
+            hash_topk_kernel<1024, 0><<<(unsigned)std::min<int64_t>(n, sms * 2), 1024, 0, s>>>(
                 pptr.p, pidx.p, tptr.p, trow.p, pinc.p, goff.p, gkey.p, gcnt.p, n, jb, topk, ecnt.p, ek0.p, ew0.p);
             SPMM_LAUNCH_CHECK();
-            if (gslots > 0) {   // rows with global tables: 1,024 threads each
-                hash_topk_kernel<1024, 0><<<(unsigned)std::min<int64_t>(n, sms * 2), 1024, 0, s>>>(
-                    pptr.p, pidx.p, tptr.p, trow.p, pinc.p, goff.p, gkey.p, gcnt.p, n, jb, topk, ecnt.p, ek0.p,
-                    ew0.p);
-                SPMM_LAUNCH_CHECK();
-            }
         }
         unsigned long long ec = 0;
         SPMM_TRY(to_host(&ec, ecnt.p, 1, s));
         ecount = (int64_t)ec;
-        pidx.release();
-        trow.release();
     }
-    if (topk < 0) {
-    // heaviest possible w: the longest pruned row
-    int64_t wmax_len = 0;
-    {
-        std::vector<int64_t> hp((size_t)n + 1);
-        SPMM_TRY(to_host(hp.data(), pptr.p, n + 1, s));
-        for (int64_t r = 0; r < n; ++r) wmax_len = std::max(wmax_len, hp[r + 1] - hp[r]);
+    if (!big.empty()) {
+        // heaviest possible w: the longest pruned row among them
+        int64_t wmax_len = 0;
+        {
+            std::vector<int64_t> hp((size_t)n + 1);
+            SPMM_TRY(to_host(hp.data(), pptr.p, n + 1, s));
+            for (int64_t r : big) wmax_len = std::max(wmax_len, hp[r + 1] - hp[r]);
+        }
+        const int wb = bit_width_u64((uint64_t)wmax_len + 1);
+        SPMM_TRY(dlist.alloc((int64_t)big.size(), s));
+        SPMM_TRY(dstart.alloc((int64_t)bstart.size(), s));
+        SPMM_CUDA_TRY(cudaMemcpyAsync(dlist.p, big.data(), big.size() * 8, cudaMemcpyHostToDevice, s));
+        SPMM_CUDA_TRY(cudaMemcpyAsync(dstart.p, bstart.data(), bstart.size() * 8, cudaMemcpyHostToDevice, s));
+        for (auto &c : chunks) {
+            const int64_t b0 = c.first, rows = c.second - c.first;
+            const int64_t P = bstart[c.second] - bstart[b0];
+            if (P == 0) continue;
+            const int rb = bit_width_u64((uint64_t)rows);
+            if (rb + jb > 63 || rb + wb + jb > 64) return SPMM_EUNSUPPORTED;
+            const uint64_t sentinel = (rb + jb == 64) ? ~0ull : ((1ull << (rb + jb)) - 1ull);
+            DBuf<uint64_t> k0, k1;
+            SPMM_TRY(k0.alloc(P, s));
+            SPMM_TRY(k1.alloc(P, s));
+            gen_pairs_kernel<<<warps_grid(rows), kHemThreads, 0, s>>>(pptr.p, pidx.p, tptr.p, trow.p, dlist.p + b0,
+                                                                      dstart.p + b0, rows, jb, sentinel, k0.p);
+            SPMM_LAUNCH_CHECK();
+            SPMM_TRY(sort_keys(k0, k1, P, rb + jb, s));
+            // unique pairs with their counts, keyed for the top-k order
+            DBuf<int64_t> flag, pos;
+            SPMM_TRY(flag.alloc(P + 1, s));
+            SPMM_TRY(pos.alloc(P + 1, s));
+            head_flags_kernel<<<grid_for(P, kHemThreads), kHemThreads, 0, s>>>(k0.p, P, sentinel, flag.p);
+            SPMM_LAUNCH_CHECK();
+            int64_t U = 0;
+            SPMM_TRY(scan_counts(flag.p, pos.p, P, s, &U));
+            if (U == 0) continue;
+            DBuf<uint64_t> u0, u1;
+            SPMM_TRY(u0.alloc(U, s));
+            SPMM_TRY(u1.alloc(U, s));
+            rle_kernel<<<grid_for(P, kHemThreads), kHemThreads, 0, s>>>(k0.p, P, sentinel, pos.p, jb, wb, u0.p);
+            SPMM_LAUNCH_CHECK();
+            k0.release();
+            k1.release();
+            SPMM_TRY(sort_keys(u0, u1, U, rb + wb + jb, s));
+            topk_flags_kernel<<<grid_for(U, kHemThreads), kHemThreads, 0, s>>>(u0.p, U, jb, wb, topk, flag.p);
+            SPMM_LAUNCH_CHECK();
+            int64_t kept = 0;
+            SPMM_TRY(scan_counts(flag.p, pos.p, U, s, &kept));
+            if (ecount + 2 * kept > ecap) return SPMM_EUNSUPPORTED;
+            topk_emit_kernel<<<grid_for(U, kHemThreads), kHemThreads, 0, s>>>(u0.p, U, flag.p, pos.p, dlist.p + b0,
+                                                                              jb, wb, ecount, ek0.p, ew0.p);
+            SPMM_LAUNCH_CHECK();
+            ecount += 2 * kept;
+        }
     }
-    const int wb = bit_width_u64((uint64_t)wmax_len + 1);
-    // directed top-k edges of all chunks, both directions
-    const int64_t kcap = topk >= 0 ? topk : n;
-    std::vector<std::pair<int64_t, int64_t>> chunks;
-    for (int64_t r0 = 0; r0 < n;) {
-        int64_t r1 = r0 + 1;
-        while (r1 < n && hstart[r1 + 1] - hstart[r0] <= kPairBudget) ++r1;
-        chunks.push_back({r0, r1});
-        r0 = r1;
-    }
-    int64_t ecap = 0;
-    for (auto &c : chunks) {
-        const int64_t rows = c.second - c.first;
-        const int64_t pairs = hstart[c.second] - hstart[c.first];
-        ecap += 2 * std::min(pairs, rows * kcap);
-    }
-    SPMM_TRY(ek0.alloc(ecap, s));
-    SPMM_TRY(ew0.alloc(ecap, s));
-    for (auto &c : chunks) {
-        const int64_t r0 = c.first, r1 = c.second, rows = r1 - r0;
-        const int64_t P = hstart[r1] - hstart[r0];
-        if (P == 0) continue;
-        const int rb = bit_width_u64((uint64_t)rows);
-        if (rb + jb > 63 || rb + wb + jb > 64) return SPMM_EUNSUPPORTED;
-        const uint64_t sentinel = (rb + jb == 64) ? ~0ull : ((1ull << (rb + jb)) - 1ull);
-        DBuf<uint64_t> k0, k1;
-        SPMM_TRY(k0.alloc(P, s));
-        SPMM_TRY(k1.alloc(P, s));
-        gen_pairs_kernel<<<warps_grid(rows), kHemThreads, 0, s>>>(pptr.p, pidx.p, tptr.p, trow.p, pstart.p, r0, r1,
-                                                                  jb, sentinel, k0.p);
-        SPMM_LAUNCH_CHECK();
-        SPMM_TRY(sort_keys(k0, k1, P, rb + jb, s));
-        // unique pairs with their counts, keyed for the top-k order
-        DBuf<int64_t> flag, pos;
-        SPMM_TRY(flag.alloc(P + 1, s));
-        SPMM_TRY(pos.alloc(P + 1, s));
-        head_flags_kernel<<<grid_for(P, kHemThreads), kHemThreads, 0, s>>>(k0.p, P, sentinel, flag.p);
-        SPMM_LAUNCH_CHECK();
-        int64_t U = 0;
-        SPMM_TRY(scan_counts(flag.p, pos.p, P, s, &U));
-        if (U == 0) continue;
-        DBuf<uint64_t> u0, u1;
-        SPMM_TRY(u0.alloc(U, s));
-        SPMM_TRY(u1.alloc(U, s));
-        rle_kernel<<<grid_for(P, kHemThreads), kHemThreads, 0, s>>>(k0.p, P, sentinel, pos.p, jb, wb, u0.p);
-        SPMM_LAUNCH_CHECK();
-        k0.release();
-        k1.release();
-        SPMM_TRY(sort_keys(u0, u1, U, rb + wb + jb, s));
-        topk_flags_kernel<<<grid_for(U, kHemThreads), kHemThreads, 0, s>>>(u0.p, U, jb, wb, topk, flag.p);
-        SPMM_LAUNCH_CHECK();
-        int64_t kept = 0;
-        SPMM_TRY(scan_counts(flag.p, pos.p, U, s, &kept));
-        if (ecount + 2 * kept > ecap) return SPMM_EUNSUPPORTED;
-        topk_emit_kernel<<<grid_for(U, kHemThreads), kHemThreads, 0, s>>>(u0.p, U, flag.p, pos.p, r0, jb, wb,
-                                                                          ecount, ek0.p, ew0.p);
-        SPMM_LAUNCH_CHECK();
-        ecount += 2 * kept;
-    }
-    }
+    pidx.release();
+    trow.release();
     if (ecount == 0) return SPMM_OK;
     // symmetric graph: sort (row, col) keys with their weights, drop repeats
     DBuf<uint32_t> ew1;
@@ -747,6 +916,36 @@ using namespace spmm;
 
 // Levels the matching loop may run for `target` (the reference's cap,
 // clustering.py:291-296): 8 * max(1, ceil(log2(target))) + 16.
+// Keeps the device's default stream-ordered pool from returning its memory to
+// the system at every synchronisation while the levels run (each level frees
+// and re-allocates gigabytes of scratch; remapping it cost more than the
+// kernels).  When the call ends the pool is trimmed to its previous release
+// threshold and that threshold is restored.
+class PoolHold {
+  public:
+    explicit PoolHold(cudaStream_t s) : s_(s) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetDefaultMemPool(&pool_, dev) != cudaSuccess) return;
+        if (cudaMemPoolGetAttribute(pool_, cudaMemPoolAttrReleaseThreshold, &old_) != cudaSuccess) return;
+        uint64_t keep = ~0ull;
+        held_ = cudaMemPoolSetAttribute(pool_, cudaMemPoolAttrReleaseThreshold, &keep) == cudaSuccess;
+    }
+    PoolHold(const PoolHold &) = delete;
+    PoolHold &operator=(const PoolHold &) = delete;
+    ~PoolHold() {
+        if (!held_) return;
+        cudaStreamSynchronize(s_);                  // the levels' frees have completed
+        cudaMemPoolTrimTo(pool_, (size_t)old_);
+        cudaMemPoolSetAttribute(pool_, cudaMemPoolAttrReleaseThreshold, &old_);
+    }
+
+  private:
+    cudaStream_t s_;
+    cudaMemPool_t pool_{};
+    uint64_t old_ = 0;
+    bool held_ = false;
+};
+
 static int hem_max_levels(int64_t target) {
     int lg = 0;
     while ((1ll << lg) < target) ++lg;
@@ -779,6 +978,7 @@ extern "C" int spmm_hem_hierarchy(int64_t rows, int64_t cols, const int64_t *ind
     SPMM_TRY(record());
     if (rows <= 1 || target <= 1) return levels ? (cudaStreamSynchronize(s) == cudaSuccess ? SPMM_OK : SPMM_ECUDA)
                                                 : SPMM_OK;
+    const PoolHold hold(s);   // declared before every level buffer: released after them
     int64_t nnz0 = 0;
     SPMM_TRY(to_host(&nnz0, indptr + rows, 1, s));
     const Caps caps{max_size, max_nnz};
@@ -815,12 +1015,26 @@ extern "C" int spmm_hem_hierarchy(int64_t rows, int64_t cols, const int64_t *ind
         SPMM_CUDA_TRY(cudaMemsetAsync(active.p, 1, (size_t)n, s));
         fill_kernel<<<grid_for(n, kHemThreads), kHemThreads, 0, s>>>(mate.p, n, -1);
         SPMM_LAUNCH_CHECK();
+        // vertices with many edges, picked by a CTA each
+        DBuf<int64_t> heavy;
+        SPMM_TRY(heavy.alloc(n, s));
+        SPMM_CUDA_TRY(cudaMemsetAsync(matched.p, 0, 8, s));
+        heavy_list_kernel<<<grid_for(n, kHemThreads), kHemThreads, 0, s>>>(gptr.p, n, matched.p, heavy.p);
+        SPMM_LAUNCH_CHECK();
+        unsigned long long n_heavy = 0;
+        SPMM_TRY(to_host(&n_heavy, matched.p, 1, s));
         unsigned long long total = 0;
         for (int round = 0; round < residual_rounds; ++round) {
             SPMM_CUDA_TRY(cudaMemsetAsync(matched.p, 0, 8, s));
             best_kernel<<<warps_grid(n), kHemThreads, 0, s>>>(gptr.p, gcol.p, gw.p, n, active.p, size.p, rnnz.p,
                                                                caps, feasible_first, best.p);
             SPMM_LAUNCH_CHECK();
+            if (n_heavy) {
+                best_heavy_kernel<<<(unsigned)std::min<unsigned long long>(n_heavy, 148ull * 8), kHeavyThreads, 0,
+                                    s>>>(gptr.p, gcol.p, gw.p, heavy.p, (int64_t)n_heavy, active.p, size.p, rnnz.p,
+                                         caps, feasible_first, best.p);
+                SPMM_LAUNCH_CHECK();
+            }
             mutual_kernel<<<grid_for(n, kHemThreads), kHemThreads, 0, s>>>(best.p, n, size.p, rnnz.p, caps, mate.p,
                                                                           active.p, matched.p);
             SPMM_LAUNCH_CHECK();
@@ -846,14 +1060,14 @@ extern "C" int spmm_hem_hierarchy(int64_t rows, int64_t cols, const int64_t *ind
         SPMM_TRY(nnnz.alloc(n_new, s));
         SPMM_CUDA_TRY(cudaMemsetAsync(nsize.p, 0, (size_t)n_new * 8, s));
         SPMM_CUDA_TRY(cudaMemsetAsync(nnnz.p, 0, (size_t)n_new * 8, s));
-        contract_kernel<<<grid_for(n, kHemThreads), kHemThreads, 0, s>>>(mate.p, n, rank.p, size.p, rnnz.p, lptr.p,
+        contract_kernel<<<warps_grid(n), kHemThreads, 0, s>>>(mate.p, n, rank.p, size.p, rnnz.p, lptr.p,
                                                                         lidx.p, new_id.p, nsize.p, nnnz.p, nlen.p);
         SPMM_LAUNCH_CHECK();
         int64_t nnz_new = 0;
         SPMM_TRY(scan_counts(nlen.p, nptr.p, n_new, s, &nnz_new));
         DBuf<int32_t> nidx;
         SPMM_TRY(nidx.alloc(nnz_new, s));
-        contract_emit_kernel<<<grid_for(n, kHemThreads), kHemThreads, 0, s>>>(mate.p, n, rank.p, lptr.p, lidx.p,
+        contract_emit_kernel<<<warps_grid(n), kHemThreads, 0, s>>>(mate.p, n, rank.p, lptr.p, lidx.p,
                                                                              nptr.p, nidx.p);
         SPMM_LAUNCH_CHECK();
         relabel_kernel<<<grid_for(rows, kHemThreads), kHemThreads, 0, s>>>(labels, rows, new_id.p);

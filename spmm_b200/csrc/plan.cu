@@ -9,7 +9,9 @@
 //     the block list;
 //   * for remainder-major matrices with scattered blocks, a row-ordered copy
 //     of every stored entry (the CSR view spmm_boo_to_csr produces), so one
-//     load-balanced nnz-flat pass computes Y (plan.cuh: plan_row_view).
+//     load-balanced nnz-flat pass computes Y (plan.cuh: plan_row_view_rem);
+//   * the same copy for matrices of a few entries per row, multiplied a warp
+//     per row (plan.cuh: plan_short_rows).
 // The plan lives in a caller-owned device buffer; the product reads it
 // through spmm_launch_cfg::plan.
 #include "plan.cuh"

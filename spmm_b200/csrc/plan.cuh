@@ -26,6 +26,7 @@ struct PlanLayout {
     size_t rv_val;      //   scalar[entries] values: every stored entry, rows ordered by (column, value)
     size_t total;
     bool row_view;
+    bool short_rows;    // the row view serves a warp-per-row product (not remainder-major)
     int64_t entries;
 };
 
@@ -36,12 +37,26 @@ inline size_t plan_align(size_t v) { return (v + 255) & ~(size_t)255; }
 // groups on a power-law graph -- are multiplied through a row-ordered copy of
 // all their entries: one load-balanced pass then computes Y, where the block
 // kernel in add mode would walk scattered blocks group by group.
-inline bool plan_row_view(const spmm_boo_dev *A) {
+inline bool plan_row_view_rem(const spmm_boo_dev *A) {
     const int64_t entries = A->nnz_c + A->rem_nnz + A->tail_nnz;
     const bool rem_major = A->rem_nnz > 0 && 2 * A->rem_nnz >= A->total_nnz;
     return rem_major && 64 * (A->nnz_c + A->tail_nnz) >= entries && entries <= 0x7fffffffLL &&
            A->rows <= 0x7fffffffLL;
 }
+
+// Other matrices of at most kShortRow entries per row on average (a 2-D
+// Laplacian: 5) are multiplied through the same copy a warp per row: the
+// block kernel's per-group chain of dependent loads outweighs their few
+// products.
+constexpr int64_t kShortRow = 16;
+inline bool plan_short_rows(const spmm_boo_dev *A) {
+    const int64_t entries = A->nnz_c + A->rem_nnz + A->tail_nnz;
+    const bool rem_major = A->rem_nnz > 0 && 2 * A->rem_nnz >= A->total_nnz;
+    return !rem_major && A->rows > 0 && entries > 0 && entries <= kShortRow * A->rows &&
+           entries <= 0x7fffffffLL && A->rows <= 0x7fffffffLL;
+}
+
+inline bool plan_row_view(const spmm_boo_dev *A) { return plan_row_view_rem(A) || plan_short_rows(A); }
 
 // Matrices the tensor-core product can take (float32, groups up to 64 x 64):
 // their sparse blocks whose entries lie in at most two 4-column quads are
@@ -56,6 +71,7 @@ inline PlanLayout plan_layout(const spmm_boo_dev *A) {
     const size_t sb = A->scalar_type == SPMM_F64 ? 8 : 4;
     L.entries = A->nnz_c + A->rem_nnz + A->tail_nnz;
     L.row_view = plan_row_view(A);
+    L.short_rows = plan_short_rows(A);
     L.packing = plan_packing(A);
     L.pw = A->max_nr <= 32 && A->max_nc <= 32 ? 32 : 64;
     size_t off = 0;

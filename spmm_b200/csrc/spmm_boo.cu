@@ -397,38 +397,30 @@ __device__ __forceinline__ void rem_span(Frag<S, VEC> (&acc)[VPT], const int32_t
             v = e < e1 ? __ldg(val + e) : S(0);
         }
         const int n = e1 - b < 32 ? (int)(e1 - b) : 32;
-        int j = 0;
-        for (; j + U <= n; j += U) {
+        // batches of U entries, the last one partial: its X rows are in flight
+        // together too (a 5-entry row issues its five loads at once)
+        for (int j = 0; j < n; j += U) {
             Frag<S, VEC> x[U][VPT];
             S a[U];
 #pragma unroll
             for (int u = 0; u < U; ++u) {
-                const int32_t cu = __shfl_sync(kFullMask, c, j + u);
-                a[u] = __shfl_sync(kFullMask, v, j + u);
-                const S *xr = xl + (int64_t)cu * K;
+                const int32_t cu = __shfl_sync(kFullMask, c, (j + u) & 31);
+                a[u] = __shfl_sync(kFullMask, v, (j + u) & 31);
+                if (j + u < n) {   // warp-uniform
+                    const S *xr = xl + (int64_t)cu * K;
 #pragma unroll
-                for (int q = 0; q < VPT; ++q)
-                    if (vm[q]) x[u][q] = ldg_frag<S, VEC>(xr + q * STR);
+                    for (int q = 0; q < VPT; ++q)
+                        if (vm[q]) x[u][q] = ldg_frag<S, VEC>(xr + q * STR);
+                }
             }
 #pragma unroll
             for (int u = 0; u < U; ++u)
+                if (j + u < n)
 #pragma unroll
-                for (int q = 0; q < VPT; ++q)
-                    if (vm[q])
+                    for (int q = 0; q < VPT; ++q)
+                        if (vm[q])
 #pragma unroll
-                        for (int t = 0; t < VEC; ++t) acc[q].v[t] = fma(a[u], x[u][q].v[t], acc[q].v[t]);
-        }
-        for (; j < n; ++j) {
-            const int32_t cu = __shfl_sync(kFullMask, c, j);
-            const S au = __shfl_sync(kFullMask, v, j);
-            const S *xr = xl + (int64_t)cu * K;
-#pragma unroll
-            for (int q = 0; q < VPT; ++q)
-                if (vm[q]) {
-                    const Frag<S, VEC> x = ldg_frag<S, VEC>(xr + q * STR);
-#pragma unroll
-                    for (int t = 0; t < VEC; ++t) acc[q].v[t] = fma(au, x.v[t], acc[q].v[t]);
-                }
+                            for (int t = 0; t < VEC; ++t) acc[q].v[t] = fma(a[u], x[u][q].v[t], acc[q].v[t]);
         }
     }
 }
@@ -495,6 +487,76 @@ __global__ void __launch_bounds__(32 * kRemWarps, 2) rem_tile_kernel(const BooPa
     }
 }
 
+
+// ---- short rows through the plan's row view ----
+//
+// Matrices of a few entries per row (a 2-D Laplacian: 5) are latency bound in
+// the block kernel: a CTA walks its group's blocks through shared memory in a
+// chain of dependent loads.  With the plan's row-ordered copy of every entry
+// a warp takes one row: its row pointers, its (column, value) pairs in one
+// coalesced load, then every X row of the row in flight at once.  Warps take
+// the positions of row groups [rg0, rg1) in the row-group order (row =
+// row_ids[k]), so a range covers exactly its rows; 24 warps per SM.
+constexpr int kShortWarps = 8;
+
+template <typename S, int VEC, int VPT>
+__global__ void __launch_bounds__(32 * kShortWarps, 3) row_warp_kernel(const BooParams<S> p, int64_t rg0, int64_t rg1) {
+    constexpr int SLAB = 32 * VPT * VEC;
+    const int lane = threadIdx.x & 31;
+    const int64_t f0 = (int64_t)blockIdx.y * SLAB + (int64_t)lane * VEC;
+    bool vm[VPT];
+#pragma unroll
+    for (int q = 0; q < VPT; ++q) vm[q] = f0 + (int64_t)q * 32 * VEC < p.K;
+    const int64_t nwarps = (int64_t)gridDim.x * kShortWarps;
+    const int64_t k0 = __ldg(p.row_grp_ptr + rg0), k1 = __ldg(p.row_grp_ptr + rg1);
+    for (int64_t bt = blockIdx.z; bt < p.batch; bt += gridDim.z) {
+        const S *xl = p.X + bt * p.cols * p.K + f0;
+        S *yb = p.Y + bt * p.rows * p.K + f0;
+        for (int64_t k = k0 + (int64_t)blockIdx.x * kShortWarps + (threadIdx.x >> 5); k < k1; k += nwarps) {
+            const int64_t row = __ldg(p.row_ids + k);
+            const int64_t e0 = __ldg(p.rem_indptr + row), e1 = __ldg(p.rem_indptr + row + 1);
+            const int32_t c = e0 + lane < e1 ? __ldg(p.rem_col + e0 + lane) : 0;
+            const S v = e0 + lane < e1 ? __ldg(p.rem_val + e0 + lane) : S(0);
+            Frag<S, VEC> acc[VPT];
+#pragma unroll
+            for (int q = 0; q < VPT; ++q)
+#pragma unroll
+                for (int u = 0; u < VEC; ++u) acc[q].v[u] = S(0);
+            rem_span<S, VEC, VPT, 8 / VPT>(acc, p.rem_col, p.rem_val, e0, e1, c, v, xl, p.K, vm, lane);
+            rem_store_row<S, VEC, VPT>(yb + row * p.K, acc, vm);
+        }
+    }
+}
+
+template <typename S, int VEC, int VPT>
+int launch_row_warp(const BooParams<S> &p, int64_t rg0, int64_t rg1, int64_t max_nr, cudaStream_t s) {
+    constexpr int SLAB = 32 * VPT * VEC;
+    const int64_t slabs = ceil_div(p.K, SLAB);
+    if (slabs > 65535) return SPMM_EUNSUPPORTED;
+    if (rg1 <= rg0) return SPMM_OK;
+    int dev = 0, sms = 0;
+    SPMM_CUDA_TRY(cudaGetDevice(&dev));
+    SPMM_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const int64_t bound = (rg1 - rg0) * max_nr < p.rows ? (rg1 - rg0) * max_nr : p.rows;   // rows of the range
+    const int64_t want = ceil_div(bound > 0 ? bound : 1, (int64_t)kShortWarps);
+    const int64_t cap = (int64_t)sms * 3 * 8;   // resident CTAs, a few waves each
+    const unsigned bz = (unsigned)(p.batch < 65535 ? p.batch : 65535);
+    dim3 grid((unsigned)(want < cap ? want : cap), (unsigned)slabs, bz);
+    row_warp_kernel<S, VEC, VPT><<<grid, 32 * kShortWarps, 0, s>>>(p, rg0, rg1);
+    SPMM_PRODUCT_LAUNCHED();
+    return SPMM_OK;
+}
+
+template <typename S>
+int row_warp_dispatch(const BooParams<S> &p, int64_t rg0, int64_t rg1, int64_t max_nr, bool aligned,
+                      cudaStream_t s) {
+    constexpr int V = 16 / (int)sizeof(S);
+    if (aligned && p.K % V == 0) {
+        if (p.K <= 32 * V) return launch_row_warp<S, V, 1>(p, rg0, rg1, max_nr, s);
+        return launch_row_warp<S, V, 2>(p, rg0, rg1, max_nr, s);
+    }
+    return launch_row_warp<S, 1, 4>(p, rg0, rg1, max_nr, s);
+}
 
 // ---- nnz-flat remainder (default on the aligned path) ----
 //
@@ -1008,6 +1070,13 @@ int boo_matmul_impl(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch
     // then the block kernel adds blocks and tail where a row group has any
     p.skip_rem = A->rem_nnz > 0 && 2 * A->rem_nnz >= A->total_nnz;
     if (p.skip_rem && (rg0 != 0 || rg1 != A->n_rg)) return SPMM_EUNSUPPORTED;   // whole matrix only
+    if (plan && pl.row_view && pl.short_rows) {
+        // a warp per row over the plan's row-ordered copy, rows of groups [rg0, rg1)
+        p.rem_indptr = reinterpret_cast<const int32_t *>(plan + pl.rv_ptr);
+        p.rem_col = reinterpret_cast<const int32_t *>(plan + pl.rv_col);
+        p.rem_val = reinterpret_cast<const S *>(plan + pl.rv_val);
+        return row_warp_dispatch<S>(p, rg0, rg1, A->max_nr, aligned, s);
+    }
     if (plan && pl.row_view) {
         // the plan's row-ordered copy of every entry: one load-balanced pass writes Y
         p.rem_indptr = reinterpret_cast<const int32_t *>(plan + pl.rv_ptr);

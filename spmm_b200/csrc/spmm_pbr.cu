@@ -171,21 +171,44 @@ pbr_stripe_kernel(const PbrParams<S, I> p) {
         for (int r = 0; r < BR; ++r)
 #pragma unroll
             for (int q = 0; q < VEC; ++q) acc[r].v[q] = S(0);
-        for (int64_t b = b0; b < b1; ++b) {
-            const uint64_t code = __ldg(p.codes + b);
-            const int64_t off = (int64_t)__ldg(p.offsets + b);
-            const int64_t col0 = (int64_t)__ldg(p.coords + 2 * b + 1);
+        // block b's code, first value and first column; its values a lane each
+        // (64 at most: two registers); the next block's are fetched while
+        // block b's X rows are in flight, so a block costs one load latency
+        uint64_t code = 0;
+        int64_t col0 = 0;
+        S v_lo = S(0), v_hi = S(0);
+        if (b0 < b1) {
+            code = __ldg(p.codes + b0);
+            const int64_t off = (int64_t)__ldg(p.offsets + b0);
+            col0 = (int64_t)__ldg(p.coords + 2 * b0 + 1);
             const int n = __popcll(code);
-            const S v_lo = lane < n ? __ldg(p.data + off + lane) : S(0);
-            const S v_hi = lane + 32 < n ? __ldg(p.data + off + 32 + lane) : S(0);
+            v_lo = lane < n ? __ldg(p.data + off + lane) : S(0);
+            v_hi = lane + 32 < n ? __ldg(p.data + off + 32 + lane) : S(0);
+        }
+        for (int64_t b = b0; b < b1; ++b) {
+            // every used column's X row in flight at once
+            Frag<S, VEC> x[BC];
+            unsigned used = 0;
 #pragma unroll
             for (int c = 0; c < BC; ++c) {
                 uint64_t colbits = 0;
 #pragma unroll
                 for (int r = 0; r < BR; ++r) colbits |= code & (1ull << (r * BC + c));
-                if (!colbits || col0 + c >= p.cols) continue;   // uniform across the warp
-                Frag<S, VEC> x;
-                if (fm) x = ldg_frag<S, VEC>(xl + (col0 + c) * p.K);
+                if (colbits && col0 + c < p.cols) {   // uniform across the warp
+                    used |= 1u << c;
+                    if (fm) x[c] = ldg_frag<S, VEC>(xl + (col0 + c) * p.K);
+                }
+            }
+            uint64_t ncode = 0;
+            int64_t noff = 0, ncol0 = 0;
+            if (b + 1 < b1) {
+                ncode = __ldg(p.codes + b + 1);
+                noff = (int64_t)__ldg(p.offsets + b + 1);
+                ncol0 = (int64_t)__ldg(p.coords + 2 * b + 3);
+            }
+#pragma unroll
+            for (int c = 0; c < BC; ++c) {
+                if (!((used >> c) & 1u)) continue;
 #pragma unroll
                 for (int r = 0; r < BR; ++r) {
                     const int bit = r * BC + c;
@@ -196,10 +219,17 @@ pbr_stripe_kernel(const PbrParams<S, I> p) {
                         const S a = rank < 32 ? lo : hi;
                         if (fm)
 #pragma unroll
-                            for (int q = 0; q < VEC; ++q) acc[r].v[q] = fma(a, x.v[q], acc[r].v[q]);
+                            for (int q = 0; q < VEC; ++q) acc[r].v[q] = fma(a, x[c].v[q], acc[r].v[q]);
                     }
                 }
             }
+            if (b + 1 < b1) {
+                const int n = __popcll(ncode);
+                v_lo = lane < n ? __ldg(p.data + noff + lane) : S(0);
+                v_hi = lane + 32 < n ? __ldg(p.data + noff + 32 + lane) : S(0);
+            }
+            code = ncode;
+            col0 = ncol0;
         }
         S *yb = p.Y + bt * p.rows * p.K + f0;
 #pragma unroll

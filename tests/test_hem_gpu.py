@@ -22,7 +22,27 @@ def _cases():
     ties = sp.csr_matrix(np.kron(np.eye(40), np.ones((3, 5))))      # identical rows: ties everywhere
     empty_rows = sp.random(300, 300, density=0.03, format='csr', random_state=2).tolil()
     empty_rows[50:80] = 0
+    # rows sharing column pools: 600 rows of ~10,800 incidences (counted by
+    # sorting), 600 of ~6,000 (the 512-thread hash tables), sparse rows after
+    pr, pc = [], []
+    for r in range(1600):
+        if r < 600:
+            c = rng.choice(200, 60, replace=False)
+        elif r < 1200:
+            c = 200 + rng.choice(250, 50, replace=False)
+        else:
+            c = rng.choice(1600, 5, replace=False)
+        pr += [r] * c.size
+        pc += list(c)
+    pools = sp.csr_matrix((np.ones(len(pr)), (pr, pc)), shape=(1600, 1600))
+    # one row over every column: each other row's heaviest neighbour, so the
+    # level graph gives it ~5,000 edges (picked by a CTA of its own)
+    sr = [0] * 5000 + list(np.repeat(np.arange(1, 5000), 3))
+    sc = list(range(5000)) + [int(c) for i in range(1, 5000) for c in (i, (7 * i + 1) % 5000, (13 * i + 2) % 5000)]
+    star = sp.csr_matrix((np.ones(len(sr)), (sr, sc)), shape=(5000, 5000))
     return {
+        'star': star,
+        'pools': pools,
         'fem3d': workloads.fem3d(n=5),
         'laplacian2d': workloads.laplacian2d(n=30),
         'powerlaw': workloads.powerlaw(n=3000),

@@ -39,6 +39,7 @@ def _groups_call(dev, x, y, rg0, rg1, engine):
 @pytest.mark.parametrize('name,gen,kw,target', [
     ('fem3d', workloads.fem3d, dict(n=10), 32),
     ('blockdiag', workloads.blockdiag, dict(n_blocks=20, b=64), 64),
+    ('laplacian2d', workloads.laplacian2d, dict(n=64), 32),     # short rows: a warp per row
 ])
 def test_ranges_reassemble_the_product(cuda, engine, name, gen, kw, target):
     mat = gen(**kw)

@@ -48,7 +48,9 @@ def _plan_size(s, f32=True):
     if f32 and s['nb'] > 0 and s['max_nr'] <= 64 and s['max_nc'] <= 64:
         n += al(s['nb']) + al(4 * (s['n_rg'] + 1)) + al(8 * s['nb'])
     entries = s['nnz_c'] + s['rem_nnz'] + s['tail_nnz']
-    if s['rem_nnz'] > 0 and 2 * s['rem_nnz'] >= s['total_nnz'] and 64 * (s['nnz_c'] + s['tail_nnz']) >= entries:
+    rem_major = s['rem_nnz'] > 0 and 2 * s['rem_nnz'] >= s['total_nnz']
+    short_rows = not rem_major and 0 < entries <= 16 * s['rows']
+    if (rem_major and 64 * (s['nnz_c'] + s['tail_nnz']) >= entries) or short_rows:
         n += al(4 * (s['rows'] + 1)) + al(4 * entries) + al((4 if f32 else 8) * entries)
     return n
 
@@ -128,6 +130,30 @@ def test_plan_without_row_view(cuda):
     assert 0 < L.spmm_boo_plan_workspace_size(C.byref(st))          # the packing pass only
     x = torch.randn(mat.shape[1], 64, generator=torch.Generator().manual_seed(3)).cuda()
     assert torch.equal(_product(dev, x, 'auto', True), _product(dev, x, 'auto', False))
+
+
+@pytest.mark.parametrize('dtype', [np.float32, np.float64])
+@pytest.mark.parametrize('k', [128, 7, 300])
+@pytest.mark.parametrize('cluster', ['identity', 'random'])
+def test_short_rows_through_the_row_view(cuda, dtype, k, cluster):
+    """A few entries per row (2-D Laplacian, tail entries from a small-block
+    threshold): the plan holds the row-ordered copy and a warp per row
+    computes Y, rows in any group order, any K, two batches."""
+    mat = workloads.laplacian2d(n=70).astype(dtype)
+    boo = S.csr_to_boo(mat, cluster=cluster, target_nr=32, target_nc=32, small_block_threshold=40,
+                       small_block_policy='tail_batch')
+    s = boo._sizes
+    assert s['nnz_c'] + s['rem_nnz'] + s['tail_nnz'] <= 16 * s['rows']
+    dev = boo.to('cuda')
+    st = dev._dev_struct(dev._gpu_meta)
+    assert _lib.lib().spmm_boo_plan_size(C.byref(st)) == _plan_size(s, dtype == np.float32)
+    tdt = torch.float32 if dtype == np.float32 else torch.float64
+    x = torch.from_numpy(np.random.default_rng(k).standard_normal((2, mat.shape[1], k))).to(tdt)
+    ref = _oracle(boo, x.numpy())
+    bound = abs_bound(mat.indptr, mat.indices, mat.data, x.numpy())
+    with_plan = _product(dev, x.cuda(), 'cuda_cores', True).cpu().numpy()
+    assert_spmm_close(with_plan, ref, bound, TOL[np.dtype(dtype)])
+    np.testing.assert_array_equal(S.boo_matmul(dev, x.cuda()).cpu().numpy(), with_plan)
 
 
 def test_plan_arguments(cuda):
