@@ -163,7 +163,7 @@ def hem_labels_gpu(pat: sp.csr_matrix, target: int, max_size: Optional[int], max
     import ctypes as C
 
     from . import _lib
-    from ._device import default_device, ptr, stream_handle
+    from ._device import default_device, ptr, stream_handle, to_device
     if not torch.cuda.is_available():
         raise RuntimeError("cluster='hem' runs on the GPU (spmm_hem_labels); no CUDA device is available")
     n, m = pat.shape
@@ -174,8 +174,8 @@ def hem_labels_gpu(pat: sp.csr_matrix, target: int, max_size: Optional[int], max
     L = _lib.lib()
     dev = default_device()
     with torch.cuda.device(dev):
-        indptr = torch.from_numpy(np.ascontiguousarray(pat.indptr, dtype=np.int64)).to(dev)
-        indices = torch.from_numpy(np.ascontiguousarray(pat.indices, dtype=np.int32)).to(dev)
+        indptr = to_device(pat.indptr, dev, np.int64)
+        indices = to_device(pat.indices, dev, np.int32)
         labels = torch.empty(n, dtype=torch.int64, device=dev)
         slots = int(L.spmm_hem_level_slots(int(target))) if hierarchy is not None else 0
         levels = torch.empty((slots, n), dtype=torch.int64, device=dev) if slots else None

@@ -11,13 +11,27 @@
 //     of every stored entry (the CSR view spmm_boo_to_csr produces), so one
 //     load-balanced nnz-flat pass computes Y (plan.cuh: plan_row_view_rem);
 //   * the same copy for matrices of a few entries per row, multiplied a warp
-//     per row (plan.cuh: plan_short_rows).
+//     per row (plan.cuh: plan_short_rows), with a flag telling whether the
+//     row-group order is the identity (the product then skips row_ids).
 // The plan lives in a caller-owned device buffer; the product reads it
 // through spmm_launch_cfg::plan.
 #include "plan.cuh"
 
 namespace spmm {
 namespace {
+
+__global__ void fill_i32_kernel(int32_t *__restrict__ out, int64_t n, int32_t v) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        out[i] = v;
+}
+
+// *flag = 0 when some position k holds another row than k (the flag starts at 1).
+__global__ void ident_kernel(const int32_t *__restrict__ row_ids, int64_t rows, int32_t *__restrict__ flag) {
+    bool same = true;
+    for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < rows; k += (int64_t)gridDim.x * blockDim.x)
+        same &= row_ids[k] == k;
+    if (!__all_sync(0xffffffffu, same) && (threadIdx.x & 31) == 0) *flag = 0;
+}
 
 // rg_blk[rg] = first block whose row group is >= rg, for rg in [0, n_rg].
 __global__ void rg_blk_kernel(const int32_t *__restrict__ blk_row_grp, int64_t nb, int64_t n_rg,
@@ -132,6 +146,14 @@ extern "C" int spmm_boo_plan_build(const spmm_boo_dev *A, void *plan, size_t pla
         pack_fill_kernel<<<grid_for(A->nb > A->n_rg + 1 ? A->nb : A->n_rg + 1, 256), 256, 0, s>>>(
             qmask, count, A->nb, reinterpret_cast<const int32_t *>(base + L.rg_blk), A->n_rg,
             reinterpret_cast<int32_t *>(base + L.slots), reinterpret_cast<int32_t *>(base + L.rg_slot));
+        SPMM_LAUNCH_CHECK();
+    }
+    if (L.short_rows) {
+        if (!A->row_ids) return SPMM_EINVAL;
+        int32_t *flag = reinterpret_cast<int32_t *>(base + L.rv_ident);
+        fill_i32_kernel<<<1, 32, 0, s>>>(flag, 1, 1);
+        SPMM_LAUNCH_CHECK();
+        ident_kernel<<<grid_for(A->rows, 256), 256, 0, s>>>(A->row_ids, A->rows, flag);
         SPMM_LAUNCH_CHECK();
     }
     if (L.row_view)

@@ -24,6 +24,7 @@ struct PlanLayout {
     size_t rv_ptr;      // row view (row_view only): int32[rows + 1] row pointers,
     size_t rv_col;      //   int32[entries] columns,
     size_t rv_val;      //   scalar[entries] values: every stored entry, rows ordered by (column, value)
+    size_t rv_ident;    // short_rows only: int32, 1 when row_ids[k] == k for every position k
     size_t total;
     bool row_view;
     bool short_rows;    // the row view serves a warp-per-row product (not remainder-major)
@@ -92,6 +93,10 @@ inline PlanLayout plan_layout(const spmm_boo_dev *A) {
         off += plan_align(4 * (size_t)L.entries);
         L.rv_val = off;
         off += plan_align(sb * (size_t)L.entries);
+    }
+    if (L.short_rows) {
+        L.rv_ident = off;
+        off += plan_align(4);
     }
     L.total = off;
     return L;

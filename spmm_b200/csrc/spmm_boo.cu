@@ -500,7 +500,7 @@ __global__ void __launch_bounds__(32 * kRemWarps, 2) rem_tile_kernel(const BooPa
 constexpr int kShortWarps = 8;
 
 template <typename S, int VEC, int VPT>
-__global__ void __launch_bounds__(32 * kShortWarps, 3) row_warp_kernel(const BooParams<S> p, int64_t rg0, int64_t rg1) {
+__global__ void __launch_bounds__(32 * kShortWarps, 3) row_warp_kernel(const BooParams<S> p, int64_t rg0, int64_t rg1, const int32_t *__restrict__ ident) {
     constexpr int SLAB = 32 * VPT * VEC;
     const int lane = threadIdx.x & 31;
     const int64_t f0 = (int64_t)blockIdx.y * SLAB + (int64_t)lane * VEC;
@@ -509,12 +509,25 @@ __global__ void __launch_bounds__(32 * kShortWarps, 3) row_warp_kernel(const Boo
     for (int q = 0; q < VPT; ++q) vm[q] = f0 + (int64_t)q * 32 * VEC < p.K;
     const int64_t nwarps = (int64_t)gridDim.x * kShortWarps;
     const int64_t k0 = __ldg(p.row_grp_ptr + rg0), k1 = __ldg(p.row_grp_ptr + rg1);
+    const bool same = __ldg(ident) != 0;   // row_ids[k] == k: one dependent load less per row
     for (int64_t bt = blockIdx.z; bt < p.batch; bt += gridDim.z) {
         const S *xl = p.X + bt * p.cols * p.K + f0;
         S *yb = p.Y + bt * p.rows * p.K + f0;
-        for (int64_t k = k0 + (int64_t)blockIdx.x * kShortWarps + (threadIdx.x >> 5); k < k1; k += nwarps) {
-            const int64_t row = __ldg(p.row_ids + k);
-            const int64_t e0 = __ldg(p.rem_indptr + row), e1 = __ldg(p.rem_indptr + row + 1);
+        int64_t k = k0 + (int64_t)blockIdx.x * kShortWarps + (threadIdx.x >> 5);
+        // this row's entry range, and the next row's fetched while this one runs
+        int64_t row = 0, e0 = 0, e1 = 0;
+        if (k < k1) {
+            row = same ? k : (int64_t)__ldg(p.row_ids + k);
+            e0 = __ldg(p.rem_indptr + row);
+            e1 = __ldg(p.rem_indptr + row + 1);
+        }
+        for (; k < k1; k += nwarps) {
+            int64_t nrow = 0, n0 = 0, n1 = 0;
+            if (k + nwarps < k1) {
+                nrow = same ? k + nwarps : (int64_t)__ldg(p.row_ids + k + nwarps);
+                n0 = __ldg(p.rem_indptr + nrow);
+                n1 = __ldg(p.rem_indptr + nrow + 1);
+            }
             const int32_t c = e0 + lane < e1 ? __ldg(p.rem_col + e0 + lane) : 0;
             const S v = e0 + lane < e1 ? __ldg(p.rem_val + e0 + lane) : S(0);
             Frag<S, VEC> acc[VPT];
@@ -524,12 +537,16 @@ __global__ void __launch_bounds__(32 * kShortWarps, 3) row_warp_kernel(const Boo
                 for (int u = 0; u < VEC; ++u) acc[q].v[u] = S(0);
             rem_span<S, VEC, VPT, 8 / VPT>(acc, p.rem_col, p.rem_val, e0, e1, c, v, xl, p.K, vm, lane);
             rem_store_row<S, VEC, VPT>(yb + row * p.K, acc, vm);
+            row = nrow;
+            e0 = n0;
+            e1 = n1;
         }
     }
 }
 
 template <typename S, int VEC, int VPT>
-int launch_row_warp(const BooParams<S> &p, int64_t rg0, int64_t rg1, int64_t max_nr, cudaStream_t s) {
+int launch_row_warp(const BooParams<S> &p, int64_t rg0, int64_t rg1, int64_t max_nr, const int32_t *ident,
+                    cudaStream_t s) {
     constexpr int SLAB = 32 * VPT * VEC;
     const int64_t slabs = ceil_div(p.K, SLAB);
     if (slabs > 65535) return SPMM_EUNSUPPORTED;
@@ -542,20 +559,20 @@ int launch_row_warp(const BooParams<S> &p, int64_t rg0, int64_t rg1, int64_t max
     const int64_t cap = (int64_t)sms * 3 * 8;   // resident CTAs, a few waves each
     const unsigned bz = (unsigned)(p.batch < 65535 ? p.batch : 65535);
     dim3 grid((unsigned)(want < cap ? want : cap), (unsigned)slabs, bz);
-    row_warp_kernel<S, VEC, VPT><<<grid, 32 * kShortWarps, 0, s>>>(p, rg0, rg1);
+    row_warp_kernel<S, VEC, VPT><<<grid, 32 * kShortWarps, 0, s>>>(p, rg0, rg1, ident);
     SPMM_PRODUCT_LAUNCHED();
     return SPMM_OK;
 }
 
 template <typename S>
-int row_warp_dispatch(const BooParams<S> &p, int64_t rg0, int64_t rg1, int64_t max_nr, bool aligned,
-                      cudaStream_t s) {
+int row_warp_dispatch(const BooParams<S> &p, int64_t rg0, int64_t rg1, int64_t max_nr, const int32_t *ident,
+                      bool aligned, cudaStream_t s) {
     constexpr int V = 16 / (int)sizeof(S);
     if (aligned && p.K % V == 0) {
-        if (p.K <= 32 * V) return launch_row_warp<S, V, 1>(p, rg0, rg1, max_nr, s);
-        return launch_row_warp<S, V, 2>(p, rg0, rg1, max_nr, s);
+        if (p.K <= 32 * V) return launch_row_warp<S, V, 1>(p, rg0, rg1, max_nr, ident, s);
+        return launch_row_warp<S, V, 2>(p, rg0, rg1, max_nr, ident, s);
     }
-    return launch_row_warp<S, 1, 4>(p, rg0, rg1, max_nr, s);
+    return launch_row_warp<S, 1, 4>(p, rg0, rg1, max_nr, ident, s);
 }
 
 // ---- nnz-flat remainder (default on the aligned path) ----
@@ -1075,7 +1092,8 @@ int boo_matmul_impl(const spmm_boo_dev *A, const void *X, void *Y, int64_t batch
         p.rem_indptr = reinterpret_cast<const int32_t *>(plan + pl.rv_ptr);
         p.rem_col = reinterpret_cast<const int32_t *>(plan + pl.rv_col);
         p.rem_val = reinterpret_cast<const S *>(plan + pl.rv_val);
-        return row_warp_dispatch<S>(p, rg0, rg1, A->max_nr, aligned, s);
+        return row_warp_dispatch<S>(p, rg0, rg1, A->max_nr, reinterpret_cast<const int32_t *>(plan + pl.rv_ident),
+                                    aligned, s);
     }
     if (plan && pl.row_view) {
         // the plan's row-ordered copy of every entry: one load-balanced pass writes Y

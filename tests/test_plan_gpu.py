@@ -52,6 +52,8 @@ def _plan_size(s, f32=True):
     short_rows = not rem_major and 0 < entries <= 16 * s['rows']
     if (rem_major and 64 * (s['nnz_c'] + s['tail_nnz']) >= entries) or short_rows:
         n += al(4 * (s['rows'] + 1)) + al(4 * entries) + al((4 if f32 else 8) * entries)
+    if short_rows:
+        n += al(4)                                  # the identity-order flag
     return n
 
 
