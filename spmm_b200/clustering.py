@@ -79,7 +79,7 @@ def _dense_rank(labels: np.ndarray) -> np.ndarray:
     return np.searchsorted(u, labels).astype(np.int64)
 
 
-def _enforce_caps(labels: np.ndarray, row_nnz: np.ndarray, max_size: Optional[int],
+def _enforce_caps(labels: np.ndarray, row_nnz: Optional[np.ndarray], max_size: Optional[int],
                   max_nnz: Optional[int]) -> np.ndarray:
     """Split every group into pieces that respect the caps.
 
@@ -100,12 +100,12 @@ def _enforce_caps(labels: np.ndarray, row_nnz: np.ndarray, max_size: Optional[in
     g = labels[order]
     heads = np.flatnonzero(np.r_[True, g[1:] != g[:-1]])
     glen = np.diff(np.r_[heads, n])
-    nz = np.asarray(row_nnz, dtype=np.int64)[order]
     piece = np.zeros(n, dtype=np.int64)                # piece index inside its group, sorted order
     if max_nnz is None:                                # size cap alone: fixed-size pieces
         pos = np.arange(n) - np.repeat(heads, glen)
         piece = pos // max(int(max_size), 1)
     else:
+        nz = np.asarray(row_nnz, dtype=np.int64)[order]
         cur = np.zeros(heads.size, dtype=np.int64)     # per group: current piece, members, load
         cnt = np.ones(heads.size, dtype=np.int64)
         load = nz[heads].copy()
@@ -131,18 +131,20 @@ def _enforce_caps(labels: np.ndarray, row_nnz: np.ndarray, max_size: Optional[in
 _COUNT_METHODS = ('identity', 'random', 'degree')
 
 
-def _axis_nnz(csr: sp.csr_matrix) -> Tuple[np.ndarray, np.ndarray]:
-    """Distinct nonzero columns per row and distinct nonzero rows per column."""
+def _axis_nnz(csr: sp.csr_matrix, axis: int) -> np.ndarray:
+    """Distinct nonzero columns per row (axis 0) or rows per column (axis 1)."""
     a = csr if csr.has_canonical_format else _pattern(csr)
-    return np.diff(a.indptr), np.bincount(a.indices, minlength=a.shape[1])
+    return np.diff(a.indptr) if axis == 0 else np.bincount(a.indices, minlength=a.shape[1])
 
 
-def _count_labels(method: str, row_nnz: np.ndarray, target: int, max_size: Optional[int],
+def _count_labels(method: str, n: int, counts, target: int, max_size: Optional[int],
                   max_nnz: Optional[int], seed: int) -> np.ndarray:
-    """Labels of the methods that need only the members' nonzero counts."""
-    n = row_nnz.size
+    """Labels of the methods that need only the members' nonzero counts;
+    `counts()` gives them and is called only when needed (degree order, or
+    a nonzero cap)."""
     if n == 0:
         return np.zeros(0, dtype=np.int32)
+    row_nnz = counts() if method == 'degree' or max_nnz is not None else None
     if method == 'identity':
         labels = np.arange(n, dtype=np.int64) // max(target, 1)
     elif method == 'random':
@@ -213,7 +215,8 @@ def cluster_axis(mat, method: str = 'hem', target: int = 32, max_size: Optional[
         raise ImportError("cluster='metis' requires pymetis, which is not installed; "
                           'no HEM fallback is performed')
     if method in _COUNT_METHODS:
-        return _count_labels(method, _axis_nnz(sp.csr_matrix(mat))[0], target, max_size, max_nnz, seed)
+        csr = sp.csr_matrix(mat)
+        return _count_labels(method, csr.shape[0], lambda: _axis_nnz(csr, 0), target, max_size, max_nnz, seed)
     pat = _pattern(mat)
     n = pat.shape[0]
     if n == 0:
@@ -249,11 +252,12 @@ def cluster_axes(mat, method: str = 'hem', target_nr: int = 32, target_nc: int =
         # These labels depend on each axis's member count and nonzero counts
         # only: a symmetric pattern gives equal row and column counts, so the
         # columns' own labels equal the rows' and no symmetry test is needed.
-        row_nnz, col_nnz = _axis_nnz(csr)
-        rows = _count_labels(method, row_nnz, target_nr, max_nr, max_block_nnz, seed)
+        rows = _count_labels(method, csr.shape[0], lambda: _axis_nnz(csr, 0), target_nr, max_nr, max_block_nnz,
+                             seed)
         if symmetric:
             return rows, rows.copy()
-        return rows, _count_labels(method, col_nnz, target_nc, max_nc, max_block_nnz, seed)
+        return rows, _count_labels(method, csr.shape[1], lambda: _axis_nnz(csr, 1), target_nc, max_nc,
+                                   max_block_nnz, seed)
     if symmetric is None:
         symmetric = target_nr == target_nc and is_pattern_symmetric(csr)
     common = dict(method=method, max_nnz=max_block_nnz, seed=seed, hub_degree=hub_degree, topk=topk,

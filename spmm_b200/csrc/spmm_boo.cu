@@ -496,11 +496,11 @@ __global__ void __launch_bounds__(32 * kRemWarps, 2) rem_tile_kernel(const BooPa
 // a warp takes one row: its row pointers, its (column, value) pairs in one
 // coalesced load, then every X row of the row in flight at once.  Warps take
 // the positions of row groups [rg0, rg1) in the row-group order (row =
-// row_ids[k]), so a range covers exactly its rows; 24 warps per SM.
+// row_ids[k]), so a range covers exactly its rows; 16 warps per SM.
 constexpr int kShortWarps = 8;
 
 template <typename S, int VEC, int VPT>
-__global__ void __launch_bounds__(32 * kShortWarps, 3) row_warp_kernel(const BooParams<S> p, int64_t rg0, int64_t rg1, const int32_t *__restrict__ ident) {
+__global__ void __launch_bounds__(32 * kShortWarps, 2) row_warp_kernel(const BooParams<S> p, int64_t rg0, int64_t rg1, const int32_t *__restrict__ ident) {
     constexpr int SLAB = 32 * VPT * VEC;
     const int lane = threadIdx.x & 31;
     const int64_t f0 = (int64_t)blockIdx.y * SLAB + (int64_t)lane * VEC;
@@ -514,22 +514,39 @@ __global__ void __launch_bounds__(32 * kShortWarps, 3) row_warp_kernel(const Boo
         const S *xl = p.X + bt * p.cols * p.K + f0;
         S *yb = p.Y + bt * p.rows * p.K + f0;
         int64_t k = k0 + (int64_t)blockIdx.x * kShortWarps + (threadIdx.x >> 5);
-        // this row's entry range, and the next row's fetched while this one runs
+        // Software pipeline over this warp's rows k, k + nwarps, ...: while a
+        // row's X rows are in flight, the next row's (column, value) pairs and
+        // the range of the row after it are fetched, so a row costs one load
+        // latency, not three.
         int64_t row = 0, e0 = 0, e1 = 0;
+        int32_t c = 0;
+        S v = S(0);
         if (k < k1) {
             row = same ? k : (int64_t)__ldg(p.row_ids + k);
             e0 = __ldg(p.rem_indptr + row);
             e1 = __ldg(p.rem_indptr + row + 1);
+            c = e0 + lane < e1 ? __ldg(p.rem_col + e0 + lane) : 0;
+            v = e0 + lane < e1 ? __ldg(p.rem_val + e0 + lane) : S(0);
+        }
+        int64_t nrow = 0, n0 = 0, n1 = 0;
+        if (k + nwarps < k1) {
+            nrow = same ? k + nwarps : (int64_t)__ldg(p.row_ids + k + nwarps);
+            n0 = __ldg(p.rem_indptr + nrow);
+            n1 = __ldg(p.rem_indptr + nrow + 1);
         }
         for (; k < k1; k += nwarps) {
-            int64_t nrow = 0, n0 = 0, n1 = 0;
-            if (k + nwarps < k1) {
-                nrow = same ? k + nwarps : (int64_t)__ldg(p.row_ids + k + nwarps);
-                n0 = __ldg(p.rem_indptr + nrow);
-                n1 = __ldg(p.rem_indptr + nrow + 1);
+            int32_t nc = 0;
+            S nv = S(0);
+            if (k + nwarps < k1 && n0 + lane < n1) {
+                nc = __ldg(p.rem_col + n0 + lane);
+                nv = __ldg(p.rem_val + n0 + lane);
             }
-            const int32_t c = e0 + lane < e1 ? __ldg(p.rem_col + e0 + lane) : 0;
-            const S v = e0 + lane < e1 ? __ldg(p.rem_val + e0 + lane) : S(0);
+            int64_t mrow = 0, m0 = 0, m1 = 0;
+            if (k + 2 * nwarps < k1) {
+                mrow = same ? k + 2 * nwarps : (int64_t)__ldg(p.row_ids + k + 2 * nwarps);
+                m0 = __ldg(p.rem_indptr + mrow);
+                m1 = __ldg(p.rem_indptr + mrow + 1);
+            }
             Frag<S, VEC> acc[VPT];
 #pragma unroll
             for (int q = 0; q < VPT; ++q)
@@ -540,6 +557,11 @@ __global__ void __launch_bounds__(32 * kShortWarps, 3) row_warp_kernel(const Boo
             row = nrow;
             e0 = n0;
             e1 = n1;
+            c = nc;
+            v = nv;
+            nrow = mrow;
+            n0 = m0;
+            n1 = m1;
         }
     }
 }
@@ -556,7 +578,7 @@ int launch_row_warp(const BooParams<S> &p, int64_t rg0, int64_t rg1, int64_t max
     SPMM_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const int64_t bound = (rg1 - rg0) * max_nr < p.rows ? (rg1 - rg0) * max_nr : p.rows;   // rows of the range
     const int64_t want = ceil_div(bound > 0 ? bound : 1, (int64_t)kShortWarps);
-    const int64_t cap = (int64_t)sms * 3 * 8;   // resident CTAs, a few waves each
+    const int64_t cap = (int64_t)sms * 2;   // resident CTAs: every warp walks its rows pipelined
     const unsigned bz = (unsigned)(p.batch < 65535 ? p.batch : 65535);
     dim3 grid((unsigned)(want < cap ? want : cap), (unsigned)slabs, bz);
     row_warp_kernel<S, VEC, VPT><<<grid, 32 * kShortWarps, 0, s>>>(p, rg0, rg1, ident);

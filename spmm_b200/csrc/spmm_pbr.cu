@@ -145,17 +145,21 @@ pbr_spmm_kernel(const PbrParams<S, I> p) {
 // Block-major matrices (most entries in blocks, e.g. a mesh stiffness pattern
 // in 8 x 8 blocks): a warp owns one stripe of BR rows and a slab of 32 VEC
 // features, with the BR rows' sums in registers.  Per block the warp loads
-// the block's values once (two coalesced loads, handed out by shuffles at
-// each bit's rank -- the reference's bit-order consumption) and one X row per
-// block column that has a set bit, instead of one X row per nonzero; then
-// the BR rows' remainder entries; every Y element is stored once.
+// the block's values once (two coalesced loads, handed out by shuffles in bit
+// order -- the reference's consumption order) and one X row per block column
+// that has a set bit, instead of one X row per nonzero, into the warp's
+// shared-memory slots; then it walks only the set bits, row by row (the row's
+// sum stays a register), reading the column's X slot.  Then the BR rows'
+// remainder entries; every Y element is stored once.
 constexpr int kStripeWarps = 8;
 
 template <typename S, typename I, int VEC, int BR, int BC>
-__global__ void __launch_bounds__(32 * kStripeWarps, 2)
+__global__ void __launch_bounds__(32 * kStripeWarps, 3)
 pbr_stripe_kernel(const PbrParams<S, I> p) {
     static_assert(BR * BC <= 64 && BR <= 8 && BC <= 8, "block shape");
+    __shared__ Frag<S, VEC> xs[kStripeWarps][BC][32];   // per warp: the block's X rows, a lane's slice each
     const int lane = threadIdx.x & 31;
+    Frag<S, VEC> (&xw)[BC][32] = xs[threadIdx.x >> 5];
     const int64_t stripe = (int64_t)blockIdx.x * kStripeWarps + (threadIdx.x >> 5);
     const int64_t row0 = stripe * BR;
     if (row0 >= p.rows) return;
@@ -186,8 +190,7 @@ pbr_stripe_kernel(const PbrParams<S, I> p) {
             v_hi = lane + 32 < n ? __ldg(p.data + off + 32 + lane) : S(0);
         }
         for (int64_t b = b0; b < b1; ++b) {
-            // every used column's X row in flight at once
-            Frag<S, VEC> x[BC];
+            // every used column's X row in flight at once, into the warp's slots
             unsigned used = 0;
 #pragma unroll
             for (int c = 0; c < BC; ++c) {
@@ -196,7 +199,7 @@ pbr_stripe_kernel(const PbrParams<S, I> p) {
                 for (int r = 0; r < BR; ++r) colbits |= code & (1ull << (r * BC + c));
                 if (colbits && col0 + c < p.cols) {   // uniform across the warp
                     used |= 1u << c;
-                    if (fm) x[c] = ldg_frag<S, VEC>(xl + (col0 + c) * p.K);
+                    if (fm) xw[c][lane] = ldg_frag<S, VEC>(xl + (col0 + c) * p.K);
                 }
             }
             uint64_t ncode = 0;
@@ -206,23 +209,26 @@ pbr_stripe_kernel(const PbrParams<S, I> p) {
                 noff = (int64_t)__ldg(p.offsets + b + 1);
                 ncol0 = (int64_t)__ldg(p.coords + 2 * b + 3);
             }
+            __syncwarp();
+            // the set bits in order: row r's bits, lowest column first; the
+            // value of the k-th set bit is the block's k-th value
+            int rank = 0;
 #pragma unroll
-            for (int c = 0; c < BC; ++c) {
-                if (!((used >> c) & 1u)) continue;
+            for (int r = 0; r < BR; ++r) {
+                uint32_t rb = (uint32_t)(code >> (r * BC)) & ((1u << BC) - 1u);
+                while (rb) {   // uniform across the warp
+                    const int c = __ffs(rb) - 1;
+                    rb &= rb - 1u;
+                    const S a = __shfl_sync(kFullMask, rank < 32 ? v_lo : v_hi, rank & 31);   // rank is uniform
+                    ++rank;
+                    if (fm && ((used >> c) & 1u)) {
+                        const Frag<S, VEC> x = xw[c][lane];
 #pragma unroll
-                for (int r = 0; r < BR; ++r) {
-                    const int bit = r * BC + c;
-                    if ((code >> bit) & 1ull) {
-                        const int rank = __popcll(code & ((1ull << bit) - 1ull));
-                        const S lo = __shfl_sync(kFullMask, v_lo, rank & 31);
-                        const S hi = __shfl_sync(kFullMask, v_hi, rank & 31);
-                        const S a = rank < 32 ? lo : hi;
-                        if (fm)
-#pragma unroll
-                            for (int q = 0; q < VEC; ++q) acc[r].v[q] = fma(a, x[c].v[q], acc[r].v[q]);
+                        for (int q = 0; q < VEC; ++q) acc[r].v[q] = fma(a, x.v[q], acc[r].v[q]);
                     }
                 }
             }
+            __syncwarp();   // the slots are rewritten by the next block
             if (b + 1 < b1) {
                 const int n = __popcll(ncode);
                 v_lo = lane < n ? __ldg(p.data + noff + lane) : S(0);
