@@ -533,12 +533,18 @@ def product_launcher(A, fmt, x, y, engine, slab_features=0):
             raise _lib.SpmmError(v, 'bench (device status)')
 
     s = A._sizes
+    entries = s['nnz_c'] + s['rem_nnz'] + (s.get('tail_nnz', 0) if fmt == 'boo' else 0)
     if fmt == 'pbr':
-        tag = 'pbr'
+        # block-major matrices (blocks hold >= half of the nonzeros) with a full
+        # warp slab of features: a warp per stripe (spmm_pbr.cu pbr_dispatch)
+        block_major = 2 * s['nnz_c'] >= s['nnz_c'] + s['rem_nnz']
+        tag = 'pbr_stripe' if block_major and K % 4 == 0 and K >= 128 else 'pbr'
     elif runs_on_tensor_cores(A, K, engine):
         tag = 'tc'
     elif s['rem_nnz'] > 0 and 2 * s['rem_nnz'] >= s['total_nnz']:
         tag = 'rem'
+    elif 0 < entries <= 16 * s['rows']:
+        tag = 'rows'     # short rows: a warp per row over the plan's row-ordered copy (plan.cuh)
     else:
         tag = 'cc'
     launch.keep = (buf, cfg, st, plan)
@@ -550,7 +556,9 @@ KERNELS = {'tc': 'boo_gather_kernel + boo_tc_kernel (one spmm_boo_matmul call)',
            'rem': 'rem_flat_plan_kernel + rem_flat_kernel + rem_flat_fix_kernel (+ boo_spmm_kernel adding '
                   'blocks and tail, unless the product plan holds a row-ordered copy of every entry; one '
                   'spmm_boo_matmul call)',
-           'pbr': 'pbr_spmm_kernel'}
+           'rows': 'row_warp_kernel (a warp per row over the product plan\'s row-ordered copy of every entry)',
+           'pbr': 'pbr_spmm_kernel',
+           'pbr_stripe': 'pbr_stripe_kernel (a warp per 8-row stripe)'}
 
 
 def cusparse_best(mat, x, timer, steps):

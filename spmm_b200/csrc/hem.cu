@@ -495,8 +495,15 @@ __global__ void diff_kernel(const int64_t *__restrict__ ptr, int64_t n, int64_t 
 // select on the key (wmax - w) << jb | j (unique per row) and emitted as both
 // directions of the directed edge.  No sort of the incidences is needed.
 constexpr int kHashThreads = 256;
-constexpr int kSmemSlots = 8192;    // small rows: 64 KB of (key, count) slots, 3 CTAs per SM
+constexpr int kTinySlots = 4096;    // most rows: 32 KB of (key, count) slots, more CTAs per SM
+constexpr int kSmemSlots = 8192;    // small rows: 64 KB, 3 CTAs per SM
 constexpr int kMidSlots = 16384;    // mid rows: 128 KB, one CTA of 512 threads per SM
+
+// Tables of (class_lo(SLOTS), SLOTS] slots are counted by the launch of SLOTS
+// (0: the global-memory class, above kMidSlots).
+__host__ __device__ constexpr int64_t class_lo(int slots) {
+    return slots == kTinySlots ? 0 : slots == kSmemSlots ? kTinySlots : slots == kMidSlots ? kSmemSlots : kMidSlots;
+}
 
 // Slots of a row's table: a power of two, at least 64 and twice the row's incidences (0: no table).
 inline int64_t table_slots(int64_t inc) {
@@ -626,9 +633,8 @@ __global__ void __launch_bounds__(THREADS) hash_topk_kernel(
         int lg = 6;
         while ((1ll << lg) < 2 * inc) ++lg;
         const int64_t S = 1ll << lg;
-        const int64_t lo_cap = SLOTS == kSmemSlots ? 0 : SLOTS == 0 ? kMidSlots : kSmemSlots;
         const int64_t hi_cap = SLOTS == 0 ? INT64_MAX : SLOTS;
-        if (S <= lo_cap || S > hi_cap) continue;   // another launch's rows
+        if (S <= class_lo(SLOTS) || S > hi_cap) continue;   // another launch's rows
         int32_t *key = skey;
         uint32_t *cnt = scnt;
         if (SLOTS == 0) {   // the row's region of the global tables
@@ -659,11 +665,33 @@ __global__ void __launch_bounds__(THREADS) hash_topk_kernel(
             }
         }
         __syncthreads();
+        int64_t live = S;   // slots the selection reads
+        if (SLOTS == 0) {
+            // a global table is at most half full: its occupied slots move to
+            // the front (in slot order, a block of slots at a time: every
+            // write lands at or before a slot already read), so the selection
+            // passes read only them
+            __shared__ int ctot;
+            int64_t base = 0;
+            for (int64_t c0 = 0; c0 < S; c0 += THREADS) {
+                const int64_t t = c0 + tid;
+                const int32_t kk = t < S ? key[t] : -1;
+                const uint32_t cc = t < S ? cnt[t] : 0u;
+                const int pos = block_exclusive_scan<int, THREADS>(kk >= 0 ? 1 : 0, &ctot);
+                if (kk >= 0) {
+                    key[base + pos] = kk;
+                    cnt[base + pos] = cc;
+                }
+                base += ctot;
+            }
+            live = base;
+            __syncthreads();
+        }
         unsigned long long U, W, kth;
-        count_and_select<THREADS>(key, cnt, S, jb, topk, sm, U, W, kth);
+        count_and_select<THREADS>(key, cnt, live, jb, topk, sm, U, W, kth);
         if (U == 0) continue;
         // emit the kept entries, both directions
-        for (int64_t t = tid; t < S; t += THREADS) {
+        for (int64_t t = tid; t < live; t += THREADS) {
             const int32_t j = key[t];
             if (j < 0) continue;
             const uint32_t w = cnt[t];
@@ -791,18 +819,27 @@ int similarity_graph(const int64_t *ptr, const int32_t *idx, int64_t n, int64_t 
         DBuf<unsigned long long> ecnt;
         SPMM_TRY(ecnt.alloc(1, s));
         SPMM_CUDA_TRY(cudaMemsetAsync(ecnt.p, 0, 8, s));
-        const size_t smem = (size_t)kSmemSlots * 8;
+        auto tiny = hash_topk_kernel<kHashThreads, kTinySlots>;
         auto small = hash_topk_kernel<kHashThreads, kSmemSlots>;
         auto mid = hash_topk_kernel<512, kMidSlots>;
-        SPMM_CUDA_TRY(cudaFuncSetAttribute(small, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        SPMM_CUDA_TRY(cudaFuncSetAttribute(tiny, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)((size_t)kTinySlots * 8)));
+        SPMM_CUDA_TRY(cudaFuncSetAttribute(small, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)((size_t)kSmemSlots * 8)));
         SPMM_CUDA_TRY(cudaFuncSetAttribute(mid, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)((size_t)kMidSlots * 8)));
-        int dev = 0, sms = 0;
+        int dev = 0, sms = 0, per_sm = 0;
         SPMM_CUDA_TRY(cudaGetDevice(&dev));
         SPMM_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        SPMM_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tiny, kHashThreads,
+                                                                    (size_t)kTinySlots * 8));
+        tiny<<<(unsigned)std::min<int64_t>(n, (int64_t)sms * std::max(per_sm, 1)), kHashThreads,
+               (size_t)kTinySlots * 8, s>>>(pptr.p, pidx.p, tptr.p, trow.p, pinc.p, goff.p, gkey.p, gcnt.p, n, jb,
+                                            topk, ecnt.p, ek0.p, ew0.p);
+        SPMM_LAUNCH_CHECK();
         const int64_t grid = std::min<int64_t>(n, (int64_t)sms * 3);
-        small<<<(unsigned)grid, kHashThreads, smem, s>>>(pptr.p, pidx.p, tptr.p, trow.p, pinc.p, goff.p, gkey.p,
-                                                         gcnt.p, n, jb, topk, ecnt.p, ek0.p, ew0.p);
+        small<<<(unsigned)grid, kHashThreads, (size_t)kSmemSlots * 8, s>>>(
+            pptr.p, pidx.p, tptr.p, trow.p, pinc.p, goff.p, gkey.p, gcnt.p, n, jb, topk, ecnt.p, ek0.p, ew0.p);
         SPMM_LAUNCH_CHECK();
         mid<<<(unsigned)std::min<int64_t>(n, sms), 512, (size_t)kMidSlots * 8, s>>>(
             pptr.p, pidx.p, tptr.p, trow.p, pinc.p, goff.p, gkey.p, gcnt.p, n, jb, topk, ecnt.p, ek0.p, ew0.p);
