@@ -540,7 +540,7 @@ def product_launcher(A, fmt, x, y, engine, slab_features=0):
         block_major = 2 * s['nnz_c'] >= s['nnz_c'] + s['rem_nnz']
         tag = 'pbr_stripe' if block_major and K % 4 == 0 and K >= 128 else 'pbr'
     elif runs_on_tensor_cores(A, K, engine):
-        tag = 'tc'
+        tag = 'tc_tf32' if engine == 'tensor_cores_tf32' else 'tc'
     elif s['rem_nnz'] > 0 and 2 * s['rem_nnz'] >= s['total_nnz']:
         tag = 'rem'
     elif 0 < entries <= 16 * s['rows']:
@@ -552,6 +552,7 @@ def product_launcher(A, fmt, x, y, engine, slab_features=0):
 
 
 KERNELS = {'tc': 'boo_gather_kernel + boo_tc_kernel (one spmm_boo_matmul call)',
+           'tc_tf32': 'boo_gather_kernel + boo_tc_kernel, one tf32 term (opt-in engine, 2e-3 tolerance)',
            'cc': 'boo_spmm_kernel',
            'rem': 'rem_flat_plan_kernel + rem_flat_kernel + rem_flat_fix_kernel (+ boo_spmm_kernel adding '
                   'blocks and tail, unless the product plan holds a row-ordered copy of every entry; one '
