@@ -191,17 +191,16 @@ pbr_stripe_kernel(const PbrParams<S, I> p) {
         }
         for (int64_t b = b0; b < b1; ++b) {
             // every used column's X row in flight at once, into the warp's slots
-            unsigned used = 0;
+            // (the block's column mask: the OR of its BR row masks)
+            uint32_t colmask = 0;
 #pragma unroll
-            for (int c = 0; c < BC; ++c) {
-                uint64_t colbits = 0;
+            for (int r = 0; r < BR; ++r) colmask |= (uint32_t)(code >> (r * BC));
+            colmask &= (1u << BC) - 1u;
+            if (col0 + BC > p.cols) colmask &= (1u << (p.cols > col0 ? p.cols - col0 : 0)) - 1u;
+            const unsigned used = colmask;
 #pragma unroll
-                for (int r = 0; r < BR; ++r) colbits |= code & (1ull << (r * BC + c));
-                if (colbits && col0 + c < p.cols) {   // uniform across the warp
-                    used |= 1u << c;
-                    if (fm) xw[c][lane] = ldg_frag<S, VEC>(xl + (col0 + c) * p.K);
-                }
-            }
+            for (int c = 0; c < BC; ++c)
+                if (((used >> c) & 1u) && fm) xw[c][lane] = ldg_frag<S, VEC>(xl + (col0 + c) * p.K);
             uint64_t ncode = 0;
             int64_t noff = 0, ncol0 = 0;
             if (b + 1 < b1) {
