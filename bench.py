@@ -542,7 +542,13 @@ def product_launcher(A, fmt, x, y, engine, slab_features=0):
     elif runs_on_tensor_cores(A, K, engine):
         tag = 'tc_tf32' if engine == 'tensor_cores_tf32' else 'tc'
     elif s['rem_nnz'] > 0 and 2 * s['rem_nnz'] >= s['total_nnz']:
-        tag = 'rem'
+        # a short remainder at narrow K goes half a warp per row by default
+        # (spmm_boo.cu rem_by_row); the plan's row view, where built, replaces it
+        view = 64 * (s['nnz_c'] + s['tail_nnz']) >= entries
+        n_rem = entries if view else s['rem_nnz']
+        vec = 4 if x.dtype == torch.float32 else 2
+        half = slab_features == 0 and K % vec == 0 and K <= 16 * vec and n_rem <= 16 * s['rows']
+        tag = 'rem_half' if half else 'rem'
     elif 0 < entries <= 16 * s['rows']:
         tag = 'rows'     # short rows: a warp per row over the plan's row-ordered copy (plan.cuh)
     else:
@@ -557,6 +563,8 @@ KERNELS = {'tc': 'boo_gather_kernel + boo_tc_kernel (one spmm_boo_matmul call)',
            'rem': 'rem_flat_plan_kernel + rem_flat_kernel + rem_flat_fix_kernel (+ boo_spmm_kernel adding '
                   'blocks and tail, unless the product plan holds a row-ordered copy of every entry; one '
                   'spmm_boo_matmul call)',
+           'rem_half': 'row_half_kernel + rem_long_kernel (half a warp per row of the remainder; rows over 1,024 '
+                       'entries by CTAs) + boo_spmm_kernel adding blocks and tail (one spmm_boo_matmul call)',
            'rows': 'row_warp_kernel (a warp per row over the product plan\'s row-ordered copy of every entry)',
            'pbr': 'pbr_spmm_kernel',
            'pbr_stripe': 'pbr_stripe_kernel (a warp per 8-row stripe)'}

@@ -144,9 +144,12 @@ typedef struct {
  * boo_kernel.cu:58-99) have no counterpart here. */
 typedef struct {
     int32_t version;        /* 1, or 2 (adds `status`) */
-    int32_t slab_features;  /* remainder-major BOO products: 0 = the nnz-flat remainder with
-                             * X rows staged by asynchronous copies (default); < 0 = rows
-                             * through registers (no workspace); > 0 is taken as 0 */
+    int32_t slab_features;  /* remainder-major BOO products: 0 = automatic (default): half a
+                             * warp per row for a remainder of <= 16 entries per row on
+                             * average with K <= 64 float32 / 32 float64 (no workspace),
+                             * else the nnz-flat chunks with X rows staged by asynchronous
+                             * copies; > 0 = the nnz-flat chunks; < 0 = rows through
+                             * registers (no workspace) */
     int32_t engine;         /* enum spmm_engine (BOO product only; PBR ignores it) */
     int32_t wait_us;        /* bounded device waits of the tensor-core product: 0 = about
                              * 2 s (default); > 0 = give up after about this many

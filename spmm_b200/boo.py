@@ -523,8 +523,9 @@ def boo_matmul(boo_mat, x: torch.Tensor, threads: int = 256, p: int = 64,
     or 'tensor_cores_tf32' (opt-in, one tf32 product: tf32 accuracy, about
     2e-3 relative, never chosen by 'auto').  ``slab_features`` (not in the
     reference) selects the remainder kernels of a remainder-major matrix: 0
-    (default) the nnz-flat chunks, a negative value the register path (no
-    workspace).  ``wait_us`` (not in the reference) bounds the tensor-core
+    (default) the nnz-flat chunks, or half a warp per row for a remainder of
+    at most 16 entries per row with K up to 64 (float32) / 32 (float64); a
+    positive value the nnz-flat chunks; a negative value the register path.  ``wait_us`` (not in the reference) bounds the tensor-core
     product's device waits (0: about 2 s); a product whose wait expired
     leaves Y incomplete and reports SPMM_ETIMEOUT through
     ``product_status(y)`` / ``check_product(y)`` (GPU ``x``; a CPU ``x``

@@ -597,6 +597,78 @@ int row_warp_dispatch(const BooParams<S> &p, int64_t rg0, int64_t rg1, int64_t m
     return launch_row_warp<S, 1, 4>(p, rg0, rg1, max_nr, ident, s);
 }
 
+// Narrow features (K <= 16 VEC, e.g. 64 floats): half a warp per row, two
+// rows per warp, so no lane idles.  Each half loads its row's (column, value)
+// pairs 16 at a time and hands them out by 16-wide shuffles; the warp walks to
+// the longer of its two rows (a uniform trip count keeps the shuffles
+// converged), each half predicating its own entries, 8 X rows in flight.
+// Rows of more than kLongRow entries are left to rem_long_kernel when
+// skip_long is set.
+template <typename S, int VEC>
+__global__ void __launch_bounds__(256, 2) row_half_kernel(const BooParams<S> p, int skip_long) {
+    constexpr int U = 8;
+    const int lane = threadIdx.x & 31, half = lane >> 4, hl = lane & 15;
+    const int64_t f0 = (int64_t)hl * VEC;
+    const bool fm = f0 < p.K;
+    const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int64_t npairs = (p.rows + 1) / 2;
+    for (int64_t bt = blockIdx.z; bt < p.batch; bt += gridDim.z) {
+        const S *xl = p.X + bt * p.cols * p.K + f0;
+        S *yb = p.Y + bt * p.rows * p.K + f0;
+        for (int64_t q = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); q < npairs; q += nwarps) {
+            const int64_t k = 2 * q + half;
+            const bool valid = k < p.rows;
+            const int64_t row = valid ? (int64_t)__ldg(p.row_ids + k) : 0;
+            const int64_t e0 = valid ? (int64_t)__ldg(p.rem_indptr + row) : 0;
+            int64_t n = valid ? (int64_t)__ldg(p.rem_indptr + row + 1) - e0 : 0;
+            const bool mine = valid && !(skip_long && n > kLongRow);
+            if (!mine) n = 0;
+            int64_t nmax = n;
+            const int64_t other = __shfl_xor_sync(kFullMask, nmax, 16);
+            nmax = other > nmax ? other : nmax;
+            Frag<S, VEC> acc;
+#pragma unroll
+            for (int t = 0; t < VEC; ++t) acc.v[t] = S(0);
+            for (int64_t b = 0; b < nmax; b += 16) {
+                const int32_t c = b + hl < n ? __ldg(p.rem_col + e0 + b + hl) : 0;
+                const S v = b + hl < n ? __ldg(p.rem_val + e0 + b + hl) : S(0);
+                const int m = nmax - b < 16 ? (int)(nmax - b) : 16;                 // uniform
+                const int mh = n - b < 16 ? (n - b > 0 ? (int)(n - b) : 0) : 16;     // this half's
+                for (int j = 0; j < m; j += U) {
+                    Frag<S, VEC> x[U];
+                    S a[U];
+#pragma unroll
+                    for (int u = 0; u < U; ++u) {
+                        const int32_t cu = __shfl_sync(kFullMask, c, (j + u) & 15, 16);
+                        a[u] = __shfl_sync(kFullMask, v, (j + u) & 15, 16);
+                        if (j + u < mh && fm) x[u] = ldg_frag<S, VEC>(xl + (int64_t)cu * p.K);
+                    }
+#pragma unroll
+                    for (int u = 0; u < U; ++u)
+                        if (j + u < mh && fm)
+#pragma unroll
+                            for (int t = 0; t < VEC; ++t) acc.v[t] = fma(a[u], x[u].v[t], acc.v[t]);
+                }
+            }
+            if (mine && fm) st_frag<S, VEC>(yb + row * p.K, acc);
+        }
+    }
+}
+
+template <typename S, int VEC>
+int launch_row_half(const BooParams<S> &p, int skip_long, cudaStream_t s) {
+    if (p.rows <= 0) return SPMM_OK;
+    int dev = 0, sms = 0;
+    SPMM_CUDA_TRY(cudaGetDevice(&dev));
+    SPMM_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const int64_t want = ceil_div((p.rows + 1) / 2, (int64_t)8);
+    const int64_t cap = (int64_t)sms * 2 * 4;   // a few waves of resident CTAs
+    const unsigned bz = (unsigned)(p.batch < 65535 ? p.batch : 65535);
+    row_half_kernel<S, VEC><<<dim3((unsigned)(want < cap ? want : cap), 1, bz), 256, 0, s>>>(p, skip_long);
+    SPMM_PRODUCT_LAUNCHED();
+    return SPMM_OK;
+}
+
 // ---- nnz-flat remainder (default on the aligned path) ----
 //
 // The CSR remainder is cut into chunks of `chunk` consecutive entries,
@@ -964,7 +1036,7 @@ int launch_rem_flat(BooParams<S> p, int sms, unsigned bz, void *ws, cudaStream_t
 // and Y, the default), else rows of at most kLongRow entries at full width
 // through registers, then the long rows.
 template <typename S, int VEC, int VPT>
-int launch_rem(const BooParams<S> &p, bool flat, void *ws, cudaStream_t s) {
+int launch_rem(const BooParams<S> &p, bool flat, bool by_row, void *ws, cudaStream_t s) {
     constexpr int SLAB = 32 * VPT * VEC;
     const int64_t slabs = ceil_div(p.K, SLAB);
     if (slabs > 65535) return SPMM_EUNSUPPORTED;
@@ -975,10 +1047,18 @@ int launch_rem(const BooParams<S> &p, bool flat, void *ws, cudaStream_t s) {
     if constexpr (VEC > 1) {
         if (flat) return launch_rem_flat<S, VEC, VPT>(p, sms, bz, ws, s);
     }
-    const int64_t tile_ctas = ceil_div(ceil_div(p.rows, (int64_t)32), (int64_t)kRemWarps);
-    const int64_t g1 = tile_ctas < (int64_t)sms * 8 ? tile_ctas : (int64_t)sms * 8;
-    rem_tile_kernel<S, VEC, VPT><<<dim3((unsigned)g1, (unsigned)slabs, bz), 32 * kRemWarps, 0, s>>>(p);
-    SPMM_PRODUCT_LAUNCHED();
+    if constexpr (VEC > 1) {
+        if (by_row) {   // narrow features, short rows: half a warp per row; long rows below
+            const int rc = launch_row_half<S, VEC>(p, 1, s);
+            if (rc != SPMM_OK) return rc;
+        }
+    }
+    if (!by_row || VEC == 1) {
+        const int64_t tile_ctas = ceil_div(ceil_div(p.rows, (int64_t)32), (int64_t)kRemWarps);
+        const int64_t g1 = tile_ctas < (int64_t)sms * 8 ? tile_ctas : (int64_t)sms * 8;
+        rem_tile_kernel<S, VEC, VPT><<<dim3((unsigned)g1, (unsigned)slabs, bz), 32 * kRemWarps, 0, s>>>(p);
+        SPMM_PRODUCT_LAUNCHED();
+    }
     const int64_t g2 = ceil_div(p.rows, (int64_t)(32 * kLongWarps));
     if (g2 > 0x7fffffffLL) return SPMM_EUNSUPPORTED;
     rem_long_kernel<S, VEC, VPT><<<dim3((unsigned)g2, (unsigned)slabs, bz), 32 * kLongWarps, 0, s>>>(p);
@@ -991,20 +1071,31 @@ int launch_rem(const BooParams<S> &p, bool flat, void *ws, cudaStream_t s) {
 template <typename S>
 constexpr int rem_vec() { return 16 / (int)sizeof(S); }
 
+// Remainders of at most kShortRow entries per row on average with narrow
+// features (K <= 16 vectors: one half warp covers a row) go half a warp per
+// row by default; slab_features > 0 forces the nnz-flat chunks, < 0 the
+// register path.
+template <typename S>
+bool rem_by_row(const BooParams<S> &p, bool aligned, int slab_req) {
+    return aligned && slab_req == 0 && p.K % rem_vec<S>() == 0 && p.K <= 16 * rem_vec<S>() &&
+           p.rem_nnz <= kShortRow * p.rows;
+}
+
 template <typename S>
 bool rem_flat_applies(const BooParams<S> &p, bool aligned, int slab_req) {
-    return aligned && p.K % rem_vec<S>() == 0 && slab_req >= 0;
+    return aligned && p.K % rem_vec<S>() == 0 && slab_req >= 0 && !rem_by_row(p, aligned, slab_req);
 }
 
 template <typename S>
 int rem_dispatch(const BooParams<S> &p, bool aligned, int slab_req, void *ws, cudaStream_t s) {
     constexpr int V = rem_vec<S>();
     const bool flat = rem_flat_applies(p, aligned, slab_req);
+    const bool by_row = rem_by_row(p, aligned, slab_req);
     if (aligned && p.K % V == 0) {
-        if (p.K <= 32 * V) return launch_rem<S, V, 1>(p, flat, ws, s);
-        return launch_rem<S, V, 2>(p, flat, ws, s);
+        if (p.K <= 32 * V) return launch_rem<S, V, 1>(p, flat, by_row, ws, s);
+        return launch_rem<S, V, 2>(p, flat, by_row, ws, s);
     }
-    return launch_rem<S, 1, 4>(p, false, ws, s);
+    return launch_rem<S, 1, 4>(p, false, false, ws, s);
 }
 
 template <typename S>
@@ -1202,5 +1293,8 @@ extern "C" size_t spmm_boo_matmul_workspace_size(const spmm_boo_dev *A, int64_t 
     const size_t elem = A->scalar_type == SPMM_F32 ? 4 : 8;
     if (!rem_major || (cfg && cfg->slab_features < 0) || K % (int64_t)(16 / elem)) return 0;
     const bool row_view = cfg && cfg->version >= 2 && cfg->plan && plan_row_view(A);
-    return rem_flat_workspace(row_view ? A->nnz_c + A->rem_nnz + A->tail_nnz : A->rem_nnz, batch, K, elem);
+    const int64_t entries = row_view ? A->nnz_c + A->rem_nnz + A->tail_nnz : A->rem_nnz;
+    if ((!cfg || cfg->slab_features == 0) && K <= 16 * (int64_t)(16 / elem) && entries <= kShortRow * A->rows)
+        return 0;   // half a warp per row, no scratch
+    return rem_flat_workspace(entries, batch, K, elem);
 }

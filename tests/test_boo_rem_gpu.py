@@ -39,7 +39,8 @@ def _check(mat, boo, x, slabs=(0,)):
         assert torch.equal(got, S.boo_matmul(dev, xd, slab_features=slab))   # deterministic
 
 
-# slab_features: the nnz-flat chunks (0, and positive values, taken as 0) and
+# slab_features: automatic (0: the nnz-flat chunks, or half a warp per row
+# for a short remainder at K <= 16 vectors), the nnz-flat chunks (> 0) and
 # the register path (< 0)
 SLABS = {np.float32: (0, -1, 16), np.float64: (0, -1, 8)}
 
@@ -81,9 +82,10 @@ def test_remainder_major_deterministic(cuda):
 def test_product_launch_counter(cuda):
     """spmm_product_launches counts the kernels each product launches: four
     for a remainder-major BOO matrix (nnz-flat plan, chunks, fix-up, block
-    kernel; three on the register path: tiles, long rows, block kernel), two
-    for the tensor-core product (gather pass + worker kernel), one for the
-    CUDA-core block kernel."""
+    kernel; three on the register path: tiles, long rows, block kernel; three
+    for its short remainder at K = 64 by default: half a warp per row, long
+    rows, block kernel), two for the tensor-core product (gather pass +
+    worker kernel), one for the CUDA-core block kernel."""
     from spmm_b200 import _lib, workloads
     L = _lib.lib()
     mat = _skewed(1200, 5000, 2, np.float32)
@@ -91,8 +93,10 @@ def test_product_launch_counter(cuda):
     fem = workloads.fem3d(n=6)
     blk = S.csr_to_boo(fem, cluster='identity', target_nr=32, target_nc=32).to('cuda')
     xr = torch.randn(5000, 128, device='cuda')
+    xn = torch.randn(5000, 64, device='cuda')
     xb = torch.randn(fem.shape[1], 128, device='cuda')
     cases = [(rem, xr, dict(), 4), (rem, xr, dict(slab_features=-1), 3),
+             (rem, xn, dict(), 3), (rem, xn, dict(slab_features=1), 4),
              (blk, xb, dict(engine='tensor_cores'), 2), (blk, xb, dict(engine='cuda_cores'), 1)]
     for boo, x, kw, want in cases:
         n0 = L.spmm_product_launches()
