@@ -10,6 +10,9 @@
 //   * for remainder-major matrices with scattered blocks, a row-ordered copy
 //     of every stored entry (the CSR view spmm_boo_to_csr produces), so one
 //     load-balanced nnz-flat pass computes Y (plan.cuh: plan_row_view_rem);
+//   * for tensor-core matrices, whether the column order is the identity
+//     (64-column panels are then read straight from X, not from a gathered
+//     copy);
 //   * the same copy for matrices of a few entries per row, multiplied a warp
 //     per row (plan.cuh: plan_short_rows), with a flag telling whether the
 //     row-group order is the identity (the product then skips row_ids).
@@ -147,6 +150,14 @@ extern "C" int spmm_boo_plan_build(const spmm_boo_dev *A, void *plan, size_t pla
             qmask, count, A->nb, reinterpret_cast<const int32_t *>(base + L.rg_blk), A->n_rg,
             reinterpret_cast<int32_t *>(base + L.slots), reinterpret_cast<int32_t *>(base + L.rg_slot));
         SPMM_LAUNCH_CHECK();
+        if (A->cols && !A->col_ids) return SPMM_EINVAL;
+        int32_t *cflag = reinterpret_cast<int32_t *>(base + L.cg_ident);
+        fill_i32_kernel<<<1, 32, 0, s>>>(cflag, 1, 1);
+        SPMM_LAUNCH_CHECK();
+        if (A->cols) {
+            ident_kernel<<<grid_for(A->cols, 256), 256, 0, s>>>(A->col_ids, A->cols, cflag);
+            SPMM_LAUNCH_CHECK();
+        }
     }
     if (L.short_rows) {
         if (!A->row_ids) return SPMM_EINVAL;

@@ -19,6 +19,8 @@ struct PlanLayout {
                         //   through a packed tensor-core tile, not the CUDA cores;
     size_t rg_slot;     //   int32[n_rg + 1]: first packed slot of each row group;
     size_t slots;       //   int32[2 nb]: packed slots, block * 16 + quad (4 columns of its group)
+    size_t cg_ident;    //   int32, 1 when col_ids[k] == k for every k (column groups are runs of
+                        //   consecutive X rows: 64-column panels are read straight from X)
     bool packing;
     int pw;             //   panel width of the tensor-core product (32 or 64 columns)
     size_t rv_ptr;      // row view (row_view only): int32[rows + 1] row pointers,
@@ -85,6 +87,8 @@ inline PlanLayout plan_layout(const spmm_boo_dev *A) {
         off += plan_align(4 * (size_t)(A->n_rg + 1));
         L.slots = off;
         off += plan_align(8 * (size_t)A->nb);
+        L.cg_ident = off;
+        off += plan_align(4);
     }
     if (L.row_view) {
         L.rv_ptr = off;

@@ -46,7 +46,7 @@ def _plan_size(s, f32=True):
     al = lambda v: (v + 255) // 256 * 256          # noqa: E731
     n = al(4 * (s['n_rg'] + 1))
     if f32 and s['nb'] > 0 and s['max_nr'] <= 64 and s['max_nc'] <= 64:
-        n += al(s['nb']) + al(4 * (s['n_rg'] + 1)) + al(8 * s['nb'])
+        n += al(s['nb']) + al(4 * (s['n_rg'] + 1)) + al(8 * s['nb']) + al(4)   # + identity-column flag
     entries = s['nnz_c'] + s['rem_nnz'] + s['tail_nnz']
     rem_major = s['rem_nnz'] > 0 and 2 * s['rem_nnz'] >= s['total_nnz']
     short_rows = not rem_major and 0 < entries <= 16 * s['rows']
