@@ -831,6 +831,21 @@ def native_arm(args):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(mat, cfg, x.cpu().numpy(), fmt)
     build = build_line(build_s, int(mat.nnz), cpu) if world == 1 else None
+    if build is not None and split != 'rows':
+        # the same build once more in this (now warm) process: pinned staging
+        # buffers and device pools already exist; the cold figure above stays
+        # the one `gpu_over_cpu` is computed from
+        tw = time.perf_counter()
+        A2 = (S.csr_to_boo(mat, cluster=args.grouping, target_nr=cfg['target'], target_nc=cfg['target'])
+              if fmt == 'boo' else S.csr_to_pbr(mat, 8, 8, 4))
+        A2.to(dev)
+        torch.cuda.synchronize(dev)
+        warm_s = time.perf_counter() - tw
+        del A2
+        build['gpu_s_warm'] = round(warm_s, 4)
+        build['gpu_nnz_per_s_warm'] = round(mat.nnz / warm_s)
+        if build.get('cpu_nnz_per_s'):
+            build['gpu_over_cpu_warm'] = round(build['gpu_nnz_per_s_warm'] / build['cpu_nnz_per_s'], 2)
     if cpu is not None:
         cpu = {k: v for k, v in cpu.items() if not k.startswith('build')}
 
