@@ -496,11 +496,19 @@ __global__ void __launch_bounds__(32 * kRemWarps, 2) rem_tile_kernel(const BooPa
 // a warp takes one row: its row pointers, its (column, value) pairs in one
 // coalesced load, then every X row of the row in flight at once.  Warps take
 // the positions of row groups [rg0, rg1) in the row-group order (row =
-// row_ids[k]), so a range covers exactly its rows; 16 warps per SM.
+// row_ids[k]), so a range covers exactly its rows.  float32 with one vector
+// per lane: 24 warps per SM, X rows in batches of 6 to stay within the
+// registers (2-D Laplacian 0.051 -> 0.041 ms against 16 warps per SM with
+// batches of 8); other shapes keep 16 warps per SM and batches of 8.
 constexpr int kShortWarps = 8;
 
+// Blocks per SM of row_warp_kernel: float32 rows of one vector per lane fit
+// three (X rows in batches of 6); other shapes two (batches of 8).
+template <typename S, int VPT>
+__host__ __device__ constexpr int row_warp_ctas() { return VPT == 1 && sizeof(S) == 4 ? 3 : 2; }
+
 template <typename S, int VEC, int VPT>
-__global__ void __launch_bounds__(32 * kShortWarps, 2) row_warp_kernel(const BooParams<S> p, int64_t rg0, int64_t rg1, const int32_t *__restrict__ ident) {
+__global__ void __launch_bounds__(32 * kShortWarps, row_warp_ctas<S, VPT>()) row_warp_kernel(const BooParams<S> p, int64_t rg0, int64_t rg1, const int32_t *__restrict__ ident) {
     constexpr int SLAB = 32 * VPT * VEC;
     const int lane = threadIdx.x & 31;
     const int64_t f0 = (int64_t)blockIdx.y * SLAB + (int64_t)lane * VEC;
@@ -552,7 +560,7 @@ __global__ void __launch_bounds__(32 * kShortWarps, 2) row_warp_kernel(const Boo
             for (int q = 0; q < VPT; ++q)
 #pragma unroll
                 for (int u = 0; u < VEC; ++u) acc[q].v[u] = S(0);
-            rem_span<S, VEC, VPT, 8 / VPT>(acc, p.rem_col, p.rem_val, e0, e1, c, v, xl, p.K, vm, lane);
+            rem_span<S, VEC, VPT, row_warp_ctas<S, VPT>() == 3 ? 6 : 8 / VPT>(acc, p.rem_col, p.rem_val, e0, e1, c, v, xl, p.K, vm, lane);
             rem_store_row<S, VEC, VPT>(yb + row * p.K, acc, vm);
             row = nrow;
             e0 = n0;
@@ -578,7 +586,7 @@ int launch_row_warp(const BooParams<S> &p, int64_t rg0, int64_t rg1, int64_t max
     SPMM_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const int64_t bound = (rg1 - rg0) * max_nr < p.rows ? (rg1 - rg0) * max_nr : p.rows;   // rows of the range
     const int64_t want = ceil_div(bound > 0 ? bound : 1, (int64_t)kShortWarps);
-    const int64_t cap = (int64_t)sms * 2;   // resident CTAs: every warp walks its rows pipelined
+    const int64_t cap = (int64_t)sms * row_warp_ctas<S, VPT>();   // resident CTAs: warps walk their rows pipelined
     const unsigned bz = (unsigned)(p.batch < 65535 ? p.batch : 65535);
     dim3 grid((unsigned)(want < cap ? want : cap), (unsigned)slabs, bz);
     row_warp_kernel<S, VEC, VPT><<<grid, 32 * kShortWarps, 0, s>>>(p, rg0, rg1, ident);
