@@ -46,7 +46,7 @@ SLABS = {np.float32: (0, -1, 16), np.float64: (0, -1, 8)}
 
 
 @pytest.mark.parametrize('dtype', [np.float32, np.float64])
-@pytest.mark.parametrize('k', [1, 7, 64, 128, 256, 300])
+@pytest.mark.parametrize('k', [1, 7, 32, 64, 128, 256, 300])
 def test_remainder_major_skewed_rows(cuda, dtype, k):
     mat = _skewed(1200, 5000, 11 + k, dtype)
     boo = S.csr_to_boo(mat, cluster="identity", target_nr=32, target_nc=32, small_block_threshold=64)
